@@ -1,0 +1,541 @@
+"""Benchmark of the paged decode-attention path on B200 (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c1|c3|c5]
+
+Default workload: BASELINE config 2 (Qwen2.5-0.5B shape batched ragged decode:
+64 sequences per GPU, 14 q heads / 2 KV heads, head_dim 64, context lengths
+U[256, 4096], 16-token pages from a shuffled shared pool, 512-token split-K
+partitions, 24 layers). One step = one decode step of all 24 layers: per layer
+the fused bias+RoPE+KV append of the new token (lc_rope_append) and paged
+attention over the cache (lc_paged_decode). Multi-GPU: weak scaling, the
+global batch of 64*N sequences is sharded by sequence (longest-first bin
+packing, lc_shard_sequences); no collective on the data path.
+
+`value` is decode-attention KV GB/s summed over ranks (each unique KV byte
+counted once per layer), inputs resident in HBM, timed with CUDA events over K
+replays of a CUDA graph of the step, max over ranks. `e2e` is the same metric
+through the C ABI with the step's inputs copied from pinned host memory and its
+outputs copied back inside the timed region. The 24 per-layer caches total
+~1.7 GB per GPU (> 126 MB L2), so no L2 flush is needed between steps.
+
+`--impl reference` runs the reference's own kernels (compiled unchanged from
+its sources into oracle/_ref) the way the reference launches them: per
+sequence, rope -> update_kv_cache -> flash_decoding, one launch each.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "lucciola-rs_b200"), str(ROOT / "tests")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "decode-attn KV GB/s & % HBM peak; tokens/s at batch 64, 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+CONFIGS = {
+    # name: (workload label, batch per rank, Hq, Hkv, hd, layers, ctx spec, partition tokens)
+    "c2": ("qwen2.5-0.5b batched ragged decode (BASELINE config 2)", 64, 14, 2, 64, 24,
+           ("uniform", 256, 4096), 512),
+    "c1": ("qwen2.5-0.5b single-sequence decode (BASELINE config 1)", 1, 14, 2, 64, 24,
+           ("fixed", 1024), 0),
+    "c3": ("qwen2.5-7b batched decode (BASELINE config 3)", 32, 28, 4, 128, 28,
+           ("fixed", 8192), 512),
+}
+
+
+# ------------------------------------------------------------------ helpers --
+
+def env_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the GPU is loaded."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(device_index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for line in out.splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), max=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = set()
+        for r in rows:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[key].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
+                "sm_max_mhz": max(r["max"] for r in rows), "reasons": sorted(reasons),
+                "samples": len(rows), "power_w_max": max(r["power"] for r in rows)}
+
+
+# ----------------------------------------------------------------- workload --
+
+class Workload:
+    """Synthetic paged decode batch for one rank, resident on the GPU."""
+
+    def __init__(self, cfg_name: str, rank: int, world: int, device, seed: int = 1234):
+        (self.label, self.batch_per_rank, self.hq, self.hkv, self.hd, self.layers, ctx_spec,
+         self.ptok) = CONFIGS[cfg_name]
+        self.cfg_name = cfg_name
+        rng = np.random.default_rng(seed)
+        global_batch = self.batch_per_rank * world
+        if ctx_spec[0] == "fixed":
+            ctx_all = np.full(global_batch, ctx_spec[1], np.int32)
+        else:
+            ctx_all = rng.integers(ctx_spec[1], ctx_spec[2] + 1, global_batch).astype(np.int32)
+        if world > 1:
+            import lucciola as L
+            owner = np.array(L.shard_sequences(ctx_all.tolist(), world))
+        else:
+            owner = np.zeros(global_batch, np.int64)
+        self.global_batch = global_batch
+        self.global_kv_tokens = int(ctx_all.sum() + global_batch)
+        self.ctx = ctx_all[owner == rank].astype(np.int32)  # cached tokens before this step
+        self.batch = len(self.ctx)
+        self.device = device
+        hd, hq, hkv, L_ = self.hd, self.hq, self.hkv, self.layers
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed + 7919 * rank)
+        # Pages: room for the context plus the token appended this step.
+        pages = (self.ctx + 1 + 15) // 16
+        self.num_blocks = int(pages.sum()) + 1
+        perm = torch.randperm(self.num_blocks, generator=gen, device=device).to(torch.int32).cpu().numpy()
+        self.max_pages = int(pages.max())
+        tables = np.full((self.batch, self.max_pages), -1, np.int32)
+        off = 0
+        for b, n in enumerate(pages):
+            tables[b, :n] = perm[off:off + n]
+            off += n
+        self.tables_np = tables
+        self.tables = torch.from_numpy(tables).to(device)
+        self.positions_np = self.ctx.copy()  # the new token's position
+        self.positions = torch.from_numpy(self.positions_np).to(device)
+        self.max_ctx = int(self.ctx.max()) + 1
+        shape = (self.num_blocks, L_, hkv, 16, hd)
+        self.k_pool = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        self.v_pool = torch.empty(shape, dtype=torch.bfloat16, device=device)
+        for t in (self.k_pool, self.v_pool):
+            flat = t.view(-1)
+            step = 1 << 28
+            for i in range(0, flat.numel(), step):
+                chunk = flat[i:i + step]
+                chunk.copy_(torch.randn(chunk.numel(), generator=gen, device=device,
+                                        dtype=torch.float32).to(torch.bfloat16))
+        self.row = (hq + 2 * hkv) * hd
+        self.qkv = torch.randn((L_, self.batch, self.row), generator=gen, device=device).to(torch.bfloat16)
+        bias = torch.randn((L_, self.row), generator=gen, device=device) * 0.01
+        self.q_bias = bias[:, :hq * hd].to(torch.bfloat16).contiguous()
+        self.k_bias = bias[:, hq * hd:(hq + hkv) * hd].to(torch.bfloat16).contiguous()
+        self.v_bias = bias[:, (hq + hkv) * hd:].to(torch.bfloat16).contiguous()
+        self.out = torch.empty((L_, self.batch, hq * hd), dtype=torch.bfloat16, device=device)
+        import lucciola as L
+        cos, sin = L.rope_table_host(32768, hd, 1e6)
+        self.cos = torch.from_numpy(cos).to(device)
+        self.sin = torch.from_numpy(sin).to(device)
+        # bytes: each unique KV byte of the attended context, once per layer
+        self.kv_bytes_per_layer = int((self.ctx.astype(np.int64) + 1).sum()) * hkv * hd * 2 * 2
+        self.kv_bytes_per_step = self.kv_bytes_per_layer * L_
+        self.h2d_bytes = self.qkv.numel() * 2 + self.positions.numel() * 4
+        self.d2h_bytes = self.out.numel() * 2
+
+
+# ------------------------------------------------------------------ our arm --
+
+class OursStep:
+    def __init__(self, w: Workload):
+        import lucciola as L
+        self.L = L
+        self.w = w
+        self.ws = L.alloc_decode_workspace(w.batch, w.hq, w.hkv, w.hd, w.max_ctx, w.ptok,
+                                           device=w.device)
+
+    def layer(self, l, decode_events=None):
+        w, L = self.w, self.L
+        L.rope_append(w.qkv[l], w.positions, w.q_bias[l], w.k_bias[l], w.v_bias[l], w.cos, w.sin,
+                      w.k_pool, w.v_pool, w.num_blocks, w.layers, l, w.hq, w.hkv, w.hd, w.tables)
+        if decode_events is not None:
+            decode_events[0].record()
+        L.paged_decode(w.out[l], w.qkv[l], w.k_pool, w.v_pool, w.num_blocks, w.layers, l, w.hq,
+                       w.hkv, w.hd, w.tables, w.positions, w.max_ctx, len_offset=1,
+                       partition_tokens=w.ptok, workspace=self.ws)
+        if decode_events is not None:
+            decode_events[1].record()
+
+    def step(self):
+        for l in range(self.w.layers):
+            self.layer(l)
+
+    launches_per_step = property(lambda self: 2 * self.w.layers)
+
+
+def time_graph(graph, steps, warmup, stream):
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def decode_kernel_time(runner, reps):
+    """Average duration of one lc_paged_decode launch: CUDA events around each
+    launch, launches queued behind a sleep so host latency is not timed."""
+    w = runner.w
+    pairs = []
+    torch.cuda.synchronize()
+    torch.cuda._sleep(50_000_000)
+    for _ in range(reps):
+        for l in range(w.layers):
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            runner.layer(l, decode_events=ev)
+            pairs.append(ev)
+    torch.cuda.synchronize()
+    times = [a.elapsed_time(b) for a, b in pairs]
+    return sum(times) / len(times)
+
+
+def cpu_baseline(w: Workload, budget_s: float = 12.0):
+    """The CPU oracle (restatement of the reference algorithm) on a bounded
+    sample of the same workload: all sequences of this rank, one layer per
+    repetition, all host cores."""
+    import oracle.oracle as O
+    from workloads import randn_bf16
+    rng = np.random.default_rng(99)
+    hq, hkv, hd = w.hq, w.hkv, w.hd
+    pages = (w.ctx + 1 + 15) // 16
+    nb = int(pages.sum()) + 1
+    tables = np.full((w.batch, int(pages.max())), -1, np.int32)
+    perm = rng.permutation(nb).astype(np.int32)
+    off = 0
+    for b, n in enumerate(pages):
+        tables[b, :n] = perm[off:off + n]
+        off += n
+    k_pool = randn_bf16(rng, (nb, 1, hkv, 16, hd))
+    v_pool = randn_bf16(rng, (nb, 1, hkv, 16, hd))
+    qkv = randn_bf16(rng, (w.batch, w.row))
+    qb, kb, vb = (randn_bf16(rng, (n * hd,)) for n in (hq, hkv, hkv))
+    cos, sin = O.rope_table(int(w.ctx.max()) + 2, hd, 1e6)
+    threads = os.cpu_count() or 1
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        x = qkv.copy()
+        O.rope_append(x, w.positions_np, qb, kb, vb, cos, sin, k_pool, v_pool, 1, 0, hq, hkv, hd,
+                      tables)
+        O.paged_decode(x, k_pool, v_pool, 0, hq, hkv, hd, tables, w.positions_np, 1,
+                       len_offset=1, threads=threads)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s or reps >= 64:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(w.kv_bytes_per_layer * reps / dt / 1e9, 3), "unit": "GB/s",
+            "cores": threads, "kind": "port",
+            "sample": f"{reps} x one layer of the rank-0 batch ({w.batch} sequences, "
+                      f"{int(w.ctx.sum() + w.batch)} KV tokens) through the CPU oracle "
+                      f"(oracle/lc_oracle.c: rope+append, then decode attention), {dt:.1f} s"}
+
+
+def run_ours(args, rank, world, local):
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    w = Workload(args.config, rank, world, device)
+    runner = OursStep(w)
+    # eager warm-up: caches tensor maps and kernel attributes before capture
+    for _ in range(2):
+        runner.step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        runner.step()
+    torch.cuda.synchronize()
+
+    # settle clocks under this load and keep sampling through the timed region
+    sampler = ClockSampler(local) if rank == 0 else None
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            graph.replay()
+        torch.cuda.synchronize()
+
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms_total = time_graph(graph, args.steps, args.warmup, torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms_step = ms_total / args.steps
+
+    # e2e: host inputs in, host outputs out, through the same C-ABI calls
+    qkv_host = w.qkv.cpu().pin_memory()
+    pos_host = w.positions.cpu().pin_memory()
+    out_host = torch.empty(w.out.shape, dtype=w.out.dtype).pin_memory()
+
+    def e2e_step():
+        w.qkv.copy_(qkv_host, non_blocking=True)
+        w.positions.copy_(pos_host, non_blocking=True)
+        graph.replay()
+        out_host.copy_(w.out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms_step = e0.elapsed_time(e1) / args.steps
+
+    # per-launch duration of the dominant kernel (roofline)
+    dec_ms = decode_kernel_time(runner, max(2, min(args.steps, 8)))
+
+    vals = torch.tensor([ms_step, e2e_ms_step, dec_ms, float(w.kv_bytes_per_step)],
+                        dtype=torch.float64, device=device)
+    if dist:
+        mx = vals[:3].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = vals[3:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms_step, e2e_ms_step, dec_ms = mx.tolist()
+        kv_bytes_all = tot.item()
+    else:
+        kv_bytes_all = float(w.kv_bytes_per_step)
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        value = kv_bytes_all / (ms_step * 1e-3) / 1e9
+        e2e_value = kv_bytes_all / (e2e_ms_step * 1e-3) / 1e9
+        achieved = w.kv_bytes_per_layer / (dec_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded bf16 ~N(0,1) K/V/Q, uniform context lengths)",
+            "config": {"workload": w.label, "batch_per_gpu": w.batch_per_rank,
+                       "global_batch": w.global_batch, "q_heads": w.hq, "kv_heads": w.hkv,
+                       "head_dim": w.hd, "layers": w.layers, "page_tokens": 16,
+                       "partition_tokens": w.ptok or "auto",
+                       "kv_tokens_per_layer": w.global_kv_tokens,
+                       "parallelism": f"sequence-sharded x{world}",
+                       "l2": "no flush: 24 per-layer caches, ~%.1f GB per GPU > 126 MB L2" %
+                             (w.kv_bytes_per_step / 1e9),
+                       "step": "per layer: lc_rope_append + lc_paged_decode; CUDA graph"},
+            "tokens_per_s": round(w.global_batch / (ms_step * 1e-3), 1),
+            "pct_hbm": round(100 * value / world / peak, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": TRAFFIC.get(args.config),
+                         "kernel": "paged_decode_kernel", "peak_kind": f"{peak_kind} (burst copy)",
+                         "launch_ms": round(dec_ms, 5)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(w.h2d_bytes), "d2h_bytes_per_step": int(w.d2h_bytes),
+                    "ms_per_step": round(e2e_ms_step, 5)},
+            "gpu_launches": runner.launches_per_step * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w)
+        else:
+            line["cpu_baseline"] = None
+        print(json.dumps(line), flush=True)
+    del graph
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum per paged_decode launch from the
+# committed ncu capture (profiles/), scaled to the bench's launch; None until captured.
+TRAFFIC: dict = {}
+
+
+# ------------------------------------------------------------ reference arm --
+
+def run_reference(args, rank, world, local):
+    if rank != 0:
+        return  # rank 0 alone runs the reference arm
+    import ctypes as C
+    import oracle.oracle as O
+    try:
+        R = O.ref_lib()
+    except Exception as e:  # pragma: no cover - only when the build is missing
+        print(json.dumps({"impl": "reference", "unavailable": f"reference kernels not built: {e}"}))
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = Workload(args.config, 0, 1, device)
+    host_pos = (C.c_int * w.batch)(*w.positions_np.tolist())
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for l in range(w.layers):
+            rc = R.ref_rope_append(P(w.qkv[l]), w.row, w.batch, 1, P(w.positions), P(w.q_bias[l]),
+                                   P(w.k_bias[l]), P(w.v_bias[l]), P(w.cos), P(w.sin),
+                                   P(w.k_pool), P(w.v_pool), w.layers, l, w.hq, w.hkv, w.hd,
+                                   P(w.tables), w.max_pages, 32768, s)
+            rc |= R.ref_paged_decode(P(w.out[l]), w.hq * w.hd, P(w.qkv[l]), w.row, P(w.k_pool),
+                                     P(w.v_pool), w.layers, l, w.hq, w.hkv, w.hd, P(w.tables),
+                                     w.max_pages, P(w.positions), host_pos, w.batch, 32768, s)
+            if rc:
+                raise RuntimeError(f"reference launch failed ({rc})")
+
+    step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    clocks = sampler.stop()
+
+    qkv_host = w.qkv.cpu().pin_memory()
+    pos_host = w.positions.cpu().pin_memory()
+    out_host = torch.empty(w.out.shape, dtype=w.out.dtype).pin_memory()
+    e0.record()
+    for _ in range(args.steps):
+        w.qkv.copy_(qkv_host, non_blocking=True)
+        w.positions.copy_(pos_host, non_blocking=True)
+        step()
+        out_host.copy_(w.out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    value = w.kv_bytes_per_step / (ms_step * 1e-3) / 1e9
+    e2e_value = w.kv_bytes_per_step / (e2e_ms * 1e-3) / 1e9
+    peak, _ = measured_peak()
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded bf16 ~N(0,1) K/V/Q, uniform context lengths)",
+        "config": {"workload": w.label, "batch_per_gpu": w.batch_per_rank,
+                   "global_batch": w.batch, "q_heads": w.hq, "kv_heads": w.hkv,
+                   "head_dim": w.hd, "layers": w.layers,
+                   "path": "reference kernels rope.cu/kv_cache.cu/attention.cu compiled "
+                           "unchanged for sm_100a, launched per sequence as src/kernels.rs and "
+                           "src/layers/kv_cache.rs do"},
+        "tokens_per_s": round(w.batch / (ms_step * 1e-3), 1),
+        "pct_hbm": round(100 * value / peak, 3),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": 1,
+                         "kind": "reference",
+                         "sample": "the reference's implementation of this path is CUDA only; "
+                                   "this arm runs its kernels on the B200 from one host thread, "
+                                   "full workload"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "e2e_with_copies": {"value": round(e2e_value, 3), "unit": "GB/s",
+                            "h2d_bytes_per_step": int(w.h2d_bytes),
+                            "d2h_bytes_per_step": int(w.d2h_bytes), "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": w.layers * w.batch * 3 * args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = env_dist()
+    if args.impl == "reference":
+        run_reference(args, rank, world, local)
+    else:
+        run_ours(args, rank, world, local)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

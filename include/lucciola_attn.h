@@ -1,0 +1,257 @@
+/*
+ * lucciola_attn.h - C ABI of the B200 (sm_100a) attention hot path of lucciola-rs.
+ *
+ * The path: bias + rotate-half RoPE on the new token's Q/K, append of K and V+bias
+ * into the paged KV pool, paged flash-decoding attention (GQA), and the causal
+ * prefill that attends over the same paged pool.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensors are device pointers; bf16 tensors are passed as void*.
+ *   - Paged pool layout (unchanged from src/layers/kv_cache.rs:60-68 and
+ *     src/kernels/kv_cache.cu:31-48):
+ *         k_pool, v_pool : bf16 [num_blocks][num_layers][num_kv_heads][16][head_dim]
+ *     A page of one (block, layer, kv_head) is 16 * head_dim contiguous bf16 values.
+ *   - Block tables are int32 logical->physical page maps; the batched entry points
+ *     take one row per sequence, `table_stride` int32 apart.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream), allocates nothing, and performs no host synchronisation, so the calls
+ *     can be captured in a CUDA graph.
+ *   - Return value: LC_OK or an lc_status code. Argument errors are detected on the
+ *     host before anything is launched. Data errors that only the device can see
+ *     (a block-table entry outside the pool, a position outside the table) are
+ *     recorded as bits in the optional `dev_status` word (int32, device memory):
+ *     the offending page is skipped (writes) or read as zeros (attention), never
+ *     dereferenced out of bounds.
+ *   - head_dim is 64 or 128 and block_size is 16, as in src/kernels.rs:37-47 and
+ *     src/layers/kv_cache.rs:35.
+ */
+#ifndef LUCCIOLA_ATTN_H
+#define LUCCIOLA_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *lc_stream_t; /* cudaStream_t */
+
+enum lc_status {
+    LC_OK = 0,
+    LC_ERR_INVALID_ARGUMENT = 1,    /* null pointer, negative or inconsistent size          */
+    LC_ERR_UNSUPPORTED_HEAD_DIM = 2,/* head_dim not 64/128 (src/kernels.rs:40-45 bails too) */
+    LC_ERR_UNSUPPORTED_SHAPE = 3,   /* block_size != 16, num_q_heads % num_kv_heads != 0     */
+    LC_ERR_WORKSPACE_TOO_SMALL = 4, /* workspace smaller than lc_*_workspace_size()          */
+    LC_ERR_MISALIGNED = 5,          /* a pool/tensor pointer not 16-byte aligned             */
+    LC_ERR_CUDA = 6,                /* a CUDA runtime/driver call failed                     */
+    LC_ERR_DEVICE_BOUNDS = 7,       /* device saw an out-of-range page or position           */
+    LC_ERR_DEVICE_TIMEOUT = 8,      /* a bounded device-side wait gave up                    */
+    LC_ERR_OUT_OF_BLOCKS = 9,       /* KV cache free list exhausted (kv_cache.rs:110-113)    */
+    LC_ERR_OUT_OF_MEMORY = 10,      /* KV cache does not fit the memory budget (:40-48)      */
+    LC_ERR_NOT_SUPPORTED = 11       /* no sm_100 device / feature unavailable                */
+};
+
+/* Bits a kernel ORs into the optional device status word. */
+#define LC_DEV_BAD_BLOCK 0x1   /* block-table entry outside [0, num_blocks)            */
+#define LC_DEV_BAD_POS 0x2     /* position outside the block table or RoPE table       */
+#define LC_DEV_TIMEOUT 0x4     /* a pipeline wait exceeded its bound                    */
+
+const char *lc_status_string(int status);
+/* Maps a device status word (read back by the caller) to an lc_status code. */
+int lc_status_from_device_word(int word);
+/* Library version string, e.g. "lucciola-b200 0.1 sm_100a". */
+const char *lc_version(void);
+
+/* ------------------------------------------------------------------------- */
+/* Reference-shaped entry points (single sequence, drop-in for the kernels).  */
+/* ------------------------------------------------------------------------- */
+
+/* Replaces `rope` (src/kernels/rope.cu:3-13) as launched by
+ * CudaFunctions::apply_rope (src/kernels.rs:203-246). In place:
+ *   q[h] <- bf16(rot(q[h] + q_bias[h]))  for h < num_q_heads
+ *   k[h] <- bf16(rot(k[h] + k_bias[h]))  for h < num_k_heads
+ * with rot = rotate-half over pairs (d, d + head_dim/2) using
+ * cos_cache/sin_cache[*pos_ptr][d] (f32 [max_pos][head_dim/2]). Bit-exact. */
+int lc_rope(void *q, const void *q_bias, void *k, const void *k_bias,
+            const float *cos_cache, const float *sin_cache, const int *pos_ptr,
+            int head_dim, int num_q_heads, int num_k_heads, lc_stream_t stream);
+
+/* Replaces `update_kv_cache_kernel` (src/kernels/kv_cache.cu:3-17) as launched
+ * by KVCache::update (src/layers/kv_cache.rs:124-173). Writes the token at
+ * position *pos_ptr: k_pool <- new_k (bit copy), v_pool <- bf16(new_v + v_bias).
+ * `max_seq_len` is accepted and unused, as in the reference. */
+int lc_update_kv_cache(void *k_pool, void *v_pool, const void *new_k,
+                       const void *new_v, const void *v_bias,
+                       const int *block_table, int layer_id, const int *pos_ptr,
+                       int num_layers, int num_kv_heads, int max_seq_len,
+                       int head_dim, int block_size, lc_stream_t stream);
+
+/* Replaces flash_decoding_kernel_64/128 (src/kernels/attention.cu:178-240) as
+ * launched by CudaFunctions::apply_flash_decoding (src/kernels.rs:248-320).
+ * Attention of num_q_heads query heads over cache positions 0..=*current_pos.
+ * Extra arguments the reference's launch site has but its kernel does not:
+ *   host_pos           - the host copy of the position (kernels.rs:258), used
+ *                        only to size the grid; the device value decides.
+ *   num_physical_blocks- pool size in pages (KVCache::num_physical_blocks).
+ *   workspace          - split-K scratch of lc_flash_decoding_workspace_size()
+ *                        bytes, zeroed once by lc_paged_decode_workspace_init. */
+size_t lc_flash_decoding_workspace_size(int num_q_heads, int head_dim,
+                                        int max_seq_len);
+int lc_flash_decoding(void *output, const void *q, const void *k_pool,
+                      const void *v_pool, const int *block_table, int layer_idx,
+                      int num_q_heads, int num_kv_heads, int head_dim,
+                      int max_seq_len, const int *current_pos, float sm_scale,
+                      int block_size, int num_layers, int host_pos,
+                      int64_t num_physical_blocks, void *workspace,
+                      size_t workspace_bytes, lc_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Batched entry points (the B200 path).                                     */
+/* ------------------------------------------------------------------------- */
+
+/* Fused bias + RoPE + KV append for `num_seqs * tokens_per_seq` token rows
+ * (decode: tokens_per_seq = 1; prefill: the prompt). Row r belongs to sequence
+ * r / tokens_per_seq and sits at position positions[r]. Each row of `qkv`
+ * (`row_stride` bf16 apart) holds [q (Hq*hd) | k (Hkv*hd) | v (Hkv*hd)], the
+ * layout of InferenceBuffers::qkv_states (src/layers/buffers.rs:28-31,
+ * src/models.rs:495-498). Effects, bit-identical to rope -> update_kv_cache:
+ *   q, k rotated in place (bf16), v untouched;
+ *   k_pool[page(pos)] <- rotated k,  v_pool[page(pos)] <- bf16(v + v_bias).
+ * Biases are bf16 [Hq*hd], [Hkv*hd], [Hkv*hd] (src/models.rs:500-502).
+ * rope_rows = rows of the cos/sin tables (positions must be < rope_rows). */
+int lc_rope_append(void *qkv, int64_t row_stride, int num_seqs,
+                   int tokens_per_seq, const int *positions,
+                   const void *q_bias, const void *k_bias, const void *v_bias,
+                   const float *cos_cache, const float *sin_cache, int rope_rows,
+                   void *k_pool, void *v_pool, int64_t num_blocks,
+                   int num_layers, int layer, int num_q_heads, int num_kv_heads,
+                   int head_dim, const int *block_tables, int table_stride,
+                   int *dev_status, lc_stream_t stream);
+
+/* Split-K workspace for lc_paged_decode. max_partitions bounds the number of
+ * partitions one sequence is split into (the grid's x extent). */
+size_t lc_paged_decode_workspace_size(int batch, int num_q_heads,
+                                      int num_kv_heads, int head_dim,
+                                      int max_partitions);
+/* Zeroes the workspace's arrival counters (once, after allocation). Every
+ * lc_paged_decode call leaves them at zero again. */
+int lc_paged_decode_workspace_init(void *workspace, size_t workspace_bytes,
+                                   lc_stream_t stream);
+/* Number of split-K partitions lc_paged_decode uses for this shape
+ * (partition_tokens = 0 picks a size that fills the GPU). */
+int lc_paged_decode_partitions(int batch, int num_q_heads, int num_kv_heads,
+                               int max_context_len, int partition_tokens);
+
+/* Batched paged decode attention. For sequence b with n_b = context_lens[b] +
+ * len_offset cached tokens (len_offset = 1 when context_lens holds positions,
+ * as the reference's pos_ptr does), every query head h of q (row b, `q_stride`
+ * bf16 between rows, heads contiguous) attends over cache tokens 0..n_b-1 of
+ * kv head h / (Hq/Hkv):
+ *   out[b][h] = softmax_t(q.k_t * sm_scale) . v_t     (fp32 accumulation)
+ * out is bf16 [batch][Hq][head_dim] with `out_stride` bf16 between rows.
+ * max_context_len is a host-side hint that sizes the grid; the device lengths
+ * decide (a longer sequence is split into longer partitions). */
+int lc_paged_decode(void *out, int64_t out_stride, const void *q,
+                    int64_t q_stride, const void *k_pool, const void *v_pool,
+                    int64_t num_blocks, int num_layers, int layer,
+                    int num_q_heads, int num_kv_heads, int head_dim,
+                    const int *block_tables, int table_stride,
+                    const int *context_lens, int len_offset, int batch,
+                    int max_context_len, int partition_tokens, float sm_scale,
+                    void *workspace, size_t workspace_bytes, int *dev_status,
+                    lc_stream_t stream);
+
+/* Causal prefill over the paged pool (tcgen05 tensor-core path). Query token i
+ * of sequence b sits at position start_pos[b] + i and attends to cache tokens
+ * 0..=start_pos[b]+i of its kv head; the K/V of the prompt must already be in
+ * the pool (lc_rope_append). q and out are [num_seqs*tokens_per_seq] rows of
+ * Hq*head_dim bf16, `q_stride` / `out_stride` apart. The reference runs this
+ * as tokens_per_seq sequential decode steps (src/models.rs:486-550). */
+int lc_paged_prefill(void *out, int64_t out_stride, const void *q,
+                     int64_t q_stride, const void *k_pool, const void *v_pool,
+                     int64_t num_blocks, int num_layers, int layer,
+                     int num_q_heads, int num_kv_heads, int head_dim,
+                     const int *block_tables, int table_stride,
+                     const int *start_pos, int num_seqs, int tokens_per_seq,
+                     int max_start_pos, float sm_scale, int *dev_status,
+                     lc_stream_t stream);
+
+/* Copies the cached K/V of every sequence into dense bf16
+ * [batch][max_context_len][Hkv][head_dim] tensors through the block tables
+ * (the same page addressing the attention kernels use; rows >= n_b untouched). */
+int lc_gather_kv(void *k_out, void *v_out, const void *k_pool,
+                 const void *v_pool, int64_t num_blocks, int num_layers,
+                 int layer, int num_kv_heads, int head_dim,
+                 const int *block_tables, int table_stride,
+                 const int *context_lens, int len_offset, int batch,
+                 int max_context_len, int *dev_status, lc_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
+/* Host-side mirror of the reference's Rust layer API (owning objects).       */
+/* ------------------------------------------------------------------------- */
+
+/* RopeCache::new (src/layers/rope.rs:10-40): f32 cos/sin [max_pos][hd/2],
+ * theta = (pos / scale) / base^(2i/hd); scale_factor <= 0 means none.
+ * lc_rope_table_host fills caller-provided host arrays (no GPU). */
+void lc_rope_table_host(int max_position_embeddings, int head_dim, float base,
+                        float scale_factor, float *cos_out, float *sin_out);
+typedef struct lc_rope_cache lc_rope_cache;
+int lc_rope_cache_new(int max_position_embeddings, int head_dim, float base,
+                      float scale_factor, lc_stream_t stream,
+                      lc_rope_cache **out);
+const float *lc_rope_cache_cos(const lc_rope_cache *rc);
+const float *lc_rope_cache_sin(const lc_rope_cache *rc);
+void lc_rope_cache_free(lc_rope_cache *rc);
+
+/* KVCache (src/layers/kv_cache.rs:12-174). Pool blocks =
+ * min(budget / bytes_per_block, ceil(max_position_embeddings / 16)) where
+ * budget = total * memory_fraction - used (kv_cache.rs:37-59). Free list is
+ * LIFO so blocks come out 0, 1, 2, ... (kv_cache.rs:73-76). */
+typedef struct lc_kv_cache lc_kv_cache;
+int lc_kv_cache_new(int num_hidden_layers, int num_attention_heads,
+                    int num_key_value_heads, int head_dim,
+                    int max_position_embeddings, float memory_fraction,
+                    lc_stream_t stream, lc_kv_cache **out);
+/* KVCache::prepare_for_step (kv_cache.rs:106-122). Unlike the reference, which
+ * pushes at most one block per call, this pushes blocks until the table covers
+ * `pos`; for consecutive positions the two are identical. */
+int lc_kv_cache_prepare_for_step(lc_kv_cache *c, lc_stream_t stream, int pos);
+/* KVCache::update (kv_cache.rs:124-173): prepare_for_step + append launch. */
+int lc_kv_cache_update(lc_kv_cache *c, lc_stream_t stream, int layer_idx,
+                       int pos, const int *pos_ptr, const void *k_input,
+                       const void *v_input, const void *v_bias);
+void *lc_kv_cache_k_pool(lc_kv_cache *c);
+void *lc_kv_cache_v_pool(lc_kv_cache *c);
+int *lc_kv_cache_block_table(lc_kv_cache *c);
+int64_t lc_kv_cache_num_physical_blocks(const lc_kv_cache *c);
+int lc_kv_cache_max_seq_len(const lc_kv_cache *c);
+int lc_kv_cache_num_allocated_blocks(const lc_kv_cache *c);
+void lc_kv_cache_free(lc_kv_cache *c);
+
+/* CudaFunctions::apply_flash_decoding (src/kernels.rs:248-320) over an
+ * lc_kv_cache: scale = 1/sqrt(head_dim) as in kernels.rs:264, workspace owned
+ * by the cache object. */
+int lc_apply_flash_decoding(lc_kv_cache *c, lc_stream_t stream, void *output,
+                            const void *q, int layer_idx, int pos,
+                            const int *pos_ptr, int num_q_heads);
+
+/* ------------------------------------------------------------------------- */
+/* Multi-GPU host logic.                                                      */
+/* ------------------------------------------------------------------------- */
+
+/* Sequence sharding: assigns each of `batch` sequences to one of `num_ranks`
+ * ranks by longest-processing-time-first bin packing on context length
+ * (ties by index). rank_of[b] receives the rank. Deterministic. */
+int lc_shard_sequences(const int *context_lens, int batch, int num_ranks,
+                       int *rank_of);
+/* KV-head sharding: rank r owns kv heads [r*Hkv/R, (r+1)*Hkv/R) and q heads
+ * [r*Hq/R, (r+1)*Hq/R). Writes first kv head and count; fails unless R | Hkv. */
+int lc_shard_kv_heads(int num_q_heads, int num_kv_heads, int num_ranks,
+                      int rank, int *first_kv_head, int *num_local_kv_heads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUCCIOLA_ATTN_H */

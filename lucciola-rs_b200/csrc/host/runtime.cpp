@@ -1,0 +1,139 @@
+// runtime.cpp - status strings, tensor-map cache, per-device launch attributes.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "../lc_host.h"
+
+extern "C" const char *lc_status_string(int status) {
+    switch (status) {
+        case LC_OK: return "ok";
+        case LC_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case LC_ERR_UNSUPPORTED_HEAD_DIM: return "unsupported head dimension (64 or 128)";
+        case LC_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+        case LC_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+        case LC_ERR_MISALIGNED: return "pointer or stride not 16-byte aligned";
+        case LC_ERR_CUDA: return "CUDA error";
+        case LC_ERR_DEVICE_BOUNDS: return "device saw an out-of-range block or position";
+        case LC_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+        case LC_ERR_OUT_OF_BLOCKS: return "KV cache out of memory blocks";
+        case LC_ERR_OUT_OF_MEMORY: return "not enough GPU memory for the KV cache";
+        case LC_ERR_NOT_SUPPORTED: return "not supported on this device";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int lc_status_from_device_word(int word) {
+    if (word & LC_DEV_TIMEOUT) return LC_ERR_DEVICE_TIMEOUT;
+    if (word & (LC_DEV_BAD_BLOCK | LC_DEV_BAD_POS)) return LC_ERR_DEVICE_BOUNDS;
+    return LC_OK;
+}
+
+extern "C" const char *lc_version(void) { return "lucciola-b200 0.1 sm_100a"; }
+
+namespace lc {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+struct MapKey {
+    const void *ptr;
+    int64_t rows;
+    int head_dim;
+    int device;
+    bool operator==(const MapKey &o) const {
+        return ptr == o.ptr && rows == o.rows && head_dim == o.head_dim && device == o.device;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        return std::hash<const void *>()(k.ptr) ^ (std::hash<int64_t>()(k.rows) * 31) ^
+               (size_t)k.head_dim * 131 ^ (size_t)k.device * 7919;
+    }
+};
+
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+}  // namespace
+
+int pool_tensor_map(const void *pool, int64_t rows, int head_dim, CUtensorMap *out) {
+    if (!aligned16(pool)) return LC_ERR_MISALIGNED;
+    if (rows <= 0 || rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return LC_ERR_CUDA;
+    MapKey key{pool, rows, head_dim, dev};
+    {
+        std::lock_guard<std::mutex> lk(g_map_mu);
+        auto it = g_maps.find(key);
+        if (it != g_maps.end()) {
+            *out = it->second;
+            return LC_OK;
+        }
+    }
+    auto fn = encode_fn();
+    if (!fn) return LC_ERR_NOT_SUPPORTED;
+    CUtensorMap map;
+    cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+    cuuint32_t box[2] = {64, 16};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(pool), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return LC_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    if (g_maps.size() > 256) g_maps.clear();
+    g_maps[key] = map;
+    *out = map;
+    return LC_OK;
+}
+
+int ensure_smem_attr(const void *func, int bytes) {
+    static std::mutex mu;
+    static std::unordered_map<const void *, std::vector<int>> done;  // per device: bytes set
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return LC_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(mu);
+    auto &v = done[func];
+    if ((int)v.size() <= dev) v.resize(dev + 1, 0);
+    if (v[dev] >= bytes) return LC_OK;
+    if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess)
+        return LC_ERR_CUDA;
+    v[dev] = bytes;
+    return LC_OK;
+}
+
+int sm_count() {
+    static std::mutex mu;
+    static std::vector<int> counts;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)counts.size() <= dev) counts.resize(dev + 1, 0);
+    if (!counts[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        counts[dev] = n > 0 ? n : 148;
+    }
+    return counts[dev];
+}
+
+}  // namespace lc

@@ -1,0 +1,34 @@
+// lc_host.h - host-side helpers shared by the C-ABI implementation files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/lucciola_attn.h"
+
+namespace lc {
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline cudaStream_t as_stream(lc_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Returns LC_OK or LC_ERR_CUDA for the last launch on this thread.
+inline int launch_status() {
+    return cudaGetLastError() == cudaSuccess ? LC_OK : LC_ERR_CUDA;
+}
+
+// Tiled 2-D tensor map over a paged pool viewed as [rows][head_dim] bf16 with
+// a {64, 16} box (one 128-byte-wide half page) and 128-byte swizzle. Maps are
+// cached by (pointer, rows, head_dim); the cache is thread-safe.
+// Returns LC_OK, LC_ERR_INVALID_ARGUMENT (rows beyond the int32 coordinate
+// range), LC_ERR_MISALIGNED or LC_ERR_CUDA.
+int pool_tensor_map(const void *pool, int64_t rows, int head_dim, CUtensorMap *out);
+
+// Applies cudaFuncAttributeMaxDynamicSharedMemorySize once per (function, device).
+int ensure_smem_attr(const void *func, int bytes);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+}  // namespace lc

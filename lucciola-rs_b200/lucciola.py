@@ -1,0 +1,301 @@
+"""Python binding of liblucciola_b200.so (the C ABI in include/lucciola_attn.h).
+
+A thin ctypes layer: every wrapper forwards device pointers of torch tensors and
+the current CUDA stream to the C entry point of the same name and raises
+LucciolaError on a non-zero status. There is no fallback: if the library is
+missing, importing this module fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from pathlib import Path
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "liblucciola_b200.so"
+
+if not LIB_PATH.exists():
+    raise ImportError(
+        f"{LIB_PATH} is missing; build it with `python lucciola-rs_b200/build.py`")
+
+lib = C.CDLL(str(LIB_PATH))
+
+_vp, _i32, _i64, _f32, _sz = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
+_pi32 = C.POINTER(C.c_int)
+
+# name -> (restype, argtypes), in the order of include/lucciola_attn.h
+SIGNATURES = {
+    "lc_status_string": (C.c_char_p, [_i32]),
+    "lc_status_from_device_word": (_i32, [_i32]),
+    "lc_version": (C.c_char_p, []),
+    "lc_rope": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
+    "lc_update_kv_cache": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32,
+                                  _i32, _i32, _vp]),
+    "lc_flash_decoding_workspace_size": (_sz, [_i32, _i32, _i32]),
+    "lc_flash_decoding": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp,
+                                 _f32, _i32, _i32, _i32, _i64, _vp, _sz, _vp]),
+    "lc_rope_append": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp,
+                              _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _vp]),
+    "lc_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "lc_paged_decode_workspace_init": (_i32, [_vp, _sz, _vp]),
+    "lc_paged_decode_partitions": (_i32, [_i32, _i32, _i32, _i32, _i32]),
+    "lc_paged_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
+                               _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _sz,
+                               _vp, _vp]),
+    "lc_paged_prefill": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
+                                _i32, _vp, _i32, _vp, _i32, _i32, _i32, _f32, _vp, _vp]),
+    "lc_gather_kv": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp,
+                            _i32, _i32, _i32, _vp, _vp]),
+    "lc_rope_table_host": (None, [_i32, _i32, _f32, _f32, _vp, _vp]),
+    "lc_rope_cache_new": (_i32, [_i32, _i32, _f32, _f32, _vp, C.POINTER(_vp)]),
+    "lc_rope_cache_cos": (_vp, [_vp]),
+    "lc_rope_cache_sin": (_vp, [_vp]),
+    "lc_rope_cache_free": (None, [_vp]),
+    "lc_kv_cache_new": (_i32, [_i32, _i32, _i32, _i32, _i32, _f32, _vp, C.POINTER(_vp)]),
+    "lc_kv_cache_prepare_for_step": (_i32, [_vp, _vp, _i32]),
+    "lc_kv_cache_update": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _vp]),
+    "lc_kv_cache_k_pool": (_vp, [_vp]),
+    "lc_kv_cache_v_pool": (_vp, [_vp]),
+    "lc_kv_cache_block_table": (_vp, [_vp]),
+    "lc_kv_cache_num_physical_blocks": (_i64, [_vp]),
+    "lc_kv_cache_max_seq_len": (_i32, [_vp]),
+    "lc_kv_cache_num_allocated_blocks": (_i32, [_vp]),
+    "lc_kv_cache_free": (None, [_vp]),
+    "lc_apply_flash_decoding": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _i32]),
+    "lc_shard_sequences": (_i32, [_pi32, _i32, _i32, _pi32]),
+    "lc_shard_kv_heads": (_i32, [_i32, _i32, _i32, _i32, _pi32, _pi32]),
+}
+
+for _name, (_res, _args) in SIGNATURES.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+LC_OK = 0
+LC_DEV_BAD_BLOCK, LC_DEV_BAD_POS, LC_DEV_TIMEOUT = 1, 2, 4
+
+
+class LucciolaError(RuntimeError):
+    def __init__(self, status: int, where: str):
+        self.status = status
+        super().__init__(f"{where}: {lib.lc_status_string(status).decode()} (status {status})")
+
+
+def check(status: int, where: str) -> None:
+    if status != LC_OK:
+        raise LucciolaError(status, where)
+
+
+def version() -> str:
+    return lib.lc_version().decode()
+
+
+def _p(t):
+    """Device pointer of a tensor (or None)."""
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+# ----------------------------------------------------------- reference shape --
+
+def rope(q, q_bias, k, k_bias, cos, sin, pos_ptr, head_dim, num_q_heads, num_k_heads,
+         stream=None):
+    check(lib.lc_rope(_p(q), _p(q_bias), _p(k), _p(k_bias), _p(cos), _p(sin), _p(pos_ptr),
+                      head_dim, num_q_heads, num_k_heads, _stream(stream)), "lc_rope")
+
+
+def update_kv_cache(k_pool, v_pool, new_k, new_v, v_bias, block_table, layer_id, pos_ptr,
+                    num_layers, num_kv_heads, max_seq_len, head_dim, block_size=16, stream=None):
+    check(lib.lc_update_kv_cache(_p(k_pool), _p(v_pool), _p(new_k), _p(new_v), _p(v_bias),
+                                 _p(block_table), layer_id, _p(pos_ptr), num_layers,
+                                 num_kv_heads, max_seq_len, head_dim, block_size,
+                                 _stream(stream)), "lc_update_kv_cache")
+
+
+def flash_decoding_workspace_size(num_q_heads, head_dim, max_seq_len) -> int:
+    return lib.lc_flash_decoding_workspace_size(num_q_heads, head_dim, max_seq_len)
+
+
+def flash_decoding(out, q, k_pool, v_pool, block_table, layer_idx, num_q_heads, num_kv_heads,
+                   head_dim, max_seq_len, pos_ptr, sm_scale, block_size, num_layers, host_pos,
+                   num_physical_blocks, workspace, stream=None):
+    check(lib.lc_flash_decoding(_p(out), _p(q), _p(k_pool), _p(v_pool), _p(block_table),
+                                layer_idx, num_q_heads, num_kv_heads, head_dim, max_seq_len,
+                                _p(pos_ptr), sm_scale, block_size, num_layers, host_pos,
+                                num_physical_blocks, _p(workspace),
+                                0 if workspace is None else workspace.numel() * workspace.element_size(),
+                                _stream(stream)), "lc_flash_decoding")
+
+
+# ------------------------------------------------------------------ batched --
+
+def rope_append(qkv, positions, q_bias, k_bias, v_bias, cos, sin, k_pool, v_pool, num_blocks,
+                num_layers, layer, num_q_heads, num_kv_heads, head_dim, block_tables,
+                tokens_per_seq=1, dev_status=None, stream=None):
+    rows = qkv.shape[0]
+    assert rows % tokens_per_seq == 0
+    check(lib.lc_rope_append(_p(qkv), qkv.stride(0), rows // tokens_per_seq, tokens_per_seq,
+                             _p(positions), _p(q_bias), _p(k_bias), _p(v_bias), _p(cos), _p(sin),
+                             cos.shape[0], _p(k_pool), _p(v_pool), num_blocks, num_layers, layer,
+                             num_q_heads, num_kv_heads, head_dim, _p(block_tables),
+                             block_tables.stride(0), _p(dev_status), _stream(stream)),
+          "lc_rope_append")
+
+
+def paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, max_partitions) -> int:
+    return lib.lc_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,
+                                              max_partitions)
+
+
+def paged_decode_partitions(batch, num_q_heads, num_kv_heads, max_context_len,
+                            partition_tokens=0) -> int:
+    return lib.lc_paged_decode_partitions(batch, num_q_heads, num_kv_heads, max_context_len,
+                                          partition_tokens)
+
+
+def alloc_decode_workspace(batch, num_q_heads, num_kv_heads, head_dim, max_context_len,
+                           partition_tokens=0, device="cuda", stream=None):
+    """Allocates (torch) and zero-initialises a workspace for lc_paged_decode."""
+    import torch
+    parts = paged_decode_partitions(batch, num_q_heads, num_kv_heads, max_context_len,
+                                    partition_tokens)
+    nbytes = paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, parts)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    check(lib.lc_paged_decode_workspace_init(_p(ws), nbytes, _stream(stream)),
+          "lc_paged_decode_workspace_init")
+    return ws
+
+
+def paged_decode(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_heads,
+                 num_kv_heads, head_dim, block_tables, context_lens, max_context_len,
+                 sm_scale=None, len_offset=0, partition_tokens=0, workspace=None,
+                 dev_status=None, stream=None):
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(head_dim)
+    batch = context_lens.shape[0]
+    check(lib.lc_paged_decode(_p(out), out.stride(0), _p(q), q.stride(0), _p(k_pool), _p(v_pool),
+                              num_blocks, num_layers, layer, num_q_heads, num_kv_heads, head_dim,
+                              _p(block_tables), block_tables.stride(0), _p(context_lens),
+                              len_offset, batch, max_context_len, partition_tokens, sm_scale,
+                              _p(workspace),
+                              0 if workspace is None else workspace.numel() * workspace.element_size(),
+                              _p(dev_status), _stream(stream)), "lc_paged_decode")
+
+
+def paged_prefill(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_heads,
+                  num_kv_heads, head_dim, block_tables, start_pos, tokens_per_seq, max_start_pos,
+                  sm_scale=None, dev_status=None, stream=None):
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(head_dim)
+    num_seqs = start_pos.shape[0]
+    check(lib.lc_paged_prefill(_p(out), out.stride(0), _p(q), q.stride(0), _p(k_pool),
+                               _p(v_pool), num_blocks, num_layers, layer, num_q_heads,
+                               num_kv_heads, head_dim, _p(block_tables), block_tables.stride(0),
+                               _p(start_pos), num_seqs, tokens_per_seq, max_start_pos, sm_scale,
+                               _p(dev_status), _stream(stream)), "lc_paged_prefill")
+
+
+def gather_kv(k_out, v_out, k_pool, v_pool, num_blocks, num_layers, layer, num_kv_heads,
+              head_dim, block_tables, context_lens, max_context_len, len_offset=0,
+              dev_status=None, stream=None):
+    check(lib.lc_gather_kv(_p(k_out), _p(v_out), _p(k_pool), _p(v_pool), num_blocks, num_layers,
+                           layer, num_kv_heads, head_dim, _p(block_tables),
+                           block_tables.stride(0), _p(context_lens), len_offset,
+                           context_lens.shape[0], max_context_len, _p(dev_status),
+                           _stream(stream)), "lc_gather_kv")
+
+
+# ------------------------------------------------------------ host mirrors --
+
+def rope_table_host(max_pos, head_dim, base, scale_factor=0.0):
+    """RopeCache's f32 cos/sin tables computed on the host (numpy arrays)."""
+    import numpy as np
+    half = head_dim // 2
+    cos = np.empty((max_pos, half), dtype=np.float32)
+    sin = np.empty((max_pos, half), dtype=np.float32)
+    lib.lc_rope_table_host(max_pos, head_dim, base, scale_factor,
+                           cos.ctypes.data_as(C.c_void_p), sin.ctypes.data_as(C.c_void_p))
+    return cos, sin
+
+
+def shard_sequences(context_lens, num_ranks):
+    """Rank of each sequence under longest-first bin packing (list of ints)."""
+    n = len(context_lens)
+    lens = (C.c_int * n)(*[int(x) for x in context_lens])
+    out = (C.c_int * n)()
+    check(lib.lc_shard_sequences(lens, n, num_ranks, out), "lc_shard_sequences")
+    return list(out)
+
+
+def shard_kv_heads(num_q_heads, num_kv_heads, num_ranks, rank):
+    first, count = C.c_int(), C.c_int()
+    check(lib.lc_shard_kv_heads(num_q_heads, num_kv_heads, num_ranks, rank, C.byref(first),
+                                C.byref(count)), "lc_shard_kv_heads")
+    return first.value, count.value
+
+
+class KVCache:
+    """Owning mirror of the reference's KVCache (src/layers/kv_cache.rs)."""
+
+    def __init__(self, num_hidden_layers, num_attention_heads, num_key_value_heads, head_dim,
+                 max_position_embeddings, memory_fraction, stream=None):
+        h = C.c_void_p()
+        check(lib.lc_kv_cache_new(num_hidden_layers, num_attention_heads, num_key_value_heads,
+                                  head_dim, max_position_embeddings, memory_fraction,
+                                  _stream(stream), C.byref(h)), "lc_kv_cache_new")
+        self._h = h
+        self.num_layers, self.num_q_heads = num_hidden_layers, num_attention_heads
+        self.num_kv_heads, self.head_dim = num_key_value_heads, head_dim
+
+    def prepare_for_step(self, pos, stream=None):
+        check(lib.lc_kv_cache_prepare_for_step(self._h, _stream(stream), pos),
+              "lc_kv_cache_prepare_for_step")
+
+    def update(self, layer_idx, pos, pos_ptr, k, v, v_bias, stream=None):
+        check(lib.lc_kv_cache_update(self._h, _stream(stream), layer_idx, pos, _p(pos_ptr),
+                                     _p(k), _p(v), _p(v_bias)), "lc_kv_cache_update")
+
+    def apply_flash_decoding(self, out, q, layer_idx, pos, pos_ptr, stream=None):
+        check(lib.lc_apply_flash_decoding(self._h, _stream(stream), _p(out), _p(q), layer_idx,
+                                          pos, _p(pos_ptr), self.num_q_heads),
+              "lc_apply_flash_decoding")
+
+    @property
+    def k_pool(self):
+        return lib.lc_kv_cache_k_pool(self._h)
+
+    @property
+    def v_pool(self):
+        return lib.lc_kv_cache_v_pool(self._h)
+
+    @property
+    def block_table(self):
+        return lib.lc_kv_cache_block_table(self._h)
+
+    @property
+    def num_physical_blocks(self):
+        return lib.lc_kv_cache_num_physical_blocks(self._h)
+
+    @property
+    def max_seq_len(self):
+        return lib.lc_kv_cache_max_seq_len(self._h)
+
+    @property
+    def num_allocated_blocks(self):
+        return lib.lc_kv_cache_num_allocated_blocks(self._h)
+
+    def close(self):
+        if self._h:
+            lib.lc_kv_cache_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

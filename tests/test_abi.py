@@ -1,0 +1,155 @@
+"""C-ABI library: loads, exports every declared symbol, validates arguments on
+the host, and its host-side logic (RoPE table, sharding, workspace sizing)
+behaves as specified. No GPU needed."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import lucciola as L
+import oracle.oracle as O
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_functions():
+    names = []
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"^[A-Za-z_][\w \*]*?\b(lc_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_headers_declare_the_path():
+    names = declared_functions()
+    for must in ("lc_rope", "lc_update_kv_cache", "lc_flash_decoding", "lc_rope_append",
+                 "lc_paged_decode", "lc_paged_prefill", "lc_gather_kv", "lc_kv_cache_new"):
+        assert must in names
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_library_exports_declared_symbol(name):
+    assert hasattr(L.lib, name), f"{name} declared in include/ but not exported"
+    assert name in L.SIGNATURES, f"{name} has no ctypes signature in lucciola.py"
+
+
+def test_status_strings():
+    for code in range(0, 12):
+        assert L.lib.lc_status_string(code)
+    assert L.lib.lc_status_from_device_word(0) == 0
+    assert L.lib.lc_status_from_device_word(L.LC_DEV_BAD_BLOCK) == 7
+    assert L.lib.lc_status_from_device_word(L.LC_DEV_BAD_POS) == 7
+    assert L.lib.lc_status_from_device_word(L.LC_DEV_TIMEOUT | 1) == 8
+    assert "sm_100a" in L.version()
+
+
+FAKE = 0x10000  # aligned non-null pointer value; never dereferenced by host validation
+
+
+def decode_call(**kw):
+    a = dict(out=FAKE, out_stride=14 * 64, q=FAKE, q_stride=14 * 64, k_pool=FAKE, v_pool=FAKE,
+             num_blocks=64, num_layers=2, layer=1, hq=14, hkv=2, hd=64, tables=FAKE,
+             table_stride=64, lens=FAKE, len_offset=0, batch=1, max_ctx=1024, ptok=0,
+             scale=0.125, ws=None, ws_bytes=0, status=None, stream=None)
+    a.update(kw)
+    return L.lib.lc_paged_decode(a["out"], a["out_stride"], a["q"], a["q_stride"], a["k_pool"],
+                                 a["v_pool"], a["num_blocks"], a["num_layers"], a["layer"],
+                                 a["hq"], a["hkv"], a["hd"], a["tables"], a["table_stride"],
+                                 a["lens"], a["len_offset"], a["batch"], a["max_ctx"], a["ptok"],
+                                 a["scale"], a["ws"], a["ws_bytes"], a["status"], a["stream"])
+
+
+def test_decode_rejects_bad_arguments_before_launch():
+    assert decode_call(hd=96) == 2            # kernels.rs:40-45 supports 64/128 only
+    assert decode_call(hd=80) == 2
+    assert decode_call(hq=14, hkv=3) == 3     # GQA needs Hq % Hkv == 0
+    assert decode_call(out=None) == 1
+    assert decode_call(layer=2) == 1
+    assert decode_call(num_blocks=0) == 1
+    assert decode_call(k_pool=FAKE + 8) == 5  # TMA needs 16-byte aligned pools
+    assert decode_call(q_stride=14 * 64 + 3) == 5
+    assert decode_call(len_offset=2) == 1
+    assert decode_call(batch=0) == 0          # nothing to do
+
+
+def test_update_kv_cache_rejects_block_size():
+    rc = L.lib.lc_update_kv_cache(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 0, FAKE, 2, 2, 1024, 64, 32,
+                                  None)
+    assert rc == 3
+
+
+def test_rope_append_rejects_bad_arguments():
+    def call(**kw):
+        a = dict(hd=64, hq=14, hkv=2, row_stride=18 * 64, rope_rows=32768)
+        a.update(kw)
+        return L.lib.lc_rope_append(FAKE, a["row_stride"], 1, 1, FAKE, FAKE, FAKE, FAKE, FAKE,
+                                    FAKE, a["rope_rows"], FAKE, FAKE, 64, 2, 0, a["hq"], a["hkv"],
+                                    a["hd"], FAKE, 64, None, None)
+    assert call(hd=72) == 2
+    assert call(hkv=4) == 3
+    assert call(row_stride=17 * 64) == 1
+    assert call(rope_rows=0) == 1
+
+
+def test_prefill_rejects_bad_arguments():
+    rc = L.lib.lc_paged_prefill(FAKE, 12 * 128, FAKE, 12 * 128, FAKE, FAKE, 64, 2, 0, 12, 2, 96,
+                                FAKE, 64, FAKE, 1, 128, 0, 0.1, None, None)
+    assert rc in (2, 11)
+
+
+def test_workspace_and_partitions():
+    # explicit partition size: ceil(ctx / P)
+    assert L.paged_decode_partitions(64, 14, 2, 4096, 512) == 8
+    assert L.paged_decode_partitions(64, 14, 2, 4000, 512) == 8
+    assert L.paged_decode_partitions(1, 14, 2, 1024, 64) == 16
+    # capped at 256 partitions
+    assert L.paged_decode_partitions(1, 14, 2, 10**6, 16) == 256
+    # auto: large batches keep 512-token partitions, a single sequence goes finer
+    assert L.paged_decode_partitions(64, 14, 2, 4096, 0) == 8
+    assert L.paged_decode_partitions(1, 14, 2, 1024, 0) == 16
+    ws1 = L.paged_decode_workspace_size(4, 28, 4, 128, 16)
+    assert ws1 >= 4 * 28 * 16 * 128 * 4 + 4 * 28 * 16 * 4 + 4 * 28 * 4
+    assert ws1 % 256 == 0 or ws1 == 4 * 28 * 4  # layout is 256-byte aligned between arrays
+    assert L.flash_decoding_workspace_size(14, 64, 32768) >= \
+        L.paged_decode_workspace_size(1, 14, 2, 64, 512)
+
+
+@pytest.mark.parametrize("hd,base,scale", [(64, 1e6, 0.0), (128, 1e6, 0.0), (128, 1e4, 4.0),
+                                            (64, 10000.0, 0.0)])
+def test_rope_table_host_matches_oracle_bit_exact(hd, base, scale):
+    c, s = L.rope_table_host(2048, hd, base, scale)
+    oc, os_ = O.rope_table(2048, hd, base, scale)
+    assert np.array_equal(c.view(np.uint32), oc.view(np.uint32))
+    assert np.array_equal(s.view(np.uint32), os_.view(np.uint32))
+
+
+def py_lpt(lens, ranks):
+    order = sorted(range(len(lens)), key=lambda b: (-lens[b], b))
+    load = [0] * ranks
+    out = [0] * len(lens)
+    for b in order:
+        r = min(range(ranks), key=lambda i: (load[i], i))
+        out[b] = r
+        load[r] += max(lens[b], 0)
+    return out
+
+
+@pytest.mark.parametrize("ranks", [1, 2, 4, 8])
+def test_shard_sequences_lpt(ranks):
+    rng = np.random.default_rng(ranks)
+    lens = rng.integers(256, 4097, 64).tolist()
+    got = L.shard_sequences(lens, ranks)
+    assert got == py_lpt(lens, ranks)
+    loads = [sum(l for l, r in zip(lens, got) if r == k) for k in range(ranks)]
+    assert max(loads) - min(loads) <= max(lens)          # LPT bound
+    assert sorted(set(got)) == list(range(ranks))
+
+
+def test_shard_kv_heads():
+    assert [L.shard_kv_heads(64, 8, 8, r) for r in range(8)] == [(r, 1) for r in range(8)]
+    assert [L.shard_kv_heads(64, 8, 4, r) for r in range(4)] == [(2 * r, 2) for r in range(4)]
+    with pytest.raises(L.LucciolaError):
+        L.shard_kv_heads(64, 8, 3, 0)
