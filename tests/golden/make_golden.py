@@ -5,7 +5,7 @@ compiled unchanged into oracle/_ref/libref_kernels.so) on seeded inputs on a
 GPU and stores inputs and outputs as small .npz files next to this script.
 tests/test_golden.py then checks the CPU oracle against them on any machine.
 
-    python tests/golden/make_golden.py        # needs a GPU and oracle/_ref
+    python tests/golden/make_golden.py [--out DIR]   # needs a GPU and oracle/_ref
 """
 from __future__ import annotations
 
@@ -94,6 +94,11 @@ def attention_fixture(R, hq, hkv, hd, pos, seed):
 
 
 def main() -> int:
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", default=str(HERE), help="directory for the .npz files")
+    out_dir = Path(ap.parse_args().out)
+    out_dir.mkdir(parents=True, exist_ok=True)
     R = O.ref_lib()
     fx = {
         "rope_hd64": rope_fixture(R, 64, 14, 2, 1),
@@ -104,7 +109,7 @@ def main() -> int:
         "attention_hd128_gqa8": attention_fixture(R, 16, 2, 128, 40, 6),
     }
     for name, d in fx.items():
-        path = HERE / f"{name}.npz"
+        path = out_dir / f"{name}.npz"
         np.savez_compressed(path, **{k: np.asarray(v) for k, v in d.items()})
         print(f"wrote {path} ({path.stat().st_size} bytes)")
     return 0
