@@ -303,7 +303,20 @@ def run_ours(args, rank, world, local):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
     w = Workload(args.config, rank, world, device)
+    if args.partition is not None:
+        w.ptok = args.partition
     runner = OursStep(w)
+    if args.mode == "kernel":
+        # Plain eager launches, nothing else: the command profiled by ncu.
+        for _ in range(args.warmup + args.steps):
+            runner.step()
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps({"mode": "kernel", "config": args.config, "steps": args.steps,
+                              "warmup": args.warmup, "launches_per_step": runner.launches_per_step}))
+        if dist:
+            dist.destroy_process_group()
+        return
     # eager warm-up: caches tensor maps and kernel attributes before capture
     for _ in range(2):
         runner.step()
@@ -526,6 +539,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
+                    help="kernel: eager launches only (for profilers), no JSON metrics")
+    ap.add_argument("--partition", type=int, default=None,
+                    help="override the split-K partition size in tokens (0 = auto)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

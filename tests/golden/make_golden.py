@@ -70,8 +70,9 @@ def update_fixture(R, seed):
     vs = randn_bf16(rng, (len(positions), hkv * hd))
     for i, pos in enumerate(positions):
         dpos = to_device(np.array([pos], np.int32))
-        assert R.ref_update_kv_cache(p(dk), p(dv), p(to_device(ks[i])), p(to_device(vs[i])),
-                                     p(to_device(vb)), p(dt), case.layer, p(dpos),
+        dki, dvi, dvb = to_device(ks[i]), to_device(vs[i]), to_device(vb)  # alive at launch
+        assert R.ref_update_kv_cache(p(dk), p(dv), p(dki), p(dvi),
+                                     p(dvb), p(dt), case.layer, p(dpos),
                                      case.num_layers, hkv, 32768, hd, 16, s()) == 0
     torch.cuda.synchronize()
     return dict(hkv=hkv, hd=hd, num_layers=case.num_layers, layer=case.layer, table=case.tables[0],

@@ -63,7 +63,8 @@ def test_reference_update_kv_cache_matches_oracle():
     for pos in (0, 15, 16, 17, 299):
         k, v = randn_bf16(rng, (hkv * hd,)), randn_bf16(rng, (hkv * hd,))
         dpos = to_device(np.array([pos], np.int32))
-        assert R.ref_update_kv_cache(p(dk), p(dv), p(to_device(k)), p(to_device(v)), p(dvb),
+        dkk, dvv = to_device(k), to_device(v)  # keep alive until the launch is queued
+        assert R.ref_update_kv_cache(p(dk), p(dv), p(dkk), p(dvv), p(dvb),
                                      p(dt), case.layer, p(dpos), case.num_layers, hkv, 32768, hd,
                                      16, stream()) == 0
         torch.cuda.synchronize()
