@@ -201,8 +201,7 @@ class OursStep:
         import lucciola as L
         self.L = L
         self.w = w
-        self.ws = L.alloc_decode_workspace(w.batch, w.hq, w.hkv, w.hd, w.max_ctx, w.ptok,
-                                           device=w.device)
+        self.ws = L.alloc_decode_workspace(w.batch, w.hq, w.hkv, w.hd, device=w.device)
 
     def layer(self, l, decode_events=None):
         w, L = self.w, self.L

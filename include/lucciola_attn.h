@@ -129,19 +129,16 @@ int lc_rope_append(void *qkv, int64_t row_stride, int num_seqs,
                    int head_dim, const int *block_tables, int table_stride,
                    int *dev_status, lc_stream_t stream);
 
-/* Split-K workspace for lc_paged_decode. max_partitions bounds the number of
- * partitions one sequence is split into (the grid's x extent). */
+/* Split-K workspace for lc_paged_decode on the current device (bytes). It holds
+ * one arrival counter per (sequence, kv-head slice) and the fp32 partials of
+ * segments split across CTAs; its size depends on the device's SM count (a
+ * host-only caller gets the size for a 148-SM B200). */
 size_t lc_paged_decode_workspace_size(int batch, int num_q_heads,
-                                      int num_kv_heads, int head_dim,
-                                      int max_partitions);
-/* Zeroes the workspace's arrival counters (once, after allocation). Every
- * lc_paged_decode call leaves them at zero again. */
+                                      int num_kv_heads, int head_dim);
+/* Zeroes the workspace (once, after allocation). Every lc_paged_decode call
+ * leaves its arrival counters at zero again. */
 int lc_paged_decode_workspace_init(void *workspace, size_t workspace_bytes,
                                    lc_stream_t stream);
-/* Number of split-K partitions lc_paged_decode uses for this shape
- * (partition_tokens = 0 picks a size that fills the GPU). */
-int lc_paged_decode_partitions(int batch, int num_q_heads, int num_kv_heads,
-                               int max_context_len, int partition_tokens);
 
 /* Batched paged decode attention. For sequence b with n_b = context_lens[b] +
  * len_offset cached tokens (len_offset = 1 when context_lens holds positions,
@@ -150,8 +147,12 @@ int lc_paged_decode_partitions(int batch, int num_q_heads, int num_kv_heads,
  * kv head h / (Hq/Hkv):
  *   out[b][h] = softmax_t(q.k_t * sm_scale) . v_t     (fp32 accumulation)
  * out is bf16 [batch][Hq][head_dim] with `out_stride` bf16 between rows.
- * max_context_len is a host-side hint that sizes the grid; the device lengths
- * decide (a longer sequence is split into longer partitions). */
+ * The kernel is persistent: the 16-token pages of all (sequence, kv head)
+ * segments are split evenly over the CTAs; split segments are merged with a
+ * log-sum-exp reduction. partition_tokens > 0 caps the split at about that
+ * many tokens per CTA (0 = fill the GPU). max_context_len is an optional host
+ * hint (0 = none) that trims the grid for small batches; lengths are read on
+ * the device. */
 int lc_paged_decode(void *out, int64_t out_stride, const void *q,
                     int64_t q_stride, const void *k_pool, const void *v_pool,
                     int64_t num_blocks, int num_layers, int layer,

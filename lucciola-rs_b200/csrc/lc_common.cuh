@@ -92,6 +92,14 @@ __device__ inline bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
     }
 }
 
+// After a wait gave up: waits (bounded again) for a phase whose copies may
+// still be in flight, so that the CTA does not exit under them.
+__device__ inline void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_timer_ns() - t0 > kWaitLimitNs) return;
+}
+
 // ------------------------------------------------------------------- TMA ----
 // 2-D tiled bulk tensor load into this CTA's shared memory, completion counted
 // on `bar` in bytes. x (innermost) must keep x*2 bytes 16-byte aligned: every

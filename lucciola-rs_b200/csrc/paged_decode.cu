@@ -4,22 +4,29 @@
 // runs one 1024-thread CTA per query head over one sequence and so reads every
 // KV byte Hq/Hkv times with scalar 2-byte loads. Here:
 //
-//  * One CTA per (partition of <= P tokens, kv head [x8-head slice], sequence).
-//    The CTA serves all query heads of the kv head's group (up to 8), so each KV
-//    byte leaves HBM once.
-//  * A producer warp streams the partition's pages into a ring of shared-memory
-//    stages with TMA tile loads (one {64 x 16} box per half page, 128-byte
-//    swizzle), completion tracked by mbarriers with a transaction count.
-//  * Four consumer warps each take one 16-token page per stage and run both
-//    products on the tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate)
-//    with tokens on M and the <= 8 query heads on N:
+//  * Work unit = one 16-token page of one (sequence, kv head [8-head slice])
+//    "segment"; a CTA serves all query heads of the kv head's group (up to 8),
+//    so each KV byte leaves HBM once.
+//  * Persistent, balanced grid: the pages of all segments form one global
+//    stream (segment order b-major, then kv head); CTA c of C takes the
+//    contiguous range [c*T/C, (c+1)*T/C) of the T pages, crossing segment
+//    boundaries. Every CTA moves the same number of bytes whatever the context
+//    lengths are, and its pipeline never drains between segments.
+//  * A producer warp streams the range into a ring of shared-memory stages
+//    with TMA tile loads (one {64 x 16} box per half page, 128-byte swizzle);
+//    the first stage of every chunk also carries the chunk's query rows (bulk
+//    copy). mbarriers with transaction counts track completion.
+//  * Four consumer warps each take one page per stage and run both products on
+//    the tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate) with tokens
+//    on M and the <= 8 query heads on N:
 //        S^T[16 tok x 8 heads]  = K_page[16 x hd] . Q^T[hd x 8]
 //        O^T[hd x 8 heads]     += V_page^T[hd x 16] . P^T[16 x 8]
-//    P^T goes from the accumulator layout to the B-operand layout with
-//    movmatrix.trans, without touching shared memory. Online softmax in base 2.
-//  * Split-K: partitions write (O/l, log2-sum-exp) to the workspace; the last
-//    CTA of a (sequence, kv head) to finish (arrival counter) merges them with a
-//    warp-shuffle log-sum-exp reduction and writes the bf16 output.
+//    P^T moves from the accumulator layout to the B-operand layout with
+//    movmatrix.trans. Online softmax in base 2.
+//  * A chunk that covers a whole segment writes the bf16 output directly. A
+//    segment split across CTAs writes (O/l, log2-sum-exp) partials; the last
+//    CTA to finish it (arrival counter) merges them with a warp-shuffle
+//    log-sum-exp reduction.
 //
 // Semantics follow attention.cu: out = softmax(q.k * scale) . v over cache
 // tokens 0..n-1, fp32 accumulation, bf16 output. Block-table entries outside
@@ -35,18 +42,27 @@ namespace {
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
 constexpr int kHeadsPerCta = 8;
-constexpr int kMaxPartitions = 256;
-constexpr int kPagesPerStage = 4;  // one page per consumer warp per stage
+constexpr int kPagesPerStage = kConsumerWarps;  // one page per consumer warp per stage
+
+enum : int { kFirst = 1, kLast = 2, kDone = 4 };
+
+struct StageMeta {
+    int b, g, page0, np;    // sequence, segment-in-sequence, first page of the stage, pages
+    int n, pages_b, flags;  // tokens of the sequence, its pages, kFirst/kLast/kDone
+    int chunk_p0, take;     // chunk = pages [chunk_p0, chunk_p0 + take) of the segment
+    long long seg_start;    // global index of the segment's first page
+};
 
 template <int HD>
 struct DecodeCfg {
     static constexpr int kPageBytes = kBlockSize * HD * 2;  // 2 KiB / 4 KiB
     static constexpr int kStages = HD == 64 ? 4 : 3;
     static constexpr int kStageBytes = kPagesPerStage * 2 * kPageBytes;  // K pages, V pages
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024;    // + alignment slack
-    static_assert(kStages * kStageBytes >=
-                      kConsumerWarps * kHeadsPerCta * (HD + 2) * 4 + kHeadsPerCta * (kMaxPartitions + 1) * 4,
-                  "merge scratch must fit in the stage ring");
+    static constexpr int kQBytes = kHeadsPerCta * HD * 2;
+    static constexpr int kRedFloats = kHeadsPerCta * HD + 2 * kHeadsPerCta;  // o, m, l
+    static constexpr int kQOffset = kStages * kStageBytes;
+    static constexpr int kRedOffset = kQOffset + kStages * kQBytes;
+    static constexpr int kSmemBytes = kRedOffset + 2 * kRedFloats * 4 + 1024;  // + alignment
 };
 
 struct DecodeParams {
@@ -58,14 +74,16 @@ struct DecodeParams {
     int table_stride;
     const int *ctx_lens;
     int len_offset;
+    int batch;
     int64_t pool_rows;  // rows of the [rows][hd] pool view; used as an all-out-of-bounds row
     int64_t num_blocks;
     int num_layers, layer, num_q_heads, num_kv_heads, group, ctas_per_kv;
+    int seg_per_seq;  // num_kv_heads * ctas_per_kv
     int partition_tokens;
     float scale_log2;  // sm_scale * log2(e)
-    float *ws_o;
-    float *ws_lse;
-    int *ws_cnt;
+    float *ws_o;       // [slots][8][HD]
+    float *ws_lse;     // [slots][8]
+    int *ws_cnt;       // [batch * seg_per_seq]
     int *status;
 };
 
@@ -75,21 +93,97 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
 // Shared-memory byte address of 16-byte chunk `kc` (of hd/8) of token row `r` in a
 // page tile stored as hd/64 boxes of [16 rows][128 B] with 128-byte swizzle.
 __device__ __forceinline__ uint32_t tile_addr(uint32_t page, int r, int kc) {
     return page + ((kc >> 3) << 11) + (r << 7) + ((((kc & 7) ^ (r & 7))) << 4);
+}
+
+__device__ __forceinline__ int seq_tokens(const DecodeParams &p, int b, bool report) {
+    int n = __ldg(p.ctx_lens + b) + p.len_offset;
+    if (n < 0) n = 0;
+    const int cap = p.table_stride * kBlockSize;
+    if (n > cap) {
+        if (report) set_status(p.status, LC_DEV_BAD_POS);
+        n = cap;
+    }
+    return n;
+}
+
+// Owner CTA of global page x under the balanced split start(c) = c*T/C.
+__device__ __forceinline__ int owner_cta(long long x, long long T, int C) {
+    return (int)(((x + 1) * C - 1) / T);
+}
+
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Barrier of the 128 consumer threads built on an mbarrier, so that a warp
+// that gave up on a wait cannot leave the others blocked for good.
+__device__ __forceinline__ void consumer_sync(uint64_t *bar, uint32_t &phase,
+                                              volatile int *abort_flag, int *status) {
+    mbar_arrive(bar);
+    mbar_wait_bounded(bar, phase & 1, abort_flag, status);
+    ++phase;
+}
+
+// Per-warp running softmax state of one chunk: heads 2c, 2c+1 of this lane.
+template <int HD>
+struct WarpState {
+    float o[HD / 16][4];
+    float m0, m1, l0, l1;
+    __device__ __forceinline__ void reset() {
+#pragma unroll
+        for (int i = 0; i < HD / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
+    }
+};
+
+// red slot layout: o[8][HD], m[8], l[8] (floats)
+template <int HD>
+__device__ __forceinline__ void state_store(float *red, const WarpState<HD> &st, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int i = 0; i < HD / 16; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            red[(2 * c + (e & 1)) * HD + 16 * i + g + (e >> 1) * 8] = st.o[i][e];
+    if (g == 0) {
+        red[kHeadsPerCta * HD + 2 * c] = st.m0;
+        red[kHeadsPerCta * HD + 2 * c + 1] = st.m1;
+        red[kHeadsPerCta * HD + kHeadsPerCta + 2 * c] = st.l0;
+        red[kHeadsPerCta * HD + kHeadsPerCta + 2 * c + 1] = st.l1;
+    }
+}
+
+template <int HD>
+__device__ __forceinline__ void state_combine(WarpState<HD> &st, const float *red, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    const float om0 = red[kHeadsPerCta * HD + 2 * c], om1 = red[kHeadsPerCta * HD + 2 * c + 1];
+    const float ol0 = red[kHeadsPerCta * HD + kHeadsPerCta + 2 * c];
+    const float ol1 = red[kHeadsPerCta * HD + kHeadsPerCta + 2 * c + 1];
+    const float M0 = fmaxf(st.m0, om0), M1 = fmaxf(st.m1, om1);
+    const float u0 = M0 == -INFINITY ? 0.f : M0, u1 = M1 == -INFINITY ? 0.f : M1;
+    const float a0 = fast_exp2(st.m0 - u0), b0 = fast_exp2(om0 - u0);
+    const float a1 = fast_exp2(st.m1 - u1), b1 = fast_exp2(om1 - u1);
+    st.m0 = M0;
+    st.m1 = M1;
+    st.l0 = st.l0 * a0 + ol0 * b0;
+    st.l1 = st.l1 * a1 + ol1 * b1;
+#pragma unroll
+    for (int i = 0; i < HD / 16; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float other = red[(2 * c + (e & 1)) * HD + 16 * i + g + (e >> 1) * 8];
+            st.o[i][e] = (e & 1) ? st.o[i][e] * a1 + other * b1 : st.o[i][e] * a0 + other * b0;
+        }
 }
 
 template <int HD>
@@ -101,123 +195,251 @@ __global__ void __launch_bounds__(kThreads)
 
     __shared__ __align__(8) uint64_t full_bar[Cfg::kStages];
     __shared__ __align__(8) uint64_t empty_bar[Cfg::kStages];
+    __shared__ __align__(8) uint64_t fin_bar;  // consumer-warp sync (bounded)
+    __shared__ StageMeta meta[Cfg::kStages];
+    __shared__ long long s_part[kThreads];
+    __shared__ long long s_total;
+    __shared__ int s_b0;
+    __shared__ long long s_pref_b0;
     __shared__ int s_abort;
-    __shared__ int s_last;
     extern __shared__ uint8_t smem_raw[];
 
-    const int b = blockIdx.z;
-    const int kvh = blockIdx.y / p.ctas_per_kv;
-    const int hsub = blockIdx.y - kvh * p.ctas_per_kv;
-    const int head0 = kvh * p.group + hsub * kHeadsPerCta;
-    const int nh = min(kHeadsPerCta, p.group - hsub * kHeadsPerCta);
-    const int part = blockIdx.x;
     const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int G = p.seg_per_seq;
 
-    int n = p.ctx_lens[b] + p.len_offset;
-    if (n < 0) n = 0;
-    const int table_cap = p.table_stride * kBlockSize;
-    if (n > table_cap) {
-        if (part == 0 && tid == 0) set_status(p.status, LC_DEV_BAD_POS);
-        n = table_cap;
+    // ---- 1. total pages T and empty-sequence outputs ------------------------
+    const int per = (p.batch + kThreads - 1) / kThreads;
+    const int bs = min(p.batch, tid * per), be = min(p.batch, bs + per);
+    long long mine = 0;
+    for (int b = bs; b < be; ++b) mine += (seq_tokens(p, b, false) + kBlockSize - 1) / kBlockSize;
+    s_part[tid] = mine;
+    for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
+        if (seq_tokens(p, b, false) == 0)
+            for (int i = tid; i < p.num_q_heads * HD; i += kThreads)
+                p.out[(int64_t)b * p.out_stride + i] = __float2bfloat16(0.f);
     }
-    if (n == 0) {  // empty context: defined as a zero output
-        if (part == 0)
-            for (int i = tid; i < nh * HD; i += kThreads)
-                p.out[(int64_t)b * p.out_stride + (int64_t)head0 * HD + i] = __float2bfloat16(0.f);
-        return;
+    __syncthreads();
+    if (warp == 0) {  // exclusive scan of the kThreads partial sums
+        constexpr int kPer = kThreads / 32;
+        long long v[kPer], run = 0;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            v[k] = s_part[lane * kPer + k];
+            run += v[k];
+        }
+        long long incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        long long ex = incl - run;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+            const long long x = v[k];
+            s_part[lane * kPer + k] = ex;
+            ex += x;
+        }
+        if (lane == 31) s_total = incl;
     }
-    int ptok = p.partition_tokens;
+    __syncthreads();
+    const long long T = s_total * G;
+    if (T == 0) return;
+    int C = gridDim.x;
     {
-        const int need = ((n + (int)gridDim.x - 1) / (int)gridDim.x + kBlockSize - 1) & ~(kBlockSize - 1);
-        if (need > ptok) ptok = need;
+        const long long want = p.partition_tokens > 0
+                                   ? (T * kBlockSize + p.partition_tokens - 1) / p.partition_tokens
+                                   : (T + 1) / 2;
+        if (want < C) C = (int)(want < 1 ? 1 : want);
+        if (T < C) C = (int)T;
     }
-    const int nparts = (n + ptok - 1) / ptok;
-    if (part >= nparts) return;
-    const int t0 = part * ptok;
-    const int t1 = min(t0 + ptok, n);
-    const int npages = (t1 - t0 + kBlockSize - 1) / kBlockSize;
-
+    const int cta = blockIdx.x;
+    if (cta >= C) return;
+    const long long start = (long long)cta * T / C;
+    const long long end = (long long)(cta + 1) * T / C;
+    if (start >= end) return;
+    // ---- 2. locate the sequence holding `start` -------------------------------
+    {
+        const long long lo = s_part[tid] * G;
+        const long long hi = lo + mine * G;
+        if (start >= lo && start < hi) {
+            long long pref = lo;
+            for (int b = bs; b < be; ++b) {
+                const long long np =
+                    (long long)((seq_tokens(p, b, false) + kBlockSize - 1) / kBlockSize) * G;
+                if (start < pref + np) {
+                    s_b0 = b;
+                    s_pref_b0 = pref;
+                    break;
+                }
+                pref += np;
+            }
+        }
+    }
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
-
     if (tid == 0) {
         for (int s = 0; s < Cfg::kStages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], kConsumerWarps);
         }
+        mbar_init(&fin_bar, kConsumerWarps * 32);
         s_abort = 0;
         fence_barrier_init();
     }
     __syncthreads();
-
-    const int warp = tid >> 5, lane = tid & 31;
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------ producer --
         if (lane == 0) {
             prefetch_tensormap(&tmap_k);
             prefetch_tensormap(&tmap_v);
+        }
+        int b = s_b0;
+        int n = seq_tokens(p, b, lane == 0);
+        int pages_b = (n + kBlockSize - 1) / kBlockSize;
+        const long long off = start - s_pref_b0;
+        int g = (int)(off / pages_b);
+        int pg = (int)(off - (long long)g * pages_b);
+        long long glob = start;
+        int it = 0;
+        bool ok = true;
+        while (glob < end && ok) {
+            if (pages_b == 0) {  // empty sequence: owns no pages
+                ++b;
+                n = seq_tokens(p, b, lane == 0);
+                pages_b = (n + kBlockSize - 1) / kBlockSize;
+                continue;
+            }
+            const int take = (int)min((long long)(pages_b - pg), end - glob);
+            const long long seg_start = glob - pg;
+            const int kvh = g / p.ctas_per_kv;
+            const int hsub = g - kvh * p.ctas_per_kv;
             const int *trow = p.tables + (int64_t)b * p.table_stride;
-            const int first_page = t0 / kBlockSize;
-            for (int pg = 0, it = 0; pg < npages; pg += kPagesPerStage, ++it) {
-                const int s = it % Cfg::kStages;
-                if (it >= Cfg::kStages &&
-                    !mbar_wait_bounded(&empty_bar[s], ((it / Cfg::kStages) - 1) & 1, &s_abort,
-                                       p.status))
-                    break;
-                const int np = min(kPagesPerStage, npages - pg);
-                mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(np * 2 * Cfg::kPageBytes));
-                const uint32_t stage = smem_base + s * Cfg::kStageBytes;
-                for (int j = 0; j < np; ++j) {
-                    const int phys = __ldg(trow + first_page + pg + j);
-                    int64_t row;
-                    if (phys < 0 || phys >= p.num_blocks) {
-                        set_status(p.status, LC_DEV_BAD_BLOCK);
-                        row = p.pool_rows;  // entirely out of bounds: TMA fills zeros
-                    } else {
-                        row = page_row(phys, p.layer, kvh, p.num_layers, p.num_kv_heads);
-                    }
-                    uint8_t *kdst = smem_gen + (stage - smem_base) + j * Cfg::kPageBytes;
-                    uint8_t *vdst = kdst + kPagesPerStage * Cfg::kPageBytes;
+            const int head0 = kvh * p.group + hsub * kHeadsPerCta;
+            const int nh = min(kHeadsPerCta, p.group - hsub * kHeadsPerCta);
+            for (int base = 0; base < take && ok; base += 32) {
+                const int cnt = min(32, take - base);
+                const int entry = lane < cnt ? __ldg(trow + pg + base + lane) : 0;
+                for (int j = 0; j < cnt && ok; j += kPagesPerStage) {
+                    const int np = min(kPagesPerStage, cnt - j);
+                    int phys[kPagesPerStage];
 #pragma unroll
-                    for (int h = 0; h < HD / 64; ++h) {
-                        tma_load_2d(kdst + h * 2048, &tmap_k, h * 64, (int)row, &full_bar[s]);
-                        tma_load_2d(vdst + h * 2048, &tmap_v, h * 64, (int)row, &full_bar[s]);
+                    for (int k = 0; k < kPagesPerStage; ++k)
+                        phys[k] = __shfl_sync(0xffffffffu, entry, (j + k) & 31);
+                    if (lane == 0) {
+                        const int s = it % Cfg::kStages;
+                        if (it >= Cfg::kStages &&
+                            !mbar_wait_bounded(&empty_bar[s], ((it / Cfg::kStages) - 1) & 1,
+                                               &s_abort, p.status)) {
+                            ok = false;
+                        } else {
+                            const bool first = base == 0 && j == 0;
+                            StageMeta &m = meta[s];
+                            m.b = b;
+                            m.g = g;
+                            m.page0 = pg + base + j;
+                            m.np = np;
+                            m.n = n;
+                            m.pages_b = pages_b;
+                            m.flags = (first ? kFirst : 0) | (base + j + np == take ? kLast : 0);
+                            m.chunk_p0 = pg;
+                            m.take = take;
+                            m.seg_start = seg_start;
+                            const uint32_t qbytes = first ? (uint32_t)(nh * HD * 2) : 0u;
+                            mbar_arrive_expect_tx(&full_bar[s],
+                                                  (uint32_t)(np * 2 * Cfg::kPageBytes) + qbytes);
+                            if (first)
+                                bulk_load(smem_gen + Cfg::kQOffset + s * Cfg::kQBytes,
+                                          p.q + (int64_t)b * p.q_stride + (int64_t)head0 * HD,
+                                          qbytes, &full_bar[s]);
+                            uint8_t *kst = smem_gen + s * Cfg::kStageBytes;
+                            for (int k = 0; k < np; ++k) {
+                                int64_t row;
+                                if (phys[k] < 0 || phys[k] >= p.num_blocks) {
+                                    set_status(p.status, LC_DEV_BAD_BLOCK);
+                                    row = p.pool_rows;  // wholly out of bounds: zero fill
+                                } else {
+                                    row = page_row(phys[k], p.layer, kvh, p.num_layers,
+                                                   p.num_kv_heads);
+                                }
+                                uint8_t *kd = kst + k * Cfg::kPageBytes;
+                                uint8_t *vd = kd + kPagesPerStage * Cfg::kPageBytes;
+#pragma unroll
+                                for (int h = 0; h < HD / 64; ++h) {
+                                    tma_load_2d(kd + h * 2048, &tmap_k, h * 64, (int)row,
+                                                &full_bar[s]);
+                                    tma_load_2d(vd + h * 2048, &tmap_v, h * 64, (int)row,
+                                                &full_bar[s]);
+                                }
+                            }
+                        }
                     }
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    ++it;
                 }
             }
+            glob += take;
+            pg = 0;
+            if (++g == G) {
+                g = 0;
+                ++b;
+                if (glob < end) {
+                    n = seq_tokens(p, b, lane == 0);
+                    pages_b = (n + kBlockSize - 1) / kBlockSize;
+                }
+            }
+        }
+        if (lane == 0 && ok) {  // end-of-range marker
+            const int s = it % Cfg::kStages;
+            if (it < Cfg::kStages || mbar_wait_bounded(&empty_bar[s], ((it / Cfg::kStages) - 1) & 1,
+                                                       &s_abort, p.status)) {
+                meta[s].flags = kDone;
+                mbar_arrive(&full_bar[s]);
+            }
+        }
+        if (lane == 0 && s_abort) {
+            // A wait gave up: let the copies of the last stages land before exit.
+            for (int k = it - Cfg::kStages; k < it; ++k)
+                if (k >= 0) mbar_wait_drain(&full_bar[k % Cfg::kStages], (k / Cfg::kStages) & 1);
         }
         return;
     }
 
     // ---------------------------------------------------------- consumers --
-    const int g = lane >> 2, c = lane & 3;
-    uint32_t qf[KSTEPS][2];
-    {
-        const bool hv = g < nh;
-        const bf16 *qrow = p.q + (int64_t)b * p.q_stride + (int64_t)(head0 + (hv ? g : 0)) * HD;
-#pragma unroll
-        for (int j = 0; j < KSTEPS; ++j) {
-            qf[j][0] = hv ? __ldg(reinterpret_cast<const uint32_t *>(qrow + 16 * j + 2 * c)) : 0u;
-            qf[j][1] = hv ? __ldg(reinterpret_cast<const uint32_t *>(qrow + 16 * j + 8 + 2 * c)) : 0u;
-        }
-    }
-    float o[KSTEPS][4];
-#pragma unroll
-    for (int i = 0; i < KSTEPS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-    // Per-lane ldmatrix row/chunk selectors.
+    const int g8 = lane >> 2, c4 = lane & 3;
     const int mi = lane >> 3, r8 = lane & 7;
     const int k_row = (mi & 1) * 8 + r8, k_chunk = mi >> 1;  // QK A operand (K tile)
     const int v_row = (mi >> 1) * 8 + r8, v_chunk = mi & 1;  // PV A operand (V^T tile)
+    float *red = reinterpret_cast<float *>(smem_gen + Cfg::kRedOffset);
+    constexpr int kRedFloats = Cfg::kRedFloats;
 
-    for (int pg = 0, it = 0; pg < npages; pg += kPagesPerStage, ++it) {
+    uint32_t qf[KSTEPS][2];
+    uint32_t fin_phase = 0;
+    WarpState<HD> st;
+    st.reset();
+    for (int it = 0;; ++it) {
         const int s = it % Cfg::kStages;
         if (!mbar_wait_bounded(&full_bar[s], (it / Cfg::kStages) & 1, &s_abort, p.status)) break;
-        const int pi = pg + warp;
-        if (pi < npages) {
-            const int valid = min(kBlockSize, t1 - (t0 + pi * kBlockSize));
+        const StageMeta m = meta[s];
+        if (m.flags & kDone) break;
+        const int kvh = m.g / p.ctas_per_kv;
+        const int hsub = m.g - kvh * p.ctas_per_kv;
+        const int nh = min(kHeadsPerCta, p.group - hsub * kHeadsPerCta);
+        if (m.flags & kFirst) {
+            const uint8_t *qs = smem_gen + Cfg::kQOffset + s * Cfg::kQBytes;
+            const bool hv = g8 < nh;
+#pragma unroll
+            for (int j = 0; j < KSTEPS; ++j) {
+                qf[j][0] = hv ? *reinterpret_cast<const uint32_t *>(qs + (g8 * HD + 16 * j + 2 * c4) * 2) : 0u;
+                qf[j][1] = hv ? *reinterpret_cast<const uint32_t *>(qs + (g8 * HD + 16 * j + 8 + 2 * c4) * 2) : 0u;
+            }
+            st.reset();
+        }
+        if (warp < m.np) {
+            const int page = m.page0 + warp;
+            const int valid = min(kBlockSize, m.n - page * kBlockSize);
             const uint32_t kpage = smem_base + s * Cfg::kStageBytes + warp * Cfg::kPageBytes;
             const uint32_t vpage = kpage + kPagesPerStage * Cfg::kPageBytes;
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -227,33 +449,33 @@ __global__ void __launch_bounds__(kThreads)
                 ldmatrix_x4(a, tile_addr(kpage, k_row, 2 * j + k_chunk));
                 mma_bf16_16816(sc, a, qf[j][0], qf[j][1]);
             }
-            // sc: (tok g, head 2c), (g, 2c+1), (g+8, 2c), (g+8, 2c+1)
-            float s0 = g < valid ? sc[0] * p.scale_log2 : -INFINITY;
-            float s1 = g < valid ? sc[1] * p.scale_log2 : -INFINITY;
-            float s2 = g + 8 < valid ? sc[2] * p.scale_log2 : -INFINITY;
-            float s3 = g + 8 < valid ? sc[3] * p.scale_log2 : -INFINITY;
+            // sc: (tok g8, head 2c4), (g8, 2c4+1), (g8+8, 2c4), (g8+8, 2c4+1)
+            const float s0 = g8 < valid ? sc[0] * p.scale_log2 : -INFINITY;
+            const float s1 = g8 < valid ? sc[1] * p.scale_log2 : -INFINITY;
+            const float s2 = g8 + 8 < valid ? sc[2] * p.scale_log2 : -INFINITY;
+            const float s3 = g8 + 8 < valid ? sc[3] * p.scale_log2 : -INFINITY;
             float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
 #pragma unroll
             for (int off = 4; off < 32; off <<= 1) {
                 mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
                 mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
             }
-            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+            const float mn0 = fmaxf(st.m0, mx0), mn1 = fmaxf(st.m1, mx1);
             const float mu0 = mn0 == -INFINITY ? 0.f : mn0;
             const float mu1 = mn1 == -INFINITY ? 0.f : mn1;
-            const float al0 = fast_exp2(m0 - mu0), al1 = fast_exp2(m1 - mu1);
-            m0 = mn0;
-            m1 = mn1;
+            const float al0 = fast_exp2(st.m0 - mu0), al1 = fast_exp2(st.m1 - mu1);
+            st.m0 = mn0;
+            st.m1 = mn1;
             const float p0 = fast_exp2(s0 - mu0), p1 = fast_exp2(s1 - mu1);
             const float p2 = fast_exp2(s2 - mu0), p3 = fast_exp2(s3 - mu1);
-            l0 = l0 * al0 + (p0 + p2);
-            l1 = l1 * al1 + (p1 + p3);
+            st.l0 = st.l0 * al0 + (p0 + p2);
+            st.l1 = st.l1 * al1 + (p1 + p3);
 #pragma unroll
             for (int i = 0; i < KSTEPS; ++i) {
-                o[i][0] *= al0;
-                o[i][1] *= al1;
-                o[i][2] *= al0;
-                o[i][3] *= al1;
+                st.o[i][0] *= al0;
+                st.o[i][1] *= al1;
+                st.o[i][2] *= al0;
+                st.o[i][3] *= al1;
             }
             const uint32_t b0 = movmatrix_trans(pack_bf16(p0, p1));
             const uint32_t b1 = movmatrix_trans(pack_bf16(p2, p3));
@@ -261,134 +483,162 @@ __global__ void __launch_bounds__(kThreads)
             for (int i = 0; i < KSTEPS; ++i) {
                 uint32_t a[4];
                 ldmatrix_x4_trans(a, tile_addr(vpage, v_row, 2 * i + v_chunk));
-                mma_bf16_16816(o[i], a, b0, b1);
+                mma_bf16_16816(st.o[i], a, b0, b1);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[s]);
-    }
+        if (!(m.flags & kLast)) continue;
 
-    // Sum l over the 8 token lanes of each head column.
+        // ---------------------------------------------- finish the chunk --
 #pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-    }
-
-    // ------------------------------------------- merge the 4 consumer warps --
-    // The stage ring is idle now (every load was waited for); reuse it.
-    float *red_m = reinterpret_cast<float *>(smem_gen);           // [4][8]
-    float *red_l = red_m + kConsumerWarps * kHeadsPerCta;          // [4][8]
-    float *red_o = red_l + kConsumerWarps * kHeadsPerCta;          // [4][8][HD]
-    float *wts = red_o + kConsumerWarps * kHeadsPerCta * HD;       // [8][kMaxPartitions]
-    float *wsum = wts + kHeadsPerCta * kMaxPartitions;             // [8]
-    named_barrier_sync(1, kConsumerWarps * 32);
-    if (g == 0) {
-        red_m[warp * kHeadsPerCta + 2 * c] = m0;
-        red_m[warp * kHeadsPerCta + 2 * c + 1] = m1;
-        red_l[warp * kHeadsPerCta + 2 * c] = l0;
-        red_l[warp * kHeadsPerCta + 2 * c + 1] = l1;
-    }
-#pragma unroll
-    for (int i = 0; i < KSTEPS; ++i)
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-            red_o[(warp * kHeadsPerCta + 2 * c + (e & 1)) * HD + 16 * i + g + (e >> 1) * 8] = o[i][e];
-    named_barrier_sync(1, kConsumerWarps * 32);
-
-    const int ct = tid;  // 0..127
-    const int64_t ws_row0 = ((int64_t)b * p.num_q_heads + head0) * gridDim.x;
-    for (int idx = ct; idx < nh * HD; idx += kConsumerWarps * 32) {
-        const int h = idx / HD, d = idx - (idx / HD) * HD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red_m[w * kHeadsPerCta + h]);
-        float L = 0.f, O = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-            const float f = fast_exp2(red_m[w * kHeadsPerCta + h] - M);
-            L += red_l[w * kHeadsPerCta + h] * f;
-            O += red_o[(w * kHeadsPerCta + h) * HD + d] * f;
+        for (int off = 4; off < 32; off <<= 1) {  // l over the 8 token lanes of a head
+            st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, off);
+            st.l1 += __shfl_xor_sync(0xffffffffu, st.l1, off);
         }
-        if (nparts == 1) {
-            p.out[(int64_t)b * p.out_stride + (int64_t)(head0 + h) * HD + d] = __float2bfloat16(O / L);
-        } else {
-            const int64_t wr = ws_row0 + (int64_t)h * gridDim.x + part;
-            p.ws_o[wr * HD + d] = O / L;
-            if (d == 0) p.ws_lse[wr] = M + __log2f(L);
+        // Tree merge of the 4 warps through two shared slots.
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        if (warp >= 2) state_store<HD>(red + (warp - 2) * kRedFloats, st, lane);
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        if (warp < 2) state_combine<HD>(st, red + warp * kRedFloats, lane);
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        if (warp == 1) state_store<HD>(red, st, lane);
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        if (warp != 0) {
+            st.reset();
+            continue;
         }
-    }
-    if (nparts == 1) return;
-
-    // ------------------------------------------------ split-K merge (last CTA) --
-    __threadfence();
-    named_barrier_sync(1, kConsumerWarps * 32);
-    int *cnt = p.ws_cnt + (int64_t)b * gridDim.y + blockIdx.y;
-    if (ct == 0) s_last = (atomicAdd(cnt, 1) == nparts - 1);
-    named_barrier_sync(1, kConsumerWarps * 32);
-    if (!s_last) return;
-    __threadfence();
-    for (int h = warp; h < nh; h += kConsumerWarps) {
-        const float *lse = p.ws_lse + ws_row0 + (int64_t)h * gridDim.x;
-        float M = -INFINITY;
-        for (int q = lane; q < nparts; q += 32) M = fmaxf(M, __ldcg(lse + q));
-        M = warp_max(M);
-        float S = 0.f;
-        for (int q = lane; q < nparts; q += 32) {
-            const float w = fast_exp2(__ldcg(lse + q) - M);
-            wts[h * kMaxPartitions + q] = w;
-            S += w;
+        state_combine<HD>(st, red, lane);
+        const int head0 = kvh * p.group + hsub * kHeadsPerCta;
+        const int seg = m.b * G + m.g;
+        const bool whole = m.chunk_p0 == 0 && m.take == m.pages_b;
+        const float il0 = 1.f / st.l0, il1 = 1.f / st.l1;
+        if (whole) {
+            bf16 *orow = p.out + (int64_t)m.b * p.out_stride + (int64_t)head0 * HD;
+#pragma unroll
+            for (int i = 0; i < KSTEPS; ++i)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int h = 2 * c4 + (e & 1);
+                    if (h < nh)
+                        orow[h * HD + 16 * i + g8 + (e >> 1) * 8] =
+                            __float2bfloat16(st.o[i][e] * ((e & 1) ? il1 : il0));
+                }
+            st.reset();
+            continue;
         }
-        S = warp_sum(S);
-        if (lane == 0) wsum[h] = S;
+        // Partial of a split segment: slot = segment + this CTA.
+        const long long slot = (long long)seg + cta;
+        float *wo = p.ws_o + slot * kHeadsPerCta * HD;
+#pragma unroll
+        for (int i = 0; i < KSTEPS; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int h = 2 * c4 + (e & 1);
+                wo[h * HD + 16 * i + g8 + (e >> 1) * 8] = st.o[i][e] * ((e & 1) ? il1 : il0);
+            }
+        if (g8 == 0) {
+            p.ws_lse[slot * kHeadsPerCta + 2 * c4] = st.m0 + __log2f(st.l0);
+            p.ws_lse[slot * kHeadsPerCta + 2 * c4 + 1] = st.m1 + __log2f(st.l1);
+        }
+        st.reset();
+        __threadfence();
+        __syncwarp();
+        const int c_first = owner_cta(m.seg_start, T, C);
+        const int c_last = owner_cta(m.seg_start + m.pages_b - 1, T, C);
+        const int nch = c_last - c_first + 1;
+        int last = 0;
+        if (lane == 0) last = atomicAdd(p.ws_cnt + seg, 1) == nch - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        // Merge the nch partials of this segment (slots seg + c_first + j).
+        const long long slot0 = (long long)seg + c_first;
+        for (int h = 0; h < nh; ++h) {
+            float M = -INFINITY;
+            for (int j = lane; j < nch; j += 32)
+                M = fmaxf(M, __ldcg(p.ws_lse + (slot0 + j) * kHeadsPerCta + h));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            float acc[HD / 32];
+#pragma unroll
+            for (int k = 0; k < HD / 32; ++k) acc[k] = 0.f;
+            float S = 0.f;
+            for (int j = 0; j < nch; ++j) {
+                const float w = fast_exp2(__ldcg(p.ws_lse + (slot0 + j) * kHeadsPerCta + h) - M);
+                S += w;
+                const float *src = p.ws_o + ((slot0 + j) * kHeadsPerCta + h) * HD;
+#pragma unroll
+                for (int k = 0; k < HD / 32; ++k) acc[k] += w * __ldcg(src + k * 32 + lane);
+            }
+            const float inv = 1.f / S;
+            bf16 *orow = p.out + (int64_t)m.b * p.out_stride + (int64_t)(head0 + h) * HD;
+#pragma unroll
+            for (int k = 0; k < HD / 32; ++k) orow[k * 32 + lane] = __float2bfloat16(acc[k] * inv);
+        }
+        if (lane == 0) p.ws_cnt[seg] = 0;  // ready for the next call
     }
-    named_barrier_sync(1, kConsumerWarps * 32);
-    for (int idx = ct; idx < nh * HD; idx += kConsumerWarps * 32) {
-        const int h = idx / HD, d = idx - (idx / HD) * HD;
-        const float *src = p.ws_o + (ws_row0 + (int64_t)h * gridDim.x) * HD + d;
-        float acc = 0.f;
-        for (int q = 0; q < nparts; ++q) acc += wts[h * kMaxPartitions + q] * __ldcg(src + (int64_t)q * HD);
-        p.out[(int64_t)b * p.out_stride + (int64_t)(head0 + h) * HD + d] = __float2bfloat16(acc / wsum[h]);
-    }
-    if (ct == 0) *cnt = 0;  // leave the counter ready for the next call
 }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace layout of one call: counters [batch*Hq] int32 | lse [batch*Hq*parts]
-// f32 | o [batch*Hq*parts*hd] f32. Counters sit first so that their place does
-// not depend on the partition count.
-size_t ws_counters_bytes(int batch, int hq) { return align256((size_t)batch * hq * 4); }
-size_t ws_lse_bytes(int batch, int hq, int parts) { return align256((size_t)batch * hq * parts * 4); }
-size_t ws_total(int batch, int hq, int hd, int parts) {
-    return ws_counters_bytes(batch, hq) + ws_lse_bytes(batch, hq, parts) +
-           (size_t)batch * hq * parts * hd * 4;
+// Workspace layout: counters [batch*segments] int32 | lse [slots][8] f32 |
+// o [slots][8][hd] f32, with slots = persistent CTAs + batch*segments.
+struct WsLayout {
+    size_t cnt_bytes, lse_bytes, o_bytes;
+    size_t total() const { return cnt_bytes + lse_bytes + o_bytes; }
+};
+
+WsLayout ws_layout(int batch, int segments_per_seq, int hd, int max_ctas) {
+    const size_t segs = (size_t)batch * segments_per_seq;
+    const size_t slots = segs + (size_t)max_ctas;
+    WsLayout l;
+    l.cnt_bytes = align256(segs * 4);
+    l.lse_bytes = align256(slots * kHeadsPerCta * 4);
+    l.o_bytes = slots * kHeadsPerCta * hd * 4;
+    return l;
 }
 
-void choose_partitions(int batch, int hq, int hkv, int max_ctx, int partition_tokens, int *ptok,
-                       int *parts) {
-    if (max_ctx < 1) max_ctx = 1;
-    int P;
-    if (partition_tokens > 0) {
-        P = (partition_tokens + kBlockSize - 1) / kBlockSize * kBlockSize;
-    } else {
-        const int group = hq / hkv;
-        const int64_t units = (int64_t)batch * hkv * ((group + kHeadsPerCta - 1) / kHeadsPerCta);
-        const int64_t target = 2 * (int64_t)sm_count();
-        P = 512;
-        while (P > 64 && units * ((max_ctx + P - 1) / P) < target) P >>= 1;
+int segments_per_seq(int hq, int hkv) {
+    const int group = hq / hkv;
+    return hkv * ((group + kHeadsPerCta - 1) / kHeadsPerCta);
+}
+
+// Persistent grid: resident CTAs per SM for this head_dim, times the SM count.
+// Without a usable device (host-only callers sizing a workspace) a B200's
+// 148 SMs are assumed.
+template <int HD>
+int max_ctas_for_device() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        dev = -1;
     }
-    int n = (max_ctx + P - 1) / P;
-    if (n > kMaxPartitions) n = kMaxPartitions;
-    if (n < 1) n = 1;
-    *ptok = P;
-    *parts = n;
+    const int idx = dev < 0 || dev >= 64 ? 0 : dev;
+    if (!cached[idx] || dev < 0) {
+        int per_sm = 0;
+        const int smem = DecodeCfg<HD>::kSmemBytes;
+        if (dev < 0 ||
+            ensure_smem_attr((const void *)paged_decode_kernel<HD>, smem) != LC_OK ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<HD>,
+                                                          kThreads, smem) != cudaSuccess ||
+            per_sm < 1) {
+            cudaGetLastError();
+            per_sm = HD == 64 ? 3 : 2;
+        }
+        const int n = per_sm * sm_count();
+        if (dev < 0) return n;
+        cached[idx] = n;
+    }
+    return cached[idx];
 }
 
+int max_ctas(int hd) { return hd == 64 ? max_ctas_for_device<64>() : max_ctas_for_device<128>(); }
 
 template <int HD>
-int launch_decode(const DecodeParams &prm, int parts, int batch, const void *k_pool,
-                  const void *v_pool, cudaStream_t stream) {
+int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const void *v_pool,
+                  cudaStream_t stream) {
     CUtensorMap mk, mv;
     int rc = pool_tensor_map(k_pool, prm.pool_rows, HD, &mk);
     if (rc) return rc;
@@ -397,7 +647,6 @@ int launch_decode(const DecodeParams &prm, int parts, int batch, const void *k_p
     const int smem = DecodeCfg<HD>::kSmemBytes;
     rc = ensure_smem_attr((const void *)paged_decode_kernel<HD>, smem);
     if (rc) return rc;
-    dim3 grid(parts, prm.num_kv_heads * prm.ctas_per_kv, batch);
     paged_decode_kernel<HD><<<grid, kThreads, smem, stream>>>(mk, mv, prm);
     return launch_status();
 }
@@ -408,12 +657,13 @@ int launch_decode(const DecodeParams &prm, int parts, int batch, const void *k_p
 using namespace lc;
 
 extern "C" size_t lc_paged_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
-                                                 int head_dim, int max_partitions) {
-    (void)num_kv_heads;
-    if (batch <= 0 || num_q_heads <= 0 || head_dim <= 0) return 0;
-    if (max_partitions < 1) max_partitions = 1;
-    if (max_partitions > kMaxPartitions) max_partitions = kMaxPartitions;
-    return ws_total(batch, num_q_heads, head_dim, max_partitions);
+                                                 int head_dim) {
+    if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads)
+        return 0;
+    if (head_dim != 64 && head_dim != 128) return 0;
+    return ws_layout(batch, segments_per_seq(num_q_heads, num_kv_heads), head_dim,
+                     max_ctas(head_dim))
+        .total();
 }
 
 extern "C" int lc_paged_decode_workspace_init(void *workspace, size_t workspace_bytes,
@@ -423,15 +673,6 @@ extern "C" int lc_paged_decode_workspace_init(void *workspace, size_t workspace_
     return cudaMemsetAsync(workspace, 0, workspace_bytes, as_stream(stream)) == cudaSuccess
                ? LC_OK
                : LC_ERR_CUDA;
-}
-
-extern "C" int lc_paged_decode_partitions(int batch, int num_q_heads, int num_kv_heads,
-                                          int max_context_len, int partition_tokens) {
-    if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0) return 1;
-    int ptok, parts;
-    choose_partitions(batch, num_q_heads, num_kv_heads, max_context_len, partition_tokens, &ptok,
-                      &parts);
-    return parts;
 }
 
 extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int64_t q_stride,
@@ -447,11 +688,10 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     if (head_dim != 64 && head_dim != 128) return LC_ERR_UNSUPPORTED_HEAD_DIM;
     if (batch < 0 || num_layers <= 0 || layer < 0 || layer >= num_layers || num_q_heads <= 0 ||
         num_kv_heads <= 0 || num_blocks <= 0 || table_stride <= 0 || len_offset < 0 ||
-        len_offset > 1)
+        len_offset > 1 || partition_tokens < 0)
         return LC_ERR_INVALID_ARGUMENT;
     if (num_q_heads % num_kv_heads) return LC_ERR_UNSUPPORTED_SHAPE;
     if (batch == 0) return LC_OK;
-    if (batch > 65535) return LC_ERR_INVALID_ARGUMENT;
     if (!aligned16(k_pool) || !aligned16(v_pool) || !aligned16(q) || (q_stride & 7) ||
         ((uintptr_t)out & 1))
         return LC_ERR_MISALIGNED;
@@ -460,9 +700,20 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     const int64_t pool_rows = num_blocks * num_layers * num_kv_heads * kBlockSize;
     if (pool_rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
 
-    int ptok, parts;
-    choose_partitions(batch, num_q_heads, num_kv_heads, max_context_len, partition_tokens, &ptok,
-                      &parts);
+    const int G = segments_per_seq(num_q_heads, num_kv_heads);
+    const int cmax = max_ctas(head_dim);
+    const WsLayout wl = ws_layout(batch, G, head_dim, cmax);
+    if (!workspace || workspace_bytes < wl.total()) return LC_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned16(workspace)) return LC_ERR_MISALIGNED;
+    // Grid: the persistent size, trimmed when the host's context hint shows
+    // there is less work than two pages per CTA.
+    int grid = cmax;
+    if (max_context_len > 0) {
+        const long long pages_hint =
+            (long long)batch * G * ((max_context_len + kBlockSize - 1) / kBlockSize);
+        const long long want = (pages_hint + 1) / 2;
+        if (want < grid) grid = (int)(want < 1 ? 1 : want);
+    }
     DecodeParams prm{};
     prm.out = (bf16 *)out;
     prm.out_stride = out_stride;
@@ -472,6 +723,7 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     prm.table_stride = table_stride;
     prm.ctx_lens = context_lens;
     prm.len_offset = len_offset;
+    prm.batch = batch;
     prm.pool_rows = pool_rows;
     prm.num_blocks = num_blocks;
     prm.num_layers = num_layers;
@@ -480,29 +732,25 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     prm.num_kv_heads = num_kv_heads;
     prm.group = num_q_heads / num_kv_heads;
     prm.ctas_per_kv = (prm.group + kHeadsPerCta - 1) / kHeadsPerCta;
-    prm.partition_tokens = ptok;
+    prm.seg_per_seq = G;
+    prm.partition_tokens = partition_tokens;
     prm.scale_log2 = sm_scale * 1.4426950408889634f;
+    uint8_t *ws = (uint8_t *)workspace;
+    prm.ws_cnt = (int *)ws;
+    prm.ws_lse = (float *)(ws + wl.cnt_bytes);
+    prm.ws_o = (float *)(ws + wl.cnt_bytes + wl.lse_bytes);
     prm.status = dev_status;
-    if (parts > 1) {
-        const size_t need = ws_total(batch, num_q_heads, head_dim, parts);
-        if (!workspace || workspace_bytes < need || !aligned16(workspace))
-            return workspace && !aligned16(workspace) ? LC_ERR_MISALIGNED
-                                                      : LC_ERR_WORKSPACE_TOO_SMALL;
-        uint8_t *ws = (uint8_t *)workspace;
-        prm.ws_cnt = (int *)ws;
-        prm.ws_lse = (float *)(ws + ws_counters_bytes(batch, num_q_heads));
-        prm.ws_o = (float *)(ws + ws_counters_bytes(batch, num_q_heads) +
-                             ws_lse_bytes(batch, num_q_heads, parts));
-    }
     cudaStream_t s = as_stream(stream);
-    return head_dim == 64 ? launch_decode<64>(prm, parts, batch, k_pool, v_pool, s)
-                          : launch_decode<128>(prm, parts, batch, k_pool, v_pool, s);
+    return head_dim == 64 ? launch_decode<64>(prm, grid, k_pool, v_pool, s)
+                          : launch_decode<128>(prm, grid, k_pool, v_pool, s);
 }
 
 extern "C" size_t lc_flash_decoding_workspace_size(int num_q_heads, int head_dim,
                                                    int max_seq_len) {
-    int parts = (max_seq_len + 63) / 64;
-    return lc_paged_decode_workspace_size(1, num_q_heads, 1, head_dim, parts);
+    (void)max_seq_len;  // the persistent split needs no per-length storage
+    // Hq bounds the number of (kv head, 8-head slice) segments of one sequence.
+    if (num_q_heads <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
+    return ws_layout(1, num_q_heads, head_dim, max_ctas(head_dim)).total();
 }
 
 extern "C" int lc_flash_decoding(void *output, const void *q, const void *k_pool,
@@ -514,11 +762,15 @@ extern "C" int lc_flash_decoding(void *output, const void *q, const void *k_pool
                                  size_t workspace_bytes, lc_stream_t stream) {
     if (block_size != kBlockSize) return LC_ERR_UNSUPPORTED_SHAPE;
     if (host_pos < 0 || max_seq_len <= 0) return LC_ERR_INVALID_ARGUMENT;
+    if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads)
+        return num_q_heads > 0 && num_kv_heads > 0 ? LC_ERR_UNSUPPORTED_SHAPE
+                                                   : LC_ERR_INVALID_ARGUMENT;
     // The reference's table holds ceil(max_position_embeddings / 16) entries
     // (src/layers/kv_cache.rs:70-71).
     int table_len = (max_seq_len + kBlockSize - 1) / kBlockSize;
     if (table_len < host_pos / kBlockSize + 1) table_len = host_pos / kBlockSize + 1;
     const int64_t stride = (int64_t)num_q_heads * head_dim;
+    // The workspace was sized with Hq segments; the call needs Hkv*ceil(group/8).
     return lc_paged_decode(output, stride, q, stride, k_pool, v_pool, num_physical_blocks,
                            num_layers, layer_idx, num_q_heads, num_kv_heads, head_dim,
                            block_table, table_len, current_pos, /*len_offset=*/1, 1,

@@ -36,9 +36,8 @@ SIGNATURES = {
                                  _f32, _i32, _i32, _i32, _i64, _vp, _sz, _vp]),
     "lc_rope_append": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp,
                               _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _vp]),
-    "lc_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32, _i32]),
+    "lc_paged_decode_workspace_size": (_sz, [_i32, _i32, _i32, _i32]),
     "lc_paged_decode_workspace_init": (_i32, [_vp, _sz, _vp]),
-    "lc_paged_decode_partitions": (_i32, [_i32, _i32, _i32, _i32, _i32]),
     "lc_paged_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _sz,
                                _vp, _vp]),
@@ -147,24 +146,15 @@ def rope_append(qkv, positions, q_bias, k_bias, v_bias, cos, sin, k_pool, v_pool
           "lc_rope_append")
 
 
-def paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, max_partitions) -> int:
-    return lib.lc_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim,
-                                              max_partitions)
+def paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim) -> int:
+    return lib.lc_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim)
 
 
-def paged_decode_partitions(batch, num_q_heads, num_kv_heads, max_context_len,
-                            partition_tokens=0) -> int:
-    return lib.lc_paged_decode_partitions(batch, num_q_heads, num_kv_heads, max_context_len,
-                                          partition_tokens)
-
-
-def alloc_decode_workspace(batch, num_q_heads, num_kv_heads, head_dim, max_context_len,
-                           partition_tokens=0, device="cuda", stream=None):
+def alloc_decode_workspace(batch, num_q_heads, num_kv_heads, head_dim, device="cuda",
+                           stream=None):
     """Allocates (torch) and zero-initialises a workspace for lc_paged_decode."""
     import torch
-    parts = paged_decode_partitions(batch, num_q_heads, num_kv_heads, max_context_len,
-                                    partition_tokens)
-    nbytes = paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, parts)
+    nbytes = paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim)
     ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
     check(lib.lc_paged_decode_workspace_init(_p(ws), nbytes, _stream(stream)),
           "lc_paged_decode_workspace_init")
@@ -172,7 +162,7 @@ def alloc_decode_workspace(batch, num_q_heads, num_kv_heads, head_dim, max_conte
 
 
 def paged_decode(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_heads,
-                 num_kv_heads, head_dim, block_tables, context_lens, max_context_len,
+                 num_kv_heads, head_dim, block_tables, context_lens, max_context_len=0,
                  sm_scale=None, len_offset=0, partition_tokens=0, workspace=None,
                  dev_status=None, stream=None):
     if sm_scale is None:

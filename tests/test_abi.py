@@ -100,21 +100,17 @@ def test_prefill_rejects_bad_arguments():
     assert rc in (2, 11)
 
 
-def test_workspace_and_partitions():
-    # explicit partition size: ceil(ctx / P)
-    assert L.paged_decode_partitions(64, 14, 2, 4096, 512) == 8
-    assert L.paged_decode_partitions(64, 14, 2, 4000, 512) == 8
-    assert L.paged_decode_partitions(1, 14, 2, 1024, 64) == 16
-    # capped at 256 partitions
-    assert L.paged_decode_partitions(1, 14, 2, 10**6, 16) == 256
-    # auto: large batches keep 512-token partitions, a single sequence goes finer
-    assert L.paged_decode_partitions(64, 14, 2, 4096, 0) == 8
-    assert L.paged_decode_partitions(1, 14, 2, 1024, 0) == 16
-    ws1 = L.paged_decode_workspace_size(4, 28, 4, 128, 16)
-    assert ws1 >= 4 * 28 * 16 * 128 * 4 + 4 * 28 * 16 * 4 + 4 * 28 * 4
-    assert ws1 % 256 == 0 or ws1 == 4 * 28 * 4  # layout is 256-byte aligned between arrays
-    assert L.flash_decoding_workspace_size(14, 64, 32768) >= \
-        L.paged_decode_workspace_size(1, 14, 2, 64, 512)
+def test_workspace_sizes():
+    # host-only sizing assumes a 148-SM B200: 3 CTAs/SM at hd 64, 2 at hd 128
+    segs = 64 * 2                      # batch x (kv heads x 8-head slices)
+    slots = segs + 148 * 3
+    want = ((segs * 4 + 255) // 256 * 256 + (slots * 8 * 4 + 255) // 256 * 256
+            + slots * 8 * 64 * 4)
+    assert L.paged_decode_workspace_size(64, 14, 2, 64) == want
+    assert L.paged_decode_workspace_size(1, 64, 4, 128) > 0   # group 16: two slices per kv head
+    assert L.paged_decode_workspace_size(4, 14, 3, 64) == 0   # invalid shape
+    assert L.paged_decode_workspace_size(4, 14, 2, 96) == 0
+    assert L.flash_decoding_workspace_size(14, 64, 32768) >= L.paged_decode_workspace_size(1, 14, 2, 64)
 
 
 @pytest.mark.parametrize("hd,base,scale", [(64, 1e6, 0.0), (128, 1e6, 0.0), (128, 1e4, 4.0),

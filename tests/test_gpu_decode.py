@@ -28,8 +28,7 @@ def gpu_decode(case, d=None, partition_tokens=0, len_offset=0, q=None, out=None,
     if lens is None:
         lens = to_device((case.ctx - len_offset).astype(np.int32))
     if ws is None:
-        ws = L.alloc_decode_workspace(case.batch, case.hq, case.hkv, case.hd, max(case.max_ctx, 1),
-                                      partition_tokens)
+        ws = L.alloc_decode_workspace(case.batch, case.hq, case.hkv, case.hd)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     L.paged_decode(out, q, d["k"], d["v"], case.num_blocks, case.num_layers, case.layer, case.hq,
                    case.hkv, case.hd, d["tables"], lens, max(case.max_ctx, 1),
@@ -79,12 +78,13 @@ def test_decode_long_context_many_partitions():
     assert max_err(from_device(out), oracle_decode(case)) <= ATTN_ATOL
 
 
-def test_decode_grid_smaller_than_context_grows_partitions():
-    # max_context_len hint far below the real lengths: the device grows partitions.
+def test_decode_context_hint_below_real_lengths():
+    # max_context_len hint far below the real lengths trims the grid; the split
+    # over the CTAs that remain still covers every page.
     case = make_case(2, 14, 2, 64, [3000, 1200], seed=9)
     d = dev_case(case)
     out = torch.empty(2, 14 * 64, dtype=torch.bfloat16, device="cuda")
-    ws = L.alloc_decode_workspace(2, 14, 2, 64, 128, 64)
+    ws = L.alloc_decode_workspace(2, 14, 2, 64)
     L.paged_decode(out, d["q"], d["k"], d["v"], case.num_blocks, case.num_layers, case.layer, 14,
                    2, 64, d["tables"], to_device(case.ctx), 128, partition_tokens=64, workspace=ws)
     torch.cuda.synchronize()
@@ -111,13 +111,13 @@ def test_decode_positions_mode_and_workspace_reuse():
     row on one workspace give the same result (arrival counters reset)."""
     case = make_case(6, 14, 2, 64, [5, 600, 1024, 1025, 2000, 16], seed=4)
     d = dev_case(case)
-    ws = L.alloc_decode_workspace(6, 14, 2, 64, case.max_ctx, 64)
+    ws = L.alloc_decode_workspace(6, 14, 2, 64)
     a, _ = gpu_decode(case, d=d, partition_tokens=64, len_offset=1, ws=ws)
     a = from_device(a)
     b, _ = gpu_decode(case, d=d, partition_tokens=64, len_offset=1, ws=ws)
     assert np.array_equal(a, from_device(b))
     assert max_err(a, oracle_decode(case)) <= ATTN_ATOL
-    assert not ws[:6 * 14 * 4].any()  # counters back at zero
+    assert not ws[:6 * 2 * 4].any()  # arrival counters (batch x kv heads) back at zero
 
 
 def test_decode_empty_context_gives_zeros():
@@ -151,6 +151,33 @@ def test_decode_context_beyond_table_is_clamped_and_reported():
     out, st = gpu_decode(case, d=d, lens=lens)
     assert st & L.LC_DEV_BAD_POS
     assert max_err(from_device(out), oracle_decode(case)) <= ATTN_ATOL
+
+
+@pytest.mark.parametrize("hq,hkv,hd,batch,lo,hi", [
+    (14, 2, 64, 64, 256, 4096),     # BASELINE config 2 shape
+    (28, 4, 128, 8, 8192, 8192),    # config 3 shape, fewer sequences
+    (14, 2, 64, 3000, 1, 40),       # many short sequences: multi-entry scan slices
+    (64, 8, 128, 16, 1024, 9000),   # config 5 shape, fewer/shorter sequences
+])
+def test_decode_persistent_split_shapes(hq, hkv, hd, batch, lo, hi):
+    rng = np.random.default_rng(batch + hd)
+    ctx = rng.integers(lo, hi + 1, batch).astype(np.int32)
+    ctx[rng.integers(0, batch, max(1, batch // 10))] = 0  # some empty sequences
+    case = make_case(batch, hq, hkv, hd, ctx, seed=batch)
+    out, st = gpu_decode(case)
+    assert st == 0
+    o = from_device(out)
+    assert max_err(o, oracle_decode(case)) <= ATTN_ATOL
+    assert not o[ctx == 0].any()
+
+
+def test_decode_one_sequence_split_over_many_ctas():
+    """C1 shape: one sequence, each segment spread over dozens of CTAs."""
+    case = make_case(1, 14, 2, 64, [1024], seed=12)
+    for ptok in (0, 16, 32):
+        out, st = gpu_decode(case, partition_tokens=ptok)
+        assert st == 0
+        assert max_err(from_device(out), oracle_decode(case)) <= ATTN_ATOL
 
 
 @pytest.mark.parametrize("hd", [64, 128])

@@ -116,7 +116,7 @@ def test_batched_ours_vs_reference_kernels():
                               case.num_layers, case.layer, hq, hkv, hd, p(d_t),
                               case.tables.shape[1], p(d_pos), host_pos, 8, 32768, stream()) == 0
     out = torch.empty(8, hq * hd, dtype=torch.bfloat16, device="cuda")
-    ws = L.alloc_decode_workspace(8, hq, hkv, hd, int(ctx.max()), 512)
+    ws = L.alloc_decode_workspace(8, hq, hkv, hd)
     L.paged_decode(out, d_q, d_k, d_v, case.num_blocks, case.num_layers, case.layer, hq, hkv, hd,
                    d_t, d_pos, int(ctx.max()), len_offset=1, partition_tokens=512, workspace=ws)
     torch.cuda.synchronize()
