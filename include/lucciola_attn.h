@@ -163,6 +163,33 @@ int lc_paged_decode(void *out, int64_t out_stride, const void *q,
                     void *workspace, size_t workspace_bytes, int *dev_status,
                     lc_stream_t stream);
 
+/* Allocation-free variant of lc_paged_decode. No counterpart in the reference.
+ * For callers that cannot allocate device memory while they decode (a serving
+ * loop that must not call cudaMalloc/cudaFree because they may synchronise the
+ * device, or a host whose device memory is all reserved for its own pools):
+ * the split-K scratch is a fixed array of LC_PAGED_DECODE_STATIC_SCRATCH_BYTES
+ * that the library keeps on every GPU it is loaded on, until the process exits.
+ * Same arguments and results as lc_paged_decode, minus the workspace.
+ *   - The first call on a device sets it up (resolves the array's device
+ *     address, sets kernel attributes); make that first call before any CUDA
+ *     stream capture on that device.
+ *   - Returns LC_ERR_WORKSPACE_TOO_SMALL, launching nothing, when the batch
+ *     needs more scratch than the fixed size (lc_paged_decode_workspace_size
+ *     tells how much a shape needs).
+ *   - Every call uses the same array: calls that may run at the same time on
+ *     the GPU (different streams) race; order them on one stream.
+ *   - Allocates nothing: no cudaMalloc/cudaFree, no host allocation. */
+#define LC_PAGED_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
+int lc_paged_decode_static(void *out, int64_t out_stride, const void *q,
+                           int64_t q_stride, const void *k_pool,
+                           const void *v_pool, int64_t num_blocks,
+                           int num_layers, int layer, int num_q_heads,
+                           int num_kv_heads, int head_dim,
+                           const int *block_tables, int table_stride,
+                           const int *context_lens, int len_offset, int batch,
+                           int max_context_len, int partition_tokens,
+                           float sm_scale, int *dev_status, lc_stream_t stream);
+
 /* Causal prefill over the paged pool (tcgen05 tensor-core path). Query token i
  * of sequence b sits at position start_pos[b] + i and attends to cache tokens
  * 0..=start_pos[b]+i of its kv head; the K/V of the prompt must already be in

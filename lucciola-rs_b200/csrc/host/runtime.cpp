@@ -137,3 +137,24 @@ int sm_count() {
 }
 
 }  // namespace lc
+
+namespace lc {
+
+// Same map as pool_tensor_map, encoded on the caller's stack without touching
+// the cache (no host allocation). Used by the allocation-free decode entry.
+int pool_tensor_map_nocache(const void *pool, int64_t rows, int head_dim, CUtensorMap *out) {
+    if (!aligned16(pool)) return LC_ERR_MISALIGNED;
+    if (rows <= 0 || rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
+    auto fn = encode_fn();
+    if (!fn) return LC_ERR_NOT_SUPPORTED;
+    cuuint64_t dims[2] = {(cuuint64_t)head_dim, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)head_dim * 2};
+    cuuint32_t box[2] = {64, 16};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(pool), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? LC_OK : LC_ERR_CUDA;
+}
+
+}  // namespace lc

@@ -25,6 +25,9 @@ inline int launch_status() {
 // range), LC_ERR_MISALIGNED or LC_ERR_CUDA.
 int pool_tensor_map(const void *pool, int64_t rows, int head_dim, CUtensorMap *out);
 
+// The same map encoded without the cache (no host allocation).
+int pool_tensor_map_nocache(const void *pool, int64_t rows, int head_dim, CUtensorMap *out);
+
 // Applies cudaFuncAttributeMaxDynamicSharedMemorySize once per (function, device).
 int ensure_smem_attr(const void *func, int bytes);
 

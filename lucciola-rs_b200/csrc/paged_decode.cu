@@ -32,6 +32,7 @@
 // tokens 0..n-1, fp32 accumulation, bf16 output. Block-table entries outside
 // the pool are reported in the status word and read as zeros (TMA bounds fill).
 #include <climits>
+#include <mutex>
 
 #include "lc_common.cuh"
 #include "lc_host.h"
@@ -776,4 +777,179 @@ extern "C" int lc_flash_decoding(void *output, const void *q, const void *k_pool
                            block_table, table_len, current_pos, /*len_offset=*/1, 1,
                            host_pos + 1, 0, sm_scale, workspace, workspace_bytes, nullptr,
                            stream);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point: lc_paged_decode_static.
+//
+// lc_paged_decode needs a caller-allocated workspace. Some callers cannot
+// allocate device memory when they decode: a serving loop that must never hit
+// cudaMalloc/cudaFree (they can synchronise the whole device and stall every
+// other stream mid-step), a host engine whose device memory is entirely
+// reserved up front for its own KV pools and buffers, or an embedding runtime
+// that only hands the attention plugin raw tensor pointers and a stream. For
+// them the split-K scratch lives in the fixed device array below, which every
+// GPU that loads this library holds (LC_PAGED_DECODE_STATIC_SCRATCH_BYTES) until
+// the process exits.
+//
+// Host code cannot use the array's name as a device address (it names a host
+// shadow); the first call on each device resolves the real address with
+// cudaGetSymbolAddress while that device is current and caches it. Calls share
+// the array and it keeps the last call's contents: each call clears the
+// arrival counters it needs, and calls that overlap on the same GPU (issued on
+// two streams, say) race on it. Each device has its own copy of the array.
+static __device__ __align__(256) unsigned char
+    lc_static_decode_scratch[LC_PAGED_DECODE_STATIC_SCRATCH_BYTES];
+
+namespace lc {
+namespace {
+
+constexpr int kStaticMaxDevices = 64;
+
+struct StaticDecodeSetup {
+    void *scratch;
+    int max_ctas64, max_ctas128;
+    bool ready;
+};
+StaticDecodeSetup g_static_setup[kStaticMaxDevices];
+std::mutex g_static_mu;
+
+template <int HD>
+int static_max_ctas(int sms, int *out) {
+    const int smem = DecodeCfg<HD>::kSmemBytes;
+    int per_sm = 0;
+    if (cudaFuncSetAttribute(paged_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<HD>, kThreads,
+                                                      smem) != cudaSuccess ||
+        per_sm < 1) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    *out = per_sm * sms;
+    return LC_OK;
+}
+
+// One-time set-up of the current device `dev` (must be current).
+int static_decode_setup(int dev, const StaticDecodeSetup **out) {
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    StaticDecodeSetup &s = g_static_setup[dev];
+    if (!s.ready) {
+        void *ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, lc_static_decode_scratch) != cudaSuccess || !ptr) {
+            cudaGetLastError();
+            return LC_ERR_CUDA;
+        }
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            sms <= 0) {
+            cudaGetLastError();
+            return LC_ERR_CUDA;
+        }
+        int rc = static_max_ctas<64>(sms, &s.max_ctas64);
+        if (!rc) rc = static_max_ctas<128>(sms, &s.max_ctas128);
+        if (rc) return rc;
+        s.scratch = ptr;
+        s.ready = true;
+    }
+    *out = &s;
+    return LC_OK;
+}
+
+template <int HD>
+int launch_decode_static(const DecodeParams &prm, int grid, const void *k_pool,
+                         const void *v_pool, cudaStream_t stream) {
+    CUtensorMap mk, mv;
+    int rc = pool_tensor_map_nocache(k_pool, prm.pool_rows, HD, &mk);
+    if (rc) return rc;
+    rc = pool_tensor_map_nocache(v_pool, prm.pool_rows, HD, &mv);
+    if (rc) return rc;
+    paged_decode_kernel<HD><<<grid, kThreads, DecodeCfg<HD>::kSmemBytes, stream>>>(mk, mv, prm);
+    return launch_status();
+}
+
+}  // namespace
+}  // namespace lc
+
+extern "C" int lc_paged_decode_static(void *out, int64_t out_stride, const void *q,
+                                      int64_t q_stride, const void *k_pool, const void *v_pool,
+                                      int64_t num_blocks, int num_layers, int layer,
+                                      int num_q_heads, int num_kv_heads, int head_dim,
+                                      const int *block_tables, int table_stride,
+                                      const int *context_lens, int len_offset, int batch,
+                                      int max_context_len, int partition_tokens, float sm_scale,
+                                      int *dev_status, lc_stream_t stream) {
+    if (!out || !q || !k_pool || !v_pool || !block_tables || !context_lens)
+        return LC_ERR_INVALID_ARGUMENT;
+    if (head_dim != 64 && head_dim != 128) return LC_ERR_UNSUPPORTED_HEAD_DIM;
+    if (batch < 0 || num_layers <= 0 || layer < 0 || layer >= num_layers || num_q_heads <= 0 ||
+        num_kv_heads <= 0 || num_blocks <= 0 || table_stride <= 0 || len_offset < 0 ||
+        len_offset > 1 || partition_tokens < 0)
+        return LC_ERR_INVALID_ARGUMENT;
+    if (num_q_heads % num_kv_heads) return LC_ERR_UNSUPPORTED_SHAPE;
+    if (batch == 0) return LC_OK;
+    if (!aligned16(k_pool) || !aligned16(v_pool) || !aligned16(q) || (q_stride & 7) ||
+        ((uintptr_t)out & 1))
+        return LC_ERR_MISALIGNED;
+    if (q_stride < (int64_t)num_q_heads * head_dim || out_stride < (int64_t)num_q_heads * head_dim)
+        return LC_ERR_INVALID_ARGUMENT;
+    const int64_t pool_rows = num_blocks * num_layers * num_kv_heads * kBlockSize;
+    if (pool_rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kStaticMaxDevices) return LC_ERR_NOT_SUPPORTED;
+    const StaticDecodeSetup *setup = nullptr;
+    int rc = static_decode_setup(dev, &setup);
+    if (rc) return rc;
+
+    const int G = segments_per_seq(num_q_heads, num_kv_heads);
+    const int cmax = head_dim == 64 ? setup->max_ctas64 : setup->max_ctas128;
+    const WsLayout wl = ws_layout(batch, G, head_dim, cmax);
+    if (wl.total() > (size_t)LC_PAGED_DECODE_STATIC_SCRATCH_BYTES)
+        return LC_ERR_WORKSPACE_TOO_SMALL;  // batch too large for the fixed scratch
+    cudaStream_t s = as_stream(stream);
+    // The arrival counters must start at zero; the partials need no clearing.
+    if (cudaMemsetAsync(setup->scratch, 0, wl.cnt_bytes, s) != cudaSuccess) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    int grid = cmax;
+    if (max_context_len > 0) {
+        const long long pages_hint =
+            (long long)batch * G * ((max_context_len + kBlockSize - 1) / kBlockSize);
+        const long long want = (pages_hint + 1) / 2;
+        if (want < grid) grid = (int)(want < 1 ? 1 : want);
+    }
+    DecodeParams prm{};
+    prm.out = (bf16 *)out;
+    prm.out_stride = out_stride;
+    prm.q = (const bf16 *)q;
+    prm.q_stride = q_stride;
+    prm.tables = block_tables;
+    prm.table_stride = table_stride;
+    prm.ctx_lens = context_lens;
+    prm.len_offset = len_offset;
+    prm.batch = batch;
+    prm.pool_rows = pool_rows;
+    prm.num_blocks = num_blocks;
+    prm.num_layers = num_layers;
+    prm.layer = layer;
+    prm.num_q_heads = num_q_heads;
+    prm.num_kv_heads = num_kv_heads;
+    prm.group = num_q_heads / num_kv_heads;
+    prm.ctas_per_kv = (prm.group + kHeadsPerCta - 1) / kHeadsPerCta;
+    prm.seg_per_seq = G;
+    prm.partition_tokens = partition_tokens;
+    prm.scale_log2 = sm_scale * 1.4426950408889634f;
+    uint8_t *ws = (uint8_t *)setup->scratch;
+    prm.ws_cnt = (int *)ws;
+    prm.ws_lse = (float *)(ws + wl.cnt_bytes);
+    prm.ws_o = (float *)(ws + wl.cnt_bytes + wl.lse_bytes);
+    prm.status = dev_status;
+    return head_dim == 64 ? launch_decode_static<64>(prm, grid, k_pool, v_pool, s)
+                          : launch_decode_static<128>(prm, grid, k_pool, v_pool, s);
 }

@@ -41,6 +41,9 @@ SIGNATURES = {
     "lc_paged_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _sz,
                                _vp, _vp]),
+    "lc_paged_decode_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
+                                      _i32, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32,
+                                      _vp, _vp]),
     "lc_paged_prefill": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                 _i32, _vp, _i32, _vp, _i32, _i32, _i32, _f32, _vp, _vp]),
     "lc_gather_kv": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp,
@@ -175,6 +178,22 @@ def paged_decode(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_he
                               _p(workspace),
                               0 if workspace is None else workspace.numel() * workspace.element_size(),
                               _p(dev_status), _stream(stream)), "lc_paged_decode")
+
+
+def paged_decode_static(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_heads,
+                        num_kv_heads, head_dim, block_tables, context_lens, max_context_len=0,
+                        sm_scale=None, len_offset=0, partition_tokens=0, dev_status=None,
+                        stream=None):
+    """lc_paged_decode without a workspace: the library's fixed device scratch."""
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(head_dim)
+    batch = context_lens.shape[0]
+    check(lib.lc_paged_decode_static(_p(out), out.stride(0), _p(q), q.stride(0), _p(k_pool),
+                                     _p(v_pool), num_blocks, num_layers, layer, num_q_heads,
+                                     num_kv_heads, head_dim, _p(block_tables),
+                                     block_tables.stride(0), _p(context_lens), len_offset, batch,
+                                     max_context_len, partition_tokens, sm_scale, _p(dev_status),
+                                     _stream(stream)), "lc_paged_decode_static")
 
 
 def paged_prefill(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_heads,
