@@ -197,21 +197,34 @@ class Workload:
 # ------------------------------------------------------------------ our arm --
 
 class OursStep:
-    def __init__(self, w: Workload):
+    """One decode step: per layer the fused bias+RoPE+append+attention launch
+    (lc_rope_append_decode), or with fused=False the two-launch form
+    (lc_rope_append, then lc_paged_decode)."""
+
+    def __init__(self, w: Workload, fused: bool = True):
         import lucciola as L
         self.L = L
         self.w = w
+        self.fused = fused
         self.ws = L.alloc_decode_workspace(w.batch, w.hq, w.hkv, w.hd, device=w.device)
 
     def layer(self, l, decode_events=None):
         w, L = self.w, self.L
-        L.rope_append(w.qkv[l], w.positions, w.q_bias[l], w.k_bias[l], w.v_bias[l], w.cos, w.sin,
-                      w.k_pool, w.v_pool, w.num_blocks, w.layers, l, w.hq, w.hkv, w.hd, w.tables)
+        if not self.fused:
+            L.rope_append(w.qkv[l], w.positions, w.q_bias[l], w.k_bias[l], w.v_bias[l], w.cos,
+                          w.sin, w.k_pool, w.v_pool, w.num_blocks, w.layers, l, w.hq, w.hkv,
+                          w.hd, w.tables)
         if decode_events is not None:
             decode_events[0].record()
-        L.paged_decode(w.out[l], w.qkv[l], w.k_pool, w.v_pool, w.num_blocks, w.layers, l, w.hq,
-                       w.hkv, w.hd, w.tables, w.positions, w.max_ctx, len_offset=1,
-                       partition_tokens=w.ptok, workspace=self.ws)
+        if self.fused:
+            L.rope_append_decode(w.out[l], w.qkv[l], w.positions, w.q_bias[l], w.k_bias[l],
+                                 w.v_bias[l], w.cos, w.sin, w.k_pool, w.v_pool, w.num_blocks,
+                                 w.layers, l, w.hq, w.hkv, w.hd, w.tables, w.max_ctx,
+                                 partition_tokens=w.ptok, workspace=self.ws)
+        else:
+            L.paged_decode(w.out[l], w.qkv[l], w.k_pool, w.v_pool, w.num_blocks, w.layers, l,
+                           w.hq, w.hkv, w.hd, w.tables, w.positions, w.max_ctx, len_offset=1,
+                           partition_tokens=w.ptok, workspace=self.ws)
         if decode_events is not None:
             decode_events[1].record()
 
@@ -219,7 +232,7 @@ class OursStep:
         for l in range(self.w.layers):
             self.layer(l)
 
-    launches_per_step = property(lambda self: 2 * self.w.layers)
+    launches_per_step = property(lambda self: (1 if self.fused else 2) * self.w.layers)
 
 
 def time_graph(graph, steps, warmup, stream):
@@ -304,7 +317,7 @@ def run_ours(args, rank, world, local):
     w = Workload(args.config, rank, world, device)
     if args.partition is not None:
         w.ptok = args.partition
-    runner = OursStep(w)
+    runner = OursStep(w, fused=not args.unfused)
     if args.mode == "kernel":
         # Plain eager launches, nothing else: the command profiled by ncu.
         for _ in range(args.warmup + args.steps):
@@ -409,13 +422,16 @@ def run_ours(args, rank, world, local):
                        "parallelism": f"sequence-sharded x{world}",
                        "l2": "no flush: 24 per-layer caches, ~%.1f GB per GPU > 126 MB L2" %
                              (w.kv_bytes_per_step / 1e9),
-                       "step": "per layer: lc_rope_append + lc_paged_decode; CUDA graph"},
+                       "step": ("per layer: lc_rope_append + lc_paged_decode" if args.unfused else
+                                "per layer: lc_rope_append_decode (fused bias+RoPE+append+"
+                                "attention)") + "; CUDA graph"},
             "tokens_per_s": round(w.global_batch / (ms_step * 1e-3), 1),
             "pct_hbm": round(100 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": TRAFFIC.get(args.config),
-                         "kernel": "paged_decode_kernel", "peak_kind": f"{peak_kind} (burst copy)",
+                         "kernel": "paged_decode_kernel<%d,%s>" % (w.hd, "fused" if runner.fused else "plain"),
+                         "peak_kind": f"{peak_kind} (burst copy)",
                          "launch_ms": round(dec_ms, 5)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(w.h2d_bytes), "d2h_bytes_per_step": int(w.d2h_bytes),
@@ -540,6 +556,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
                     help="kernel: eager launches only (for profilers), no JSON metrics")
+    ap.add_argument("--unfused", action="store_true",
+                    help="two launches per layer (lc_rope_append, lc_paged_decode)")
     ap.add_argument("--partition", type=int, default=None,
                     help="override the split-K partition size in tokens (0 = auto)")
     args = ap.parse_args()

@@ -163,6 +163,30 @@ int lc_paged_decode(void *out, int64_t out_stride, const void *q,
                     void *workspace, size_t workspace_bytes, int *dev_status,
                     lc_stream_t stream);
 
+/* Fused decode step for a batch: lc_rope_append with one
+ * row per sequence followed by lc_paged_decode with len_offset = 1, in ONE
+ * launch. For sequence b the new token sits at position positions[b]; its q
+ * and k are biased and rotated, its k and v + v_bias are appended to the pools
+ * at that position, and the attention covers positions 0..positions[b]
+ * inclusive. qkv rows are [q | k | v] (`row_stride` bf16 apart) and are only
+ * read: unlike rope (src/kernels/rope.cu:37-53) the rotated q/k are not written
+ * back, a side effect nothing after the attention reads (o_proj consumes the
+ * attention output, src/models.rs:553-566). Pool writes are bit-identical to
+ * lc_rope_append; the output is that of lc_paged_decode. Workspace as for
+ * lc_paged_decode (lc_paged_decode_workspace_size). */
+int lc_rope_append_decode(void *out, int64_t out_stride, const void *qkv,
+                          int64_t row_stride, const int *positions,
+                          const void *q_bias, const void *k_bias,
+                          const void *v_bias, const float *cos_cache,
+                          const float *sin_cache, int rope_rows, void *k_pool,
+                          void *v_pool, int64_t num_blocks, int num_layers,
+                          int layer, int num_q_heads, int num_kv_heads,
+                          int head_dim, const int *block_tables,
+                          int table_stride, int batch, int max_context_len,
+                          int partition_tokens, float sm_scale, void *workspace,
+                          size_t workspace_bytes, int *dev_status,
+                          lc_stream_t stream);
+
 /* Allocation-free variant of lc_paged_decode. No counterpart in the reference.
  * For callers that cannot allocate device memory while they decode (a serving
  * loop that must not call cudaMalloc/cudaFree because they may synchronise the

@@ -36,12 +36,15 @@
 
 #include "lc_common.cuh"
 #include "lc_host.h"
+#include "rope_math.cuh"
 
 namespace lc {
 namespace {
 
 constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kProducerWarp = kConsumerWarps;      // warp 4
+constexpr int kEpilogueWarp = kConsumerWarps + 1;  // warp 5
+constexpr int kThreads = (kConsumerWarps + 2) * 32;
 constexpr int kHeadsPerCta = 8;
 constexpr int kPagesPerStage = kConsumerWarps;  // one page per consumer warp per stage
 
@@ -51,7 +54,14 @@ struct StageMeta {
     int b, g, page0, np;    // sequence, segment-in-sequence, first page of the stage, pages
     int n, pages_b, flags;  // tokens of the sequence, its pages, kFirst/kLast/kDone
     int chunk_p0, take;     // chunk = pages [chunk_p0, chunk_p0 + take) of the segment
+    int pos;                // fused: the new token's position (unclamped)
     long long seg_start;    // global index of the segment's first page
+};
+
+// Finished chunk handed from the consumer warps to the epilogue warp.
+struct EpiInfo {
+    int b, seg, nh, head0, pages_b, whole, done;
+    long long seg_start;
 };
 
 template <int HD>
@@ -86,18 +96,142 @@ struct DecodeParams {
     float *ws_lse;     // [slots][8]
     int *ws_cnt;       // [batch * seg_per_seq]
     int *status;
+    // Fused bias + RoPE + append (FUSED kernels only). q/q_stride then address
+    // qkv rows [q | k | v]; context_lens holds the new token's position.
+    const bf16 *qkv;
+    const bf16 *q_bias, *k_bias, *v_bias;
+    const float *cos_t, *sin_t;
+    int rope_rows;
+    bf16 *k_pool_w, *v_pool_w;
+};
+
+// Shared-memory byte address of 16-byte chunk `kc` (of hd/8) of token row `r` in a
+// page tile stored as hd/64 boxes of [16 rows][128 B] with 128-byte swizzle.
+__device__ __forceinline__ uint32_t tile_addr(uint32_t page, int r, int kc) {
+    return page + ((kc >> 3) << 11) + (r << 7) + ((((kc & 7) ^ (r & 7))) << 4);
+}
+
+// Fused mode, consumer warp: the B fragments of Q^T for this lane's query head,
+// biased and rotated (rope_math.cuh, the arithmetic of rope_append.cu) straight
+// from the qkv row. A lane's fragments hold dims {16j + 2c, +1, +8, +9} of every
+// 16-dim step j, so the rotation partners d and d + hd/2 (same residue mod 16)
+// are both in the lane: no data moves between lanes.
+template <int HD>
+__device__ __forceinline__ void rope_q_fragments(const DecodeParams &p, int b, int head, bool hv,
+                                                 int pos, int c4, uint32_t (&qf)[HD / 16][2]) {
+    constexpr int half = HD / 2, KH = HD / 32;  // fragment steps per half
+    if (!hv) {
+#pragma unroll
+        for (int j = 0; j < HD / 16; ++j) qf[j][0] = qf[j][1] = 0u;
+        return;
+    }
+    const bf16 *row = p.qkv + (int64_t)b * p.q_stride + (int64_t)head * HD;
+    const bf16 *bias = p.q_bias + (int64_t)head * HD;
+    const bool pos_ok = pos >= 0 && pos < p.rope_rows;
+    const float *ct = p.cos_t + (int64_t)(pos_ok ? pos : 0) * half;
+    const float *st = p.sin_t + (int64_t)(pos_ok ? pos : 0) * half;
+#pragma unroll
+    for (int j = 0; j < KH; ++j) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int d = 16 * j + 8 * r + 2 * c4;  // this lane's pair (d, d+1), d < half
+            const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162 *>(row + d);
+            const __nv_bfloat162 x2 = *reinterpret_cast<const __nv_bfloat162 *>(row + d + half);
+            const __nv_bfloat162 b1 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d));
+            const __nv_bfloat162 b2 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d + half));
+            const float2 c = pos_ok ? __ldg(reinterpret_cast<const float2 *>(ct + d)) : make_float2(1.f, 1.f);
+            const float2 sn = pos_ok ? __ldg(reinterpret_cast<const float2 *>(st + d)) : make_float2(0.f, 0.f);
+            const float a0 = __fadd_rn(__low2float(x1), __low2float(b1));
+            const float a1 = __fadd_rn(__high2float(x1), __high2float(b1));
+            const float e0 = __fadd_rn(__low2float(x2), __low2float(b2));
+            const float e1 = __fadd_rn(__high2float(x2), __high2float(b2));
+            const __nv_bfloat162 lo =
+                __halves2bfloat162(__float2bfloat16(rot_sub(a0, c.x, e0, sn.x)),
+                                   __float2bfloat16(rot_sub(a1, c.y, e1, sn.y)));
+            const __nv_bfloat162 hi =
+                __halves2bfloat162(__float2bfloat16(rot_add(a0, sn.x, e0, c.x)),
+                                   __float2bfloat16(rot_add(a1, sn.y, e1, c.y)));
+            qf[j][r] = *reinterpret_cast<const uint32_t *>(&lo);
+            qf[j + KH][r] = *reinterpret_cast<const uint32_t *>(&hi);
+        }
+    }
+}
+
+// Fused mode: raw inputs of the new token's K/V row for one kv head, loaded by
+// the consumer warp that will process its page well before it is needed.
+template <int HD>
+struct NewKvInputs {
+    static constexpr int kPairs = HD / 64;  // rotation pairs per lane
+    __nv_bfloat16 k1[kPairs], k2[kPairs], v1[kPairs], v2[kPairs];
+    __nv_bfloat16 kb1[kPairs], kb2[kPairs], vb1[kPairs], vb2[kPairs];
+    float c[kPairs], s[kPairs];
+    int phys;
+
+    __device__ __forceinline__ void load(const DecodeParams &p, int b, int kvh, int pos,
+                                         int page, int lane) {
+        constexpr int half = HD / 2;
+        const bf16 *row = p.qkv + (int64_t)b * p.q_stride;
+        const int ko = p.num_q_heads * HD + kvh * HD, vo = ko + p.num_kv_heads * HD;
+        const bool pos_ok = pos < p.rope_rows;
+#pragma unroll
+        for (int i = 0; i < kPairs; ++i) {
+            const int d = lane + 32 * i;
+            k1[i] = row[ko + d];
+            k2[i] = row[ko + d + half];
+            v1[i] = row[vo + d];
+            v2[i] = row[vo + d + half];
+            kb1[i] = p.k_bias[kvh * HD + d];
+            kb2[i] = p.k_bias[kvh * HD + d + half];
+            vb1[i] = p.v_bias[kvh * HD + d];
+            vb2[i] = p.v_bias[kvh * HD + d + half];
+            c[i] = pos_ok ? __ldg(p.cos_t + (int64_t)pos * half + d) : 1.f;
+            s[i] = pos_ok ? __ldg(p.sin_t + (int64_t)pos * half + d) : 0.f;
+        }
+        phys = __ldg(p.tables + (int64_t)b * p.table_stride + page);
+    }
+
+    // Rotated k and v + bias (the arithmetic of rope_append.cu): patched into
+    // row `r` of the page tiles in shared memory and, when `append`, written to
+    // the pools at position `pos`.
+    __device__ __forceinline__ void apply(const DecodeParams &p, int kvh, int pos, bool append,
+                                          uint8_t *smem_gen, uint32_t smem_base, uint32_t kpage,
+                                          uint32_t vpage, int r, int lane) {
+        constexpr int half = HD / 2;
+        const bool ph_ok = phys >= 0 && phys < p.num_blocks;
+        const int64_t dst = page_row(ph_ok ? phys : 0, p.layer, kvh, p.num_layers,
+                                     p.num_kv_heads) * HD + (int64_t)(pos % kBlockSize) * HD;
+#pragma unroll
+        for (int i = 0; i < kPairs; ++i) {
+            const int d = lane + 32 * i;
+            const float a1 = __fadd_rn(__bfloat162float(k1[i]), __bfloat162float(kb1[i]));
+            const float a2 = __fadd_rn(__bfloat162float(k2[i]), __bfloat162float(kb2[i]));
+            const bf16 rk1 = __float2bfloat16(rot_sub(a1, c[i], a2, s[i]));
+            const bf16 rk2 = __float2bfloat16(rot_add(a1, s[i], a2, c[i]));
+            const bf16 rv1 = __float2bfloat16(__fadd_rn(__bfloat162float(v1[i]), __bfloat162float(vb1[i])));
+            const bf16 rv2 = __float2bfloat16(__fadd_rn(__bfloat162float(v2[i]), __bfloat162float(vb2[i])));
+            // element d of row r sits in 16-byte chunk d/8 of the swizzled tile
+            auto put = [&](uint32_t tile, int dd, bf16 v) {
+                *reinterpret_cast<bf16 *>(smem_gen + (tile_addr(tile, r, dd >> 3) - smem_base) +
+                                          (dd & 7) * 2) = v;
+            };
+            put(kpage, d, rk1);
+            put(kpage, d + half, rk2);
+            put(vpage, d, rv1);
+            put(vpage, d + half, rv2);
+            if (append && ph_ok) {
+                p.k_pool_w[dst + d] = rk1;
+                p.k_pool_w[dst + d + half] = rk2;
+                p.v_pool_w[dst + d] = rv1;
+                p.v_pool_w[dst + d + half] = rv2;
+            }
+        }
+    }
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// Shared-memory byte address of 16-byte chunk `kc` (of hd/8) of token row `r` in a
-// page tile stored as hd/64 boxes of [16 rows][128 B] with 128-byte swizzle.
-__device__ __forceinline__ uint32_t tile_addr(uint32_t page, int r, int kc) {
-    return page + ((kc >> 3) << 11) + (r << 7) + ((((kc & 7) ^ (r & 7))) << 4);
 }
 
 __device__ __forceinline__ int seq_tokens(const DecodeParams &p, int b, bool report) {
@@ -187,8 +321,8 @@ __device__ __forceinline__ void state_combine(WarpState<HD> &st, const float *re
         }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kThreads)
+template <int HD, bool FUSED>
+__global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
     using Cfg = DecodeCfg<HD>;
@@ -196,9 +330,11 @@ __global__ void __launch_bounds__(kThreads)
 
     __shared__ __align__(8) uint64_t full_bar[Cfg::kStages];
     __shared__ __align__(8) uint64_t empty_bar[Cfg::kStages];
-    __shared__ __align__(8) uint64_t fin_bar;  // consumer-warp sync (bounded)
+    __shared__ __align__(8) uint64_t fin_bar;    // consumer-warp sync (bounded)
+    __shared__ __align__(8) uint64_t epi_full;   // consumers -> epilogue: slots hold a chunk
+    __shared__ __align__(8) uint64_t epi_empty;  // epilogue -> consumers: slots free again
     __shared__ StageMeta meta[Cfg::kStages];
-    __shared__ long long s_part[kThreads];
+    __shared__ EpiInfo epi;
     __shared__ long long s_total;
     __shared__ int s_b0;
     __shared__ long long s_pref_b0;
@@ -208,6 +344,10 @@ __global__ void __launch_bounds__(kThreads)
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int G = p.seg_per_seq;
+    const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    uint8_t *smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
+    // Set-up scan scratch: the head of the stage ring, free until the first TMA.
+    long long *s_part = reinterpret_cast<long long *>(smem_gen);
 
     // ---- 1. total pages T and empty-sequence outputs ------------------------
     const int per = (p.batch + kThreads - 1) / kThreads;
@@ -278,20 +418,22 @@ __global__ void __launch_bounds__(kThreads)
             }
         }
     }
-    const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
-    uint8_t *smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
+    // Order the scan's generic accesses to the ring before the TMA writes to it.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (tid == 0) {
         for (int s = 0; s < Cfg::kStages; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], kConsumerWarps);
         }
         mbar_init(&fin_bar, kConsumerWarps * 32);
+        mbar_init(&epi_full, 2);
+        mbar_init(&epi_empty, 1);
         s_abort = 0;
         fence_barrier_init();
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
+    if (warp == kProducerWarp) {
         // ------------------------------------------------------ producer --
         if (lane == 0) {
             prefetch_tensormap(&tmap_k);
@@ -329,55 +471,58 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
                     for (int k = 0; k < kPagesPerStage; ++k)
                         phys[k] = __shfl_sync(0xffffffffu, entry, (j + k) & 31);
+                    const int s = it % Cfg::kStages;
+                    const bool first = base == 0 && j == 0;
+                    if (lane == 0 && it >= Cfg::kStages &&
+                        !mbar_wait_bounded(&empty_bar[s], ((it / Cfg::kStages) - 1) & 1, &s_abort,
+                                           p.status))
+                        ok = false;
+                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (!ok) break;
+                    uint32_t qbytes = 0;
                     if (lane == 0) {
-                        const int s = it % Cfg::kStages;
-                        if (it >= Cfg::kStages &&
-                            !mbar_wait_bounded(&empty_bar[s], ((it / Cfg::kStages) - 1) & 1,
-                                               &s_abort, p.status)) {
-                            ok = false;
-                        } else {
-                            const bool first = base == 0 && j == 0;
-                            StageMeta &m = meta[s];
-                            m.b = b;
-                            m.g = g;
-                            m.page0 = pg + base + j;
-                            m.np = np;
-                            m.n = n;
-                            m.pages_b = pages_b;
-                            m.flags = (first ? kFirst : 0) | (base + j + np == take ? kLast : 0);
-                            m.chunk_p0 = pg;
-                            m.take = take;
-                            m.seg_start = seg_start;
-                            const uint32_t qbytes = first ? (uint32_t)(nh * HD * 2) : 0u;
-                            mbar_arrive_expect_tx(&full_bar[s],
-                                                  (uint32_t)(np * 2 * Cfg::kPageBytes) + qbytes);
-                            if (first)
-                                bulk_load(smem_gen + Cfg::kQOffset + s * Cfg::kQBytes,
-                                          p.q + (int64_t)b * p.q_stride + (int64_t)head0 * HD,
-                                          qbytes, &full_bar[s]);
-                            uint8_t *kst = smem_gen + s * Cfg::kStageBytes;
-                            for (int k = 0; k < np; ++k) {
-                                int64_t row;
-                                if (phys[k] < 0 || phys[k] >= p.num_blocks) {
-                                    set_status(p.status, LC_DEV_BAD_BLOCK);
-                                    row = p.pool_rows;  // wholly out of bounds: zero fill
-                                } else {
-                                    row = page_row(phys[k], p.layer, kvh, p.num_layers,
-                                                   p.num_kv_heads);
-                                }
-                                uint8_t *kd = kst + k * Cfg::kPageBytes;
-                                uint8_t *vd = kd + kPagesPerStage * Cfg::kPageBytes;
+                        if (!FUSED && first) {
+                            qbytes = (uint32_t)(nh * HD * 2);
+                            bulk_load(smem_gen + Cfg::kQOffset + s * Cfg::kQBytes,
+                                      p.q + (int64_t)b * p.q_stride + (int64_t)head0 * HD, qbytes,
+                                      &full_bar[s]);
+                        }
+                        uint8_t *kst = smem_gen + s * Cfg::kStageBytes;
+                        for (int k = 0; k < np; ++k) {
+                            int64_t row;
+                            if (phys[k] < 0 || phys[k] >= p.num_blocks) {
+                                set_status(p.status, LC_DEV_BAD_BLOCK);
+                                row = p.pool_rows;  // wholly out of bounds: zero fill
+                            } else {
+                                row = page_row(phys[k], p.layer, kvh, p.num_layers, p.num_kv_heads);
+                            }
+                            uint8_t *kd = kst + k * Cfg::kPageBytes;
+                            uint8_t *vd = kd + kPagesPerStage * Cfg::kPageBytes;
 #pragma unroll
-                                for (int h = 0; h < HD / 64; ++h) {
-                                    tma_load_2d(kd + h * 2048, &tmap_k, h * 64, (int)row,
-                                                &full_bar[s]);
-                                    tma_load_2d(vd + h * 2048, &tmap_v, h * 64, (int)row,
-                                                &full_bar[s]);
-                                }
+                            for (int h = 0; h < HD / 64; ++h) {
+                                tma_load_2d(kd + h * 2048, &tmap_k, h * 64, (int)row, &full_bar[s]);
+                                tma_load_2d(vd + h * 2048, &tmap_v, h * 64, (int)row, &full_bar[s]);
                             }
                         }
                     }
-                    ok = __shfl_sync(0xffffffffu, ok, 0);
+                    if (lane == 0) {
+                        StageMeta &m = meta[s];
+                        m.b = b;
+                        m.g = g;
+                        m.page0 = pg + base + j;
+                        m.np = np;
+                        m.n = n;
+                        m.pages_b = pages_b;
+                        m.flags = (first ? kFirst : 0) | (base + j + np == take ? kLast : 0);
+                        m.chunk_p0 = pg;
+                        m.take = take;
+                        m.pos = FUSED ? __ldg(p.ctx_lens + b) + p.len_offset - 1 : -1;
+                        m.seg_start = seg_start;
+                        // Copies may have landed already: the transaction count of a
+                        // phase may run below zero until this arrival states it.
+                        mbar_arrive_expect_tx(&full_bar[s],
+                                              (uint32_t)(np * 2 * Cfg::kPageBytes) + qbytes);
+                    }
                     ++it;
                 }
             }
@@ -408,33 +553,175 @@ __global__ void __launch_bounds__(kThreads)
         return;
     }
 
+    float *red = reinterpret_cast<float *>(smem_gen + Cfg::kRedOffset);
+    constexpr int kRedFloats = Cfg::kRedFloats;
+
+    if (warp == kEpilogueWarp) {
+        // ------------------------------------------------------ epilogue --
+        // Combines the two half-CTA states of a finished chunk, then writes the
+        // bf16 output (whole segment) or a partial plus, for the last chunk of a
+        // split segment to arrive, the log-sum-exp merge of all its partials.
+        constexpr int KD = HD / 32;  // head dims per lane
+        for (int k = 0;; ++k) {
+            if (!mbar_wait_bounded(&epi_full, k & 1, &s_abort, p.status)) break;
+            const EpiInfo e = epi;
+            if (e.done) break;
+            float O[kHeadsPerCta][KD], Mh[kHeadsPerCta], Lh[kHeadsPerCta];
+            const float *r0 = red, *r1 = red + kRedFloats;
+#pragma unroll
+            for (int h = 0; h < kHeadsPerCta; ++h) {
+                const float m0 = r0[kHeadsPerCta * HD + h], m1 = r1[kHeadsPerCta * HD + h];
+                const float l0 = r0[kHeadsPerCta * HD + kHeadsPerCta + h];
+                const float l1 = r1[kHeadsPerCta * HD + kHeadsPerCta + h];
+                const float M = fmaxf(m0, m1);
+                const float u = M == -INFINITY ? 0.f : M;
+                const float e0 = fast_exp2(m0 - u), e1 = fast_exp2(m1 - u);
+                Mh[h] = M;
+                Lh[h] = l0 * e0 + l1 * e1;
+#pragma unroll
+                for (int kk = 0; kk < KD; ++kk)
+                    O[h][kk] = r0[h * HD + kk * 32 + lane] * e0 + r1[h * HD + kk * 32 + lane] * e1;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&epi_empty);  // the slots are free again
+            if (e.whole) {
+                bf16 *orow = p.out + (int64_t)e.b * p.out_stride + (int64_t)e.head0 * HD;
+#pragma unroll
+                for (int h = 0; h < kHeadsPerCta; ++h) {
+                    if (h >= e.nh) break;
+                    const float il = 1.f / Lh[h];
+#pragma unroll
+                    for (int kk = 0; kk < KD; ++kk)
+                        orow[h * HD + kk * 32 + lane] = __float2bfloat16(O[h][kk] * il);
+                }
+                continue;
+            }
+            // Partial of a split segment: slot = segment + this CTA.
+            const long long slot = (long long)e.seg + cta;
+            float *wo = p.ws_o + slot * kHeadsPerCta * HD;
+#pragma unroll
+            for (int h = 0; h < kHeadsPerCta; ++h) {
+                const float il = 1.f / Lh[h];
+#pragma unroll
+                for (int kk = 0; kk < KD; ++kk) wo[h * HD + kk * 32 + lane] = O[h][kk] * il;
+                if (lane == h) p.ws_lse[slot * kHeadsPerCta + h] = Mh[h] + __log2f(Lh[h]);
+            }
+            __threadfence();
+            __syncwarp();
+            const int c_first = owner_cta(e.seg_start, T, C);
+            const int nch = owner_cta(e.seg_start + e.pages_b - 1, T, C) - c_first + 1;
+            int last = 0;
+            if (lane == 0) last = atomicAdd(p.ws_cnt + e.seg, 1) == nch - 1;
+            if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+            __threadfence();
+            // Merge: weights 2^(lse_j - max_j lse_j) per head, loads in parallel.
+            const long long slot0 = (long long)e.seg + c_first;
+            float Mx[kHeadsPerCta];
+#pragma unroll
+            for (int h = 0; h < kHeadsPerCta; ++h) Mx[h] = -INFINITY;
+            for (int jb = 0; jb < nch; jb += 32) {
+                const int j = jb + lane;
+                if (j < nch) {
+                    const float4 *row = reinterpret_cast<const float4 *>(p.ws_lse + (slot0 + j) * kHeadsPerCta);
+                    const float4 a = __ldcg(row), b4 = __ldcg(row + 1);
+                    const float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                    for (int h = 0; h < kHeadsPerCta; ++h) Mx[h] = fmaxf(Mx[h], v[h]);
+                }
+            }
+#pragma unroll
+            for (int h = 0; h < kHeadsPerCta; ++h)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+                    Mx[h] = fmaxf(Mx[h], __shfl_xor_sync(0xffffffffu, Mx[h], o));
+            float S[kHeadsPerCta];
+#pragma unroll
+            for (int h = 0; h < kHeadsPerCta; ++h) {
+                S[h] = 0.f;
+#pragma unroll
+                for (int kk = 0; kk < KD; ++kk) O[h][kk] = 0.f;
+            }
+#pragma unroll 2
+            for (int j = 0; j < nch; ++j) {
+                const float4 *row = reinterpret_cast<const float4 *>(p.ws_lse + (slot0 + j) * kHeadsPerCta);
+                const float4 a = __ldcg(row), b4 = __ldcg(row + 1);
+                const float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
+                const float *src = p.ws_o + (slot0 + j) * kHeadsPerCta * HD;
+#pragma unroll
+                for (int h = 0; h < kHeadsPerCta; ++h) {
+                    if (h < e.nh) {
+                        const float w = fast_exp2(v[h] - Mx[h]);
+                        S[h] += w;
+#pragma unroll
+                        for (int kk = 0; kk < KD; ++kk)
+                            O[h][kk] += w * __ldcg(src + h * HD + kk * 32 + lane);
+                    }
+                }
+            }
+            bf16 *orow = p.out + (int64_t)e.b * p.out_stride + (int64_t)e.head0 * HD;
+#pragma unroll
+            for (int h = 0; h < kHeadsPerCta; ++h) {
+                if (h >= e.nh) break;
+                const float inv = 1.f / S[h];
+#pragma unroll
+                for (int kk = 0; kk < KD; ++kk)
+                    orow[h * HD + kk * 32 + lane] = __float2bfloat16(O[h][kk] * inv);
+            }
+            if (lane == 0) p.ws_cnt[e.seg] = 0;  // ready for the next call
+        }
+        return;
+    }
+
     // ---------------------------------------------------------- consumers --
     const int g8 = lane >> 2, c4 = lane & 3;
     const int mi = lane >> 3, r8 = lane & 7;
     const int k_row = (mi & 1) * 8 + r8, k_chunk = mi >> 1;  // QK A operand (K tile)
     const int v_row = (mi >> 1) * 8 + r8, v_chunk = mi & 1;  // PV A operand (V^T tile)
-    float *red = reinterpret_cast<float *>(smem_gen + Cfg::kRedOffset);
-    constexpr int kRedFloats = Cfg::kRedFloats;
-
     uint32_t qf[KSTEPS][2];
     uint32_t fin_phase = 0;
+    int chunk_idx = 0;  // chunks handed to the epilogue so far
+    int nk_it = -1, nk_warp = -1;  // fused: stage and warp of the new token's page
+    NewKvInputs<HD> nk_in;
     WarpState<HD> st;
     st.reset();
     for (int it = 0;; ++it) {
         const int s = it % Cfg::kStages;
         if (!mbar_wait_bounded(&full_bar[s], (it / Cfg::kStages) & 1, &s_abort, p.status)) break;
         const StageMeta m = meta[s];
-        if (m.flags & kDone) break;
+        if (m.flags & kDone) {
+            if (warp < 2) {  // tell the epilogue warp to finish
+                if (chunk_idx > 0)
+                    mbar_wait_bounded(&epi_empty, (chunk_idx - 1) & 1, &s_abort, p.status);
+                if (warp == 0 && lane == 0) epi.done = 1;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&epi_full);
+            }
+            break;
+        }
         const int kvh = m.g / p.ctas_per_kv;
         const int hsub = m.g - kvh * p.ctas_per_kv;
         const int nh = min(kHeadsPerCta, p.group - hsub * kHeadsPerCta);
         if (m.flags & kFirst) {
-            const uint8_t *qs = smem_gen + Cfg::kQOffset + s * Cfg::kQBytes;
             const bool hv = g8 < nh;
+            if constexpr (FUSED) {
+                rope_q_fragments<HD>(p, m.b, kvh * p.group + hsub * kHeadsPerCta + g8, hv, m.pos,
+                                     c4, qf);
+                // Does this chunk end with the new token's page, and which warp
+                // and stage will hold it? Stages start at the chunk's first page.
+                nk_it = -1;
+                if (m.pos == m.n - 1 && m.chunk_p0 + m.take == m.pages_b) {
+                    const int k = m.pages_b - 1 - m.chunk_p0;
+                    nk_it = it + k / kPagesPerStage;
+                    nk_warp = k % kPagesPerStage;
+                    if (warp == nk_warp) nk_in.load(p, m.b, kvh, m.pos, m.pages_b - 1, lane);
+                }
+            } else {
+                const uint8_t *qs = smem_gen + Cfg::kQOffset + s * Cfg::kQBytes;
 #pragma unroll
-            for (int j = 0; j < KSTEPS; ++j) {
-                qf[j][0] = hv ? *reinterpret_cast<const uint32_t *>(qs + (g8 * HD + 16 * j + 2 * c4) * 2) : 0u;
-                qf[j][1] = hv ? *reinterpret_cast<const uint32_t *>(qs + (g8 * HD + 16 * j + 8 + 2 * c4) * 2) : 0u;
+                for (int j = 0; j < KSTEPS; ++j) {
+                    qf[j][0] = hv ? *reinterpret_cast<const uint32_t *>(qs + (g8 * HD + 16 * j + 2 * c4) * 2) : 0u;
+                    qf[j][1] = hv ? *reinterpret_cast<const uint32_t *>(qs + (g8 * HD + 16 * j + 8 + 2 * c4) * 2) : 0u;
+                }
             }
             st.reset();
         }
@@ -443,6 +730,14 @@ __global__ void __launch_bounds__(kThreads)
             const int valid = min(kBlockSize, m.n - page * kBlockSize);
             const uint32_t kpage = smem_base + s * Cfg::kStageBytes + warp * Cfg::kPageBytes;
             const uint32_t vpage = kpage + kPagesPerStage * Cfg::kPageBytes;
+            if (FUSED && it == nk_it && warp == nk_warp) {
+                // The new token: its rotated K and V + bias replace the tile row
+                // (loaded before the append) and are appended to the pools by the
+                // first 8-head slice of the kv head.
+                nk_in.apply(p, kvh, m.pos, hsub == 0, smem_gen, smem_base, kpage, vpage,
+                            m.pos % kBlockSize, lane);
+                __syncwarp();
+            }
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int j = 0; j < KSTEPS; ++j) {
@@ -497,87 +792,29 @@ __global__ void __launch_bounds__(kThreads)
             st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, off);
             st.l1 += __shfl_xor_sync(0xffffffffu, st.l1, off);
         }
-        // Tree merge of the 4 warps through two shared slots.
-        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        // Halve the 4 warp states into the 2 shared slots, hand them over.
+        if (chunk_idx > 0) mbar_wait_bounded(&epi_empty, (chunk_idx - 1) & 1, &s_abort, p.status);
         if (warp >= 2) state_store<HD>(red + (warp - 2) * kRedFloats, st, lane);
         consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
-        if (warp < 2) state_combine<HD>(st, red + warp * kRedFloats, lane);
-        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
-        if (warp == 1) state_store<HD>(red, st, lane);
-        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
-        if (warp != 0) {
-            st.reset();
-            continue;
-        }
-        state_combine<HD>(st, red, lane);
-        const int head0 = kvh * p.group + hsub * kHeadsPerCta;
-        const int seg = m.b * G + m.g;
-        const bool whole = m.chunk_p0 == 0 && m.take == m.pages_b;
-        const float il0 = 1.f / st.l0, il1 = 1.f / st.l1;
-        if (whole) {
-            bf16 *orow = p.out + (int64_t)m.b * p.out_stride + (int64_t)head0 * HD;
-#pragma unroll
-            for (int i = 0; i < KSTEPS; ++i)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int h = 2 * c4 + (e & 1);
-                    if (h < nh)
-                        orow[h * HD + 16 * i + g8 + (e >> 1) * 8] =
-                            __float2bfloat16(st.o[i][e] * ((e & 1) ? il1 : il0));
-                }
-            st.reset();
-            continue;
-        }
-        // Partial of a split segment: slot = segment + this CTA.
-        const long long slot = (long long)seg + cta;
-        float *wo = p.ws_o + slot * kHeadsPerCta * HD;
-#pragma unroll
-        for (int i = 0; i < KSTEPS; ++i)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int h = 2 * c4 + (e & 1);
-                wo[h * HD + 16 * i + g8 + (e >> 1) * 8] = st.o[i][e] * ((e & 1) ? il1 : il0);
+        if (warp < 2) {
+            state_combine<HD>(st, red + warp * kRedFloats, lane);
+            __syncwarp();
+            state_store<HD>(red + warp * kRedFloats, st, lane);
+            if (warp == 0 && lane == 0) {
+                epi.b = m.b;
+                epi.seg = m.b * G + m.g;
+                epi.nh = nh;
+                epi.head0 = kvh * p.group + hsub * kHeadsPerCta;
+                epi.pages_b = m.pages_b;
+                epi.whole = m.chunk_p0 == 0 && m.take == m.pages_b;
+                epi.done = 0;
+                epi.seg_start = m.seg_start;
             }
-        if (g8 == 0) {
-            p.ws_lse[slot * kHeadsPerCta + 2 * c4] = st.m0 + __log2f(st.l0);
-            p.ws_lse[slot * kHeadsPerCta + 2 * c4 + 1] = st.m1 + __log2f(st.l1);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&epi_full);
         }
+        ++chunk_idx;
         st.reset();
-        __threadfence();
-        __syncwarp();
-        const int c_first = owner_cta(m.seg_start, T, C);
-        const int c_last = owner_cta(m.seg_start + m.pages_b - 1, T, C);
-        const int nch = c_last - c_first + 1;
-        int last = 0;
-        if (lane == 0) last = atomicAdd(p.ws_cnt + seg, 1) == nch - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
-        // Merge the nch partials of this segment (slots seg + c_first + j).
-        const long long slot0 = (long long)seg + c_first;
-        for (int h = 0; h < nh; ++h) {
-            float M = -INFINITY;
-            for (int j = lane; j < nch; j += 32)
-                M = fmaxf(M, __ldcg(p.ws_lse + (slot0 + j) * kHeadsPerCta + h));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            float acc[HD / 32];
-#pragma unroll
-            for (int k = 0; k < HD / 32; ++k) acc[k] = 0.f;
-            float S = 0.f;
-            for (int j = 0; j < nch; ++j) {
-                const float w = fast_exp2(__ldcg(p.ws_lse + (slot0 + j) * kHeadsPerCta + h) - M);
-                S += w;
-                const float *src = p.ws_o + ((slot0 + j) * kHeadsPerCta + h) * HD;
-#pragma unroll
-                for (int k = 0; k < HD / 32; ++k) acc[k] += w * __ldcg(src + k * 32 + lane);
-            }
-            const float inv = 1.f / S;
-            bf16 *orow = p.out + (int64_t)m.b * p.out_stride + (int64_t)(head0 + h) * HD;
-#pragma unroll
-            for (int k = 0; k < HD / 32; ++k) orow[k * 32 + lane] = __float2bfloat16(acc[k] * inv);
-        }
-        if (lane == 0) p.ws_cnt[seg] = 0;  // ready for the next call
     }
 }
 
@@ -621,8 +858,8 @@ int max_ctas_for_device() {
         int per_sm = 0;
         const int smem = DecodeCfg<HD>::kSmemBytes;
         if (dev < 0 ||
-            ensure_smem_attr((const void *)paged_decode_kernel<HD>, smem) != LC_OK ||
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<HD>,
+            ensure_smem_attr((const void *)paged_decode_kernel<HD, false>, smem) != LC_OK ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<HD, false>,
                                                           kThreads, smem) != cudaSuccess ||
             per_sm < 1) {
             cudaGetLastError();
@@ -637,7 +874,7 @@ int max_ctas_for_device() {
 
 int max_ctas(int hd) { return hd == 64 ? max_ctas_for_device<64>() : max_ctas_for_device<128>(); }
 
-template <int HD>
+template <int HD, bool FUSED = false>
 int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const void *v_pool,
                   cudaStream_t stream) {
     CUtensorMap mk, mv;
@@ -646,9 +883,9 @@ int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const v
     rc = pool_tensor_map(v_pool, prm.pool_rows, HD, &mv);
     if (rc) return rc;
     const int smem = DecodeCfg<HD>::kSmemBytes;
-    rc = ensure_smem_attr((const void *)paged_decode_kernel<HD>, smem);
+    rc = ensure_smem_attr((const void *)paged_decode_kernel<HD, FUSED>, smem);
     if (rc) return rc;
-    paged_decode_kernel<HD><<<grid, kThreads, smem, stream>>>(mk, mv, prm);
+    paged_decode_kernel<HD, FUSED><<<grid, kThreads, smem, stream>>>(mk, mv, prm);
     return launch_status();
 }
 
@@ -746,6 +983,88 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
                           : launch_decode<128>(prm, grid, k_pool, v_pool, s);
 }
 
+extern "C" int lc_rope_append_decode(void *out, int64_t out_stride, const void *qkv,
+                                     int64_t row_stride, const int *positions,
+                                     const void *q_bias, const void *k_bias, const void *v_bias,
+                                     const float *cos_cache, const float *sin_cache,
+                                     int rope_rows, void *k_pool, void *v_pool,
+                                     int64_t num_blocks, int num_layers, int layer,
+                                     int num_q_heads, int num_kv_heads, int head_dim,
+                                     const int *block_tables, int table_stride, int batch,
+                                     int max_context_len, int partition_tokens, float sm_scale,
+                                     void *workspace, size_t workspace_bytes, int *dev_status,
+                                     lc_stream_t stream) {
+    if (!out || !qkv || !positions || !q_bias || !k_bias || !v_bias || !cos_cache ||
+        !sin_cache || !k_pool || !v_pool || !block_tables)
+        return LC_ERR_INVALID_ARGUMENT;
+    if (head_dim != 64 && head_dim != 128) return LC_ERR_UNSUPPORTED_HEAD_DIM;
+    if (batch < 0 || num_layers <= 0 || layer < 0 || layer >= num_layers || num_q_heads <= 0 ||
+        num_kv_heads <= 0 || num_blocks <= 0 || table_stride <= 0 || rope_rows <= 0 ||
+        partition_tokens < 0)
+        return LC_ERR_INVALID_ARGUMENT;
+    if (num_q_heads % num_kv_heads) return LC_ERR_UNSUPPORTED_SHAPE;
+    if (batch == 0) return LC_OK;
+    if (!aligned16(k_pool) || !aligned16(v_pool) || !aligned16(qkv) || (row_stride & 7) ||
+        ((uintptr_t)out & 1))
+        return LC_ERR_MISALIGNED;
+    if (row_stride < (int64_t)(num_q_heads + 2 * num_kv_heads) * head_dim ||
+        out_stride < (int64_t)num_q_heads * head_dim)
+        return LC_ERR_INVALID_ARGUMENT;
+    const int64_t pool_rows = num_blocks * num_layers * num_kv_heads * kBlockSize;
+    if (pool_rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
+
+    const int G = segments_per_seq(num_q_heads, num_kv_heads);
+    const int cmax = max_ctas(head_dim);
+    const WsLayout wl = ws_layout(batch, G, head_dim, cmax);
+    if (!workspace || workspace_bytes < wl.total()) return LC_ERR_WORKSPACE_TOO_SMALL;
+    if (!aligned16(workspace)) return LC_ERR_MISALIGNED;
+    int grid = cmax;
+    if (max_context_len > 0) {
+        const long long pages_hint =
+            (long long)batch * G * ((max_context_len + kBlockSize - 1) / kBlockSize);
+        const long long want = (pages_hint + 1) / 2;
+        if (want < grid) grid = (int)(want < 1 ? 1 : want);
+    }
+    DecodeParams prm{};
+    prm.out = (bf16 *)out;
+    prm.out_stride = out_stride;
+    prm.q = (const bf16 *)qkv;
+    prm.q_stride = row_stride;
+    prm.tables = block_tables;
+    prm.table_stride = table_stride;
+    prm.ctx_lens = positions;
+    prm.len_offset = 1;
+    prm.batch = batch;
+    prm.pool_rows = pool_rows;
+    prm.num_blocks = num_blocks;
+    prm.num_layers = num_layers;
+    prm.layer = layer;
+    prm.num_q_heads = num_q_heads;
+    prm.num_kv_heads = num_kv_heads;
+    prm.group = num_q_heads / num_kv_heads;
+    prm.ctas_per_kv = (prm.group + kHeadsPerCta - 1) / kHeadsPerCta;
+    prm.seg_per_seq = G;
+    prm.partition_tokens = partition_tokens;
+    prm.scale_log2 = sm_scale * 1.4426950408889634f;
+    uint8_t *ws = (uint8_t *)workspace;
+    prm.ws_cnt = (int *)ws;
+    prm.ws_lse = (float *)(ws + wl.cnt_bytes);
+    prm.ws_o = (float *)(ws + wl.cnt_bytes + wl.lse_bytes);
+    prm.status = dev_status;
+    prm.qkv = (const bf16 *)qkv;
+    prm.q_bias = (const bf16 *)q_bias;
+    prm.k_bias = (const bf16 *)k_bias;
+    prm.v_bias = (const bf16 *)v_bias;
+    prm.cos_t = cos_cache;
+    prm.sin_t = sin_cache;
+    prm.rope_rows = rope_rows;
+    prm.k_pool_w = (bf16 *)k_pool;
+    prm.v_pool_w = (bf16 *)v_pool;
+    cudaStream_t s = as_stream(stream);
+    return head_dim == 64 ? launch_decode<64, true>(prm, grid, k_pool, v_pool, s)
+                          : launch_decode<128, true>(prm, grid, k_pool, v_pool, s);
+}
+
 extern "C" size_t lc_flash_decoding_workspace_size(int num_q_heads, int head_dim,
                                                    int max_seq_len) {
     (void)max_seq_len;  // the persistent split needs no per-length storage
@@ -818,9 +1137,9 @@ template <int HD>
 int static_max_ctas(int sms, int *out) {
     const int smem = DecodeCfg<HD>::kSmemBytes;
     int per_sm = 0;
-    if (cudaFuncSetAttribute(paged_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(paged_decode_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem) != cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<HD>, kThreads,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_kernel<HD, false>, kThreads,
                                                       smem) != cudaSuccess ||
         per_sm < 1) {
         cudaGetLastError();
@@ -864,7 +1183,7 @@ int launch_decode_static(const DecodeParams &prm, int grid, const void *k_pool,
     if (rc) return rc;
     rc = pool_tensor_map_nocache(v_pool, prm.pool_rows, HD, &mv);
     if (rc) return rc;
-    paged_decode_kernel<HD><<<grid, kThreads, DecodeCfg<HD>::kSmemBytes, stream>>>(mk, mv, prm);
+    paged_decode_kernel<HD, false><<<grid, kThreads, DecodeCfg<HD>::kSmemBytes, stream>>>(mk, mv, prm);
     return launch_status();
 }
 

@@ -5,23 +5,14 @@
 //   lc_update_kv_cache append one token's k and v+bias           (src/kernels/kv_cache.cu:3-59)
 //   lc_rope_append     both, for a batch of token rows, one launch (src/models.rs:506-534)
 //
-// Bit-exactness: the reference computes in fp32 with the CUDA compiler's default
-// FMA contraction. The two rotate-half expressions x1*c - x2*s and x1*s + x2*c
-// are written here with explicit round-to-nearest intrinsics in the contraction
-// form that reproduces the reference kernel's results (pinned by comparing
-// outputs on a B200; modes as in oracle/lc_oracle.h). The q+bias and v+bias
-// additions are single fp32 adds; results round to bf16 with RNE.
+// Bit-exactness: the rotate-half arithmetic (rope_math.cuh) rounds as the
+// reference kernel does; the q+bias and v+bias additions are single fp32 adds;
+// results round to bf16 with RNE.
 #include <climits>
 
 #include "lc_common.cuh"
 #include "lc_host.h"
-
-#ifndef LC_ROPE_SUB_MODE
-#define LC_ROPE_SUB_MODE 1  // x1*c - x2*s  ->  fma(x1, c, -(x2*s))
-#endif
-#ifndef LC_ROPE_ADD_MODE
-#define LC_ROPE_ADD_MODE 1  // x1*s + x2*c  ->  fma(x1, s, x2*c)
-#endif
+#include "rope_math.cuh"
 
 namespace lc {
 namespace {
@@ -45,26 +36,6 @@ struct RopeAppendParams {
     int table_stride;  // <= 0: unchecked
     int *status;
 };
-
-__device__ __forceinline__ float rot_sub(float x1, float c, float x2, float s) {
-#if LC_ROPE_SUB_MODE == 1
-    return __fmaf_rn(x1, c, -__fmul_rn(x2, s));
-#elif LC_ROPE_SUB_MODE == 2
-    return __fmaf_rn(-x2, s, __fmul_rn(x1, c));
-#else
-    return __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-#endif
-}
-
-__device__ __forceinline__ float rot_add(float x1, float s, float x2, float c) {
-#if LC_ROPE_ADD_MODE == 1
-    return __fmaf_rn(x1, s, __fmul_rn(x2, c));
-#elif LC_ROPE_ADD_MODE == 2
-    return __fmaf_rn(x2, c, __fmul_rn(x1, s));
-#else
-    return __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
-#endif
-}
 
 // Returns the pool element offset of (pos, kv head 0) for row `row`, or -1 when
 // the row must not be appended (status bits set for bad positions/blocks).

@@ -41,6 +41,9 @@ SIGNATURES = {
     "lc_paged_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32, _vp, _sz,
                                _vp, _vp]),
+    "lc_rope_append_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
+                                     _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _i32,
+                                     _i32, _i32, _i32, _f32, _vp, _sz, _vp, _vp]),
     "lc_paged_decode_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                       _i32, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32,
                                       _vp, _vp]),
@@ -178,6 +181,24 @@ def paged_decode(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_he
                               _p(workspace),
                               0 if workspace is None else workspace.numel() * workspace.element_size(),
                               _p(dev_status), _stream(stream)), "lc_paged_decode")
+
+
+def rope_append_decode(out, qkv, positions, q_bias, k_bias, v_bias, cos, sin, k_pool, v_pool,
+                       num_blocks, num_layers, layer, num_q_heads, num_kv_heads, head_dim,
+                       block_tables, max_context_len=0, sm_scale=None, partition_tokens=0,
+                       workspace=None, dev_status=None, stream=None):
+    """One launch: bias + RoPE + append of each sequence's new token, then decode."""
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(head_dim)
+    batch = positions.shape[0]
+    check(lib.lc_rope_append_decode(_p(out), out.stride(0), _p(qkv), qkv.stride(0),
+                                    _p(positions), _p(q_bias), _p(k_bias), _p(v_bias), _p(cos),
+                                    _p(sin), cos.shape[0], _p(k_pool), _p(v_pool), num_blocks,
+                                    num_layers, layer, num_q_heads, num_kv_heads, head_dim,
+                                    _p(block_tables), block_tables.stride(0), batch,
+                                    max_context_len, partition_tokens, sm_scale, _p(workspace),
+                                    0 if workspace is None else workspace.numel() * workspace.element_size(),
+                                    _p(dev_status), _stream(stream)), "lc_rope_append_decode")
 
 
 def paged_decode_static(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_heads,

@@ -1,0 +1,76 @@
+"""lc_rope_append_decode (one launch) against lc_rope_append + lc_paged_decode
+(two launches) and against the CPU oracle: identical pool writes and attention
+outputs; the fused form leaves the qkv rows unmodified."""
+import numpy as np
+import pytest
+
+import lucciola as L
+import oracle.oracle as O
+from conftest import ATTN_ATOL
+from workloads import from_device, make_case, randn_bf16, to_device
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def run_both(hq, hkv, hd, ctx, seed, partition_tokens=0):
+    rng = np.random.default_rng(seed)
+    ctx = np.asarray(ctx, np.int32)
+    B = len(ctx)
+    case = make_case(B, hq, hkv, hd, ctx + 1, seed=seed)  # room for the new token
+    row = (hq + 2 * hkv) * hd + 16
+    qkv = randn_bf16(rng, (B, row))
+    qb, kb, vb = (randn_bf16(rng, (n * hd,)) for n in (hq, hkv, hkv))
+    cos, sin = O.rope_table(int(ctx.max()) + 8, hd, 1e6)
+    dev = [to_device(x) for x in (qb, kb, vb, cos, sin, ctx, case.tables)]
+    ws = L.alloc_decode_workspace(B, hq, hkv, hd)
+
+    # two launches
+    qkv_a, ka, va = to_device(qkv), to_device(case.k_pool), to_device(case.v_pool)
+    out_a = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    L.rope_append(qkv_a, dev[5], dev[0], dev[1], dev[2], dev[3], dev[4], ka, va, case.num_blocks,
+                  case.num_layers, case.layer, hq, hkv, hd, dev[6])
+    L.paged_decode(out_a, qkv_a, ka, va, case.num_blocks, case.num_layers, case.layer, hq, hkv, hd,
+                   dev[6], dev[5], int(ctx.max()) + 1, len_offset=1,
+                   partition_tokens=partition_tokens, workspace=ws)
+    # one launch
+    qkv_b, kb_, vb_ = to_device(qkv), to_device(case.k_pool), to_device(case.v_pool)
+    out_b = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.rope_append_decode(out_b, qkv_b, dev[5], dev[0], dev[1], dev[2], dev[3], dev[4], kb_, vb_,
+                         case.num_blocks, case.num_layers, case.layer, hq, hkv, hd, dev[6],
+                         int(ctx.max()) + 1, partition_tokens=partition_tokens, workspace=ws,
+                         dev_status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    return case, qkv, (qb, kb, vb, cos, sin), (qkv_a, ka, va, out_a), (qkv_b, kb_, vb_, out_b)
+
+
+@pytest.mark.parametrize("hq,hkv,hd", [(14, 2, 64), (28, 4, 128), (12, 2, 128), (64, 8, 128),
+                                       (32, 2, 64), (8, 8, 64)])
+def test_fused_equals_two_launches_and_oracle(hq, hkv, hd):
+    ctx = [0, 15, 16, 31, 300, 511, 1023, 2000]
+    case, qkv, bias, a, b = run_both(hq, hkv, hd, ctx, seed=hq + hd)
+    for x, y in zip(a[1:], b[1:]):  # pools and outputs
+        assert torch.equal(x.view(torch.int16), y.view(torch.int16))
+    assert np.array_equal(from_device(b[0]), qkv)  # qkv only read
+    # oracle: rope -> append -> attention over positions 0..ctx inclusive
+    qb, kb, vb, cos, sin = bias
+    q2 = qkv.copy()
+    O.rope_append(q2, np.asarray(ctx, np.int32), qb, kb, vb, cos, sin, case.k_pool, case.v_pool,
+                  case.num_layers, case.layer, hq, hkv, hd, case.tables)
+    assert np.array_equal(from_device(a[0]), q2)
+    ref = O.paged_decode(q2, case.k_pool, case.v_pool, case.layer, hq, hkv, hd, case.tables,
+                         np.asarray(ctx, np.int32), case.num_layers, len_offset=1, threads=8)
+    got = O.bf16_to_f32(from_device(b[3]))
+    assert float(np.abs(got - O.bf16_to_f32(ref)).max()) <= ATTN_ATOL
+
+
+@pytest.mark.parametrize("ptok", [16, 64])
+def test_fused_new_token_page_owned_by_a_later_cta(ptok):
+    """Small partitions: the page holding the new token belongs to a CTA that
+    does not own the segment's first page; every CTA rotates q itself."""
+    case, qkv, bias, a, b = run_both(28, 4, 128, [4095, 1040, 17], seed=ptok, partition_tokens=ptok)
+    for x, y in zip(a[1:], b[1:]):
+        assert torch.equal(x.view(torch.int16), y.view(torch.int16))
