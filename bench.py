@@ -314,6 +314,8 @@ def run_ours(args, rank, world, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
+    import lucciola as L
+    L.set_dependent_launch(args.pdl)
     w = Workload(args.config, rank, world, device)
     if args.partition is not None:
         w.ptok = args.partition
@@ -424,7 +426,8 @@ def run_ours(args, rank, world, local):
                              (w.kv_bytes_per_step / 1e9),
                        "step": ("per layer: lc_rope_append + lc_paged_decode" if args.unfused else
                                 "per layer: lc_rope_append_decode (fused bias+RoPE+append+"
-                                "attention)") + "; CUDA graph"},
+                                "attention)") + "; CUDA graph" +
+                               (f"; programmatic dependent launch mode {args.pdl}" if args.pdl else "")},
             "tokens_per_s": round(w.global_batch / (ms_step * 1e-3), 1),
             "pct_hbm": round(100 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -556,6 +559,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
                     help="kernel: eager launches only (for profilers), no JSON metrics")
+    ap.add_argument("--pdl", type=int, default=0, choices=[0, 1, 2],
+                    help="programmatic dependent launch mode (lc_set_dependent_launch)")
     ap.add_argument("--unfused", action="store_true",
                     help="two launches per layer (lc_rope_append, lc_paged_decode)")
     ap.add_argument("--partition", type=int, default=None,

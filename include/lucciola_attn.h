@@ -63,6 +63,18 @@ int lc_status_from_device_word(int word);
 /* Library version string, e.g. "lucciola-b200 0.1 sm_100a". */
 const char *lc_version(void);
 
+/* Programmatic dependent launch for the decode kernels (lc_paged_decode,
+ * lc_rope_append_decode, lc_flash_decoding), process-wide:
+ *   0 (default) plain launches;
+ *   1 launched with programmatic stream serialization: a decode grid may be
+ *     scheduled while the preceding grid in the stream retires and waits for
+ *     it (griddepcontrol.wait) before reading or writing any memory;
+ *   2 as 1, but the grid reads the context lengths and computes its split
+ *     before that wait: the kernel launched just before it on the stream must
+ *     not write the context lengths (positions) it is given.
+ * Returns the previous mode, or -1 for an invalid mode. */
+int lc_set_dependent_launch(int mode);
+
 /* ------------------------------------------------------------------------- */
 /* Reference-shaped entry points (single sequence, drop-in for the kernels).  */
 /* ------------------------------------------------------------------------- */

@@ -1,6 +1,7 @@
 // runtime.cpp - status strings, tensor-map cache, per-device launch attributes.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -158,3 +159,15 @@ int pool_tensor_map_nocache(const void *pool, int64_t rows, int head_dim, CUtens
 }
 
 }  // namespace lc
+
+namespace lc {
+namespace {
+std::atomic<int> g_dependent_launch{0};
+}
+int dependent_launch_mode() { return g_dependent_launch.load(std::memory_order_relaxed); }
+}  // namespace lc
+
+extern "C" int lc_set_dependent_launch(int mode) {
+    if (mode < 0 || mode > 2) return -1;
+    return lc::g_dependent_launch.exchange(mode);
+}

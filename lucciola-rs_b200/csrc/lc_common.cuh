@@ -28,6 +28,13 @@ __device__ inline void set_status(int *status, int bits) {
     if (status) atomicOr(status, bits);
 }
 
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ inline int atom_add_acq_rel_gpu(int *addr, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+
 __device__ inline uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -37,6 +44,13 @@ __device__ inline uint64_t global_timer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+
+// Programmatic dependent launch (sm_90+): both are no-ops for a grid that was
+// not launched with programmatic stream serialization.
+__device__ inline void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ inline void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ---------------------------------------------------------------- mbarrier --
 __device__ inline void mbar_init(uint64_t *bar, uint32_t count) {

@@ -34,4 +34,7 @@ int ensure_smem_attr(const void *func, int bytes);
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Process-wide programmatic-dependent-launch mode (lc_set_dependent_launch).
+int dependent_launch_mode();
+
 }  // namespace lc

@@ -47,6 +47,7 @@ constexpr int kEpilogueWarp = kConsumerWarps + 1;  // warp 5
 constexpr int kThreads = (kConsumerWarps + 2) * 32;
 constexpr int kHeadsPerCta = 8;
 constexpr int kPagesPerStage = kConsumerWarps;  // one page per consumer warp per stage
+constexpr int kMinPagesPerCta = 8;               // auto split: two stages per CTA at least
 
 enum : int { kFirst = 1, kLast = 2, kDone = 4 };
 
@@ -92,6 +93,7 @@ struct DecodeParams {
     int seg_per_seq;  // num_kv_heads * ctas_per_kv
     int partition_tokens;
     float scale_log2;  // sm_scale * log2(e)
+    int early_setup;   // read context lengths before waiting for the preceding grid
     float *ws_o;       // [slots][8][HD]
     float *ws_lse;     // [slots][8]
     int *ws_cnt;       // [batch * seg_per_seq]
@@ -344,6 +346,11 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int G = p.seg_per_seq;
+    // Programmatic dependent launch (no-ops otherwise): let the next grid in the
+    // stream be scheduled as our CTAs retire, and wait for the preceding grid
+    // before touching its outputs.
+    griddep_launch_dependents();
+    if (!p.early_setup) griddep_wait();
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
     // Set-up scan scratch: the head of the stage ring, free until the first TMA.
@@ -355,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     long long mine = 0;
     for (int b = bs; b < be; ++b) mine += (seq_tokens(p, b, false) + kBlockSize - 1) / kBlockSize;
     s_part[tid] = mine;
+    if (p.early_setup) griddep_wait();
     for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
         if (seq_tokens(p, b, false) == 0)
             for (int i = tid; i < p.num_q_heads * HD; i += kThreads)
@@ -389,9 +397,11 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     if (T == 0) return;
     int C = gridDim.x;
     {
+        // Auto: at least kMinPagesPerCta pages per CTA, so that a short batch is
+        // not split into more partials than its merge can absorb cheaply.
         const long long want = p.partition_tokens > 0
                                    ? (T * kBlockSize + p.partition_tokens - 1) / p.partition_tokens
-                                   : (T + 1) / 2;
+                                   : (T + kMinPagesPerCta - 1) / kMinPagesPerCta;
         if (want < C) C = (int)(want < 1 ? 1 : want);
         if (T < C) C = (int)T;
     }
@@ -606,6 +616,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                 for (int kk = 0; kk < KD; ++kk) wo[h * HD + kk * 32 + lane] = O[h][kk] * il;
                 if (lane == h) p.ws_lse[slot * kHeadsPerCta + h] = Mh[h] + __log2f(Lh[h]);
             }
+            // Publish the partial, then count it; the last CTA to arrive merges.
             __threadfence();
             __syncwarp();
             const int c_first = owner_cta(e.seg_start, T, C);
@@ -641,22 +652,38 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
 #pragma unroll
                 for (int kk = 0; kk < KD; ++kk) O[h][kk] = 0.f;
             }
-#pragma unroll 2
-            for (int j = 0; j < nch; ++j) {
-                const float4 *row = reinterpret_cast<const float4 *>(p.ws_lse + (slot0 + j) * kHeadsPerCta);
-                const float4 a = __ldcg(row), b4 = __ldcg(row + 1);
-                const float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
-                const float *src = p.ws_o + (slot0 + j) * kHeadsPerCta * HD;
+            // Partials in groups of kMergeGroup with predicated loads: a group's
+            // loads are all in flight together, whatever nch is.
+            constexpr int kMergeGroup = 2;
+            for (int jb = 0; jb < nch; jb += kMergeGroup) {
+                float w[kMergeGroup][kHeadsPerCta];
+                float vals[kMergeGroup][kHeadsPerCta][KD];
 #pragma unroll
-                for (int h = 0; h < kHeadsPerCta; ++h) {
-                    if (h < e.nh) {
-                        const float w = fast_exp2(v[h] - Mx[h]);
-                        S[h] += w;
+                for (int u = 0; u < kMergeGroup; ++u) {
+                    const int j = jb + u;
+                    const bool in = j < nch;
+                    const long long sl = slot0 + (in ? j : 0);
+                    const float4 *row = reinterpret_cast<const float4 *>(p.ws_lse + sl * kHeadsPerCta);
+                    const float4 a = __ldcg(row), b4 = __ldcg(row + 1);
+                    const float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
+                    const float *src = p.ws_o + sl * kHeadsPerCta * HD;
+#pragma unroll
+                    for (int h = 0; h < kHeadsPerCta; ++h) {
+                        w[u][h] = in ? v[h] : -INFINITY;
 #pragma unroll
                         for (int kk = 0; kk < KD; ++kk)
-                            O[h][kk] += w * __ldcg(src + h * HD + kk * 32 + lane);
+                            vals[u][h][kk] = h < e.nh ? __ldcg(src + h * HD + kk * 32 + lane) : 0.f;
                     }
                 }
+#pragma unroll
+                for (int u = 0; u < kMergeGroup; ++u)
+#pragma unroll
+                    for (int h = 0; h < kHeadsPerCta; ++h) {
+                        const float wt = fast_exp2(w[u][h] - Mx[h]);  // 0 for padding
+                        S[h] += wt;
+#pragma unroll
+                        for (int kk = 0; kk < KD; ++kk) O[h][kk] += wt * vals[u][h][kk];
+                    }
             }
             bf16 *orow = p.out + (int64_t)e.b * p.out_stride + (int64_t)e.head0 * HD;
 #pragma unroll
@@ -885,8 +912,24 @@ int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const v
     const int smem = DecodeCfg<HD>::kSmemBytes;
     rc = ensure_smem_attr((const void *)paged_decode_kernel<HD, FUSED>, smem);
     if (rc) return rc;
-    paged_decode_kernel<HD, FUSED><<<grid, kThreads, smem, stream>>>(mk, mv, prm);
-    return launch_status();
+    const int mode = dependent_launch_mode();
+    DecodeParams prm2 = prm;
+    prm2.early_setup = mode == 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = mode > 0 ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, paged_decode_kernel<HD, FUSED>, mk, mv, prm2) != cudaSuccess) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    return LC_OK;
 }
 
 }  // namespace
@@ -949,7 +992,7 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     if (max_context_len > 0) {
         const long long pages_hint =
             (long long)batch * G * ((max_context_len + kBlockSize - 1) / kBlockSize);
-        const long long want = (pages_hint + 1) / 2;
+        const long long want = (pages_hint + kMinPagesPerCta - 1) / kMinPagesPerCta;
         if (want < grid) grid = (int)(want < 1 ? 1 : want);
     }
     DecodeParams prm{};
@@ -1022,7 +1065,7 @@ extern "C" int lc_rope_append_decode(void *out, int64_t out_stride, const void *
     if (max_context_len > 0) {
         const long long pages_hint =
             (long long)batch * G * ((max_context_len + kBlockSize - 1) / kBlockSize);
-        const long long want = (pages_hint + 1) / 2;
+        const long long want = (pages_hint + kMinPagesPerCta - 1) / kMinPagesPerCta;
         if (want < grid) grid = (int)(want < 1 ? 1 : want);
     }
     DecodeParams prm{};
@@ -1240,7 +1283,7 @@ extern "C" int lc_paged_decode_static(void *out, int64_t out_stride, const void 
     if (max_context_len > 0) {
         const long long pages_hint =
             (long long)batch * G * ((max_context_len + kBlockSize - 1) / kBlockSize);
-        const long long want = (pages_hint + 1) / 2;
+        const long long want = (pages_hint + kMinPagesPerCta - 1) / kMinPagesPerCta;
         if (want < grid) grid = (int)(want < 1 ? 1 : want);
     }
     DecodeParams prm{};

@@ -74,3 +74,52 @@ def test_fused_new_token_page_owned_by_a_later_cta(ptok):
     case, qkv, bias, a, b = run_both(28, 4, 128, [4095, 1040, 17], seed=ptok, partition_tokens=ptok)
     for x, y in zip(a[1:], b[1:]):
         assert torch.equal(x.view(torch.int16), y.view(torch.int16))
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_dependent_launch_modes_give_identical_results(mode):
+    """Back-to-back fused decode launches of several layers, eager and captured
+    in a CUDA graph, with programmatic dependent launch on: same outputs and
+    pools as plain launches."""
+    hq, hkv, hd, layers = 14, 2, 64, 3
+    rng = np.random.default_rng(mode)
+    ctx = rng.integers(1, 3000, 24).astype(np.int32)
+    case = make_case(24, hq, hkv, hd, ctx + 1, num_layers=layers, layer=0, seed=mode)
+    row = (hq + 2 * hkv) * hd
+    qkv = to_device(randn_bf16(rng, (layers, 24, row)))
+    qb, kb, vb = (to_device(randn_bf16(rng, (n * hd,))) for n in (hq, hkv, hkv))
+    cos, sin = (to_device(x) for x in O.rope_table(4096, hd, 1e6))
+    pos, tables = to_device(ctx), to_device(case.tables)
+    ws = L.alloc_decode_workspace(24, hq, hkv, hd)
+
+    def run(m, graph):
+        kp, vp = to_device(case.k_pool), to_device(case.v_pool)
+        out = torch.zeros(layers, 24, hq * hd, dtype=torch.bfloat16, device="cuda")
+        old = L.set_dependent_launch(m)
+        try:
+            def step():
+                for l in range(layers):
+                    L.rope_append_decode(out[l], qkv[l], pos, qb, kb, vb, cos, sin, kp, vp,
+                                         case.num_blocks, layers, l, hq, hkv, hd, tables,
+                                         int(ctx.max()) + 1, workspace=ws)
+            if graph:
+                step()  # warm-up outside capture
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                s = torch.cuda.Stream()
+                with torch.cuda.graph(g, stream=s):
+                    step()
+                g.replay()
+                g.replay()
+            else:
+                step()
+            torch.cuda.synchronize()
+        finally:
+            L.set_dependent_launch(old)
+        return out, kp, vp
+
+    base = run(0, False)
+    for graph in (False, True):
+        got = run(mode, graph)
+        for x, y in zip(base, got):
+            assert torch.equal(x.view(torch.int16), y.view(torch.int16))
