@@ -28,6 +28,7 @@ SIGNATURES = {
     "lc_status_string": (C.c_char_p, [_i32]),
     "lc_status_from_device_word": (_i32, [_i32]),
     "lc_version": (C.c_char_p, []),
+    "lc_set_dependent_launch": (_i32, [_i32]),
     "lc_rope": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
     "lc_update_kv_cache": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32, _i32,
                                   _i32, _i32, _vp]),
@@ -89,6 +90,14 @@ class LucciolaError(RuntimeError):
 def check(status: int, where: str) -> None:
     if status != LC_OK:
         raise LucciolaError(status, where)
+
+
+def set_dependent_launch(mode: int) -> int:
+    """Programmatic dependent launch mode for decode launches (0, 1 or 2); returns the old one."""
+    old = lib.lc_set_dependent_launch(mode)
+    if old < 0:
+        raise ValueError(f"invalid dependent-launch mode {mode}")
+    return old
 
 
 def version() -> str:
