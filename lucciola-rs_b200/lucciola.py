@@ -278,6 +278,14 @@ def shard_kv_heads(num_q_heads, num_kv_heads, num_ranks, rank):
     return first.value, count.value
 
 
+def assemble_head_shards(gathered, num_ranks):
+    """[R*B, Hq/R*hd] rows from an all-gather of per-rank head slices (rank-major)
+    -> [B, Hq*hd]: rank r's slice holds q heads [r*Hq/R, (r+1)*Hq/R)."""
+    rows, width = gathered.shape
+    batch = rows // num_ranks
+    return gathered.reshape(num_ranks, batch, width).transpose(0, 1).reshape(batch, num_ranks * width)
+
+
 class KVCache:
     """Owning mirror of the reference's KVCache (src/layers/kv_cache.rs)."""
 
