@@ -559,8 +559,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
                     help="kernel: eager launches only (for profilers), no JSON metrics")
-    ap.add_argument("--pdl", type=int, default=0, choices=[0, 1, 2],
-                    help="programmatic dependent launch mode (lc_set_dependent_launch)")
+    ap.add_argument("--pdl", type=int, default=2, choices=[0, 1, 2],
+                    help="programmatic dependent launch mode (lc_set_dependent_launch); the "
+                         "step satisfies mode 2's contract: between layers nothing writes the "
+                         "context lengths, tables or the next layer's cached pages")
     ap.add_argument("--unfused", action="store_true",
                     help="two launches per layer (lc_rope_append, lc_paged_decode)")
     ap.add_argument("--partition", type=int, default=None,

@@ -70,8 +70,11 @@ const char *lc_version(void);
  *     scheduled while the preceding grid in the stream retires and waits for
  *     it (griddepcontrol.wait) before reading or writing any memory;
  *   2 as 1, but the grid reads the context lengths and computes its split
- *     before that wait: the kernel launched just before it on the stream must
- *     not write the context lengths (positions) it is given.
+ *     before that wait, and lc_rope_append_decode also reads block tables and
+ *     starts loading this layer's cached K/V pages before it. The kernel
+ *     launched just before on the same stream must then not write the context
+ *     lengths, the block tables, or this layer's cached K/V (a decode step's
+ *     QKV projection or another layer's attention qualifies).
  * Returns the previous mode, or -1 for an invalid mode. */
 int lc_set_dependent_launch(int mode);
 

@@ -93,7 +93,12 @@ struct DecodeParams {
     int seg_per_seq;  // num_kv_heads * ctas_per_kv
     int partition_tokens;
     float scale_log2;  // sm_scale * log2(e)
-    int early_setup;   // read context lengths before waiting for the preceding grid
+    // Programmatic dependent launch (lc_set_dependent_launch): 1 = every warp
+    // waits for the preceding grid first; 2 = set-up (context lengths, split)
+    // runs before that wait, and in the fused kernel the producer warp, which
+    // only reads context lengths, block tables and this layer's cached pages,
+    // never waits: its first stages land while the preceding grid drains.
+    int pdl_mode;
     float *ws_o;       // [slots][8][HD]
     float *ws_lse;     // [slots][8]
     int *ws_cnt;       // [batch * seg_per_seq]
@@ -247,6 +252,17 @@ __device__ __forceinline__ int seq_tokens(const DecodeParams &p, int b, bool rep
     return n;
 }
 
+// Sequences without cached tokens own no pages: their output rows are zero.
+// CTA `first` of `count` zeroes sequences first, first + count, ...
+template <int HD>
+__device__ __forceinline__ void zero_empty_outputs(const DecodeParams &p, int first, int count,
+                                                   int t, int nthreads) {
+    for (int b = first; b < p.batch; b += count)
+        if (seq_tokens(p, b, false) == 0)
+            for (int i = t; i < p.num_q_heads * HD; i += nthreads)
+                p.out[(int64_t)b * p.out_stride + i] = __float2bfloat16(0.f);
+}
+
 // Owner CTA of global page x under the balanced split start(c) = c*T/C.
 __device__ __forceinline__ int owner_cta(long long x, long long T, int C) {
     return (int)(((x + 1) * C - 1) / T);
@@ -350,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     // stream be scheduled as our CTAs retire, and wait for the preceding grid
     // before touching its outputs.
     griddep_launch_dependents();
-    if (!p.early_setup) griddep_wait();
+    if (p.pdl_mode == 1) griddep_wait();
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
     // Set-up scan scratch: the head of the stage ring, free until the first TMA.
@@ -362,12 +378,6 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     long long mine = 0;
     for (int b = bs; b < be; ++b) mine += (seq_tokens(p, b, false) + kBlockSize - 1) / kBlockSize;
     s_part[tid] = mine;
-    if (p.early_setup) griddep_wait();
-    for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
-        if (seq_tokens(p, b, false) == 0)
-            for (int i = tid; i < p.num_q_heads * HD; i += kThreads)
-                p.out[(int64_t)b * p.out_stride + i] = __float2bfloat16(0.f);
-    }
     __syncthreads();
     if (warp == 0) {  // exclusive scan of the kThreads partial sums
         constexpr int kPer = kThreads / 32;
@@ -394,7 +404,11 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     }
     __syncthreads();
     const long long T = s_total * G;
-    if (T == 0) return;
+    if (T == 0) {  // every sequence is empty: zero outputs, nothing else
+        if (p.pdl_mode == 2) griddep_wait();
+        zero_empty_outputs<HD>(p, blockIdx.x, gridDim.x, tid, kThreads);
+        return;
+    }
     int C = gridDim.x;
     {
         // Auto: at least kMinPagesPerCta pages per CTA, so that a short batch is
@@ -445,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------------ producer --
+        if (p.pdl_mode == 2 && !FUSED) griddep_wait();
         if (lane == 0) {
             prefetch_tensormap(&tmap_k);
             prefetch_tensormap(&tmap_v);
@@ -572,6 +587,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         // bf16 output (whole segment) or a partial plus, for the last chunk of a
         // split segment to arrive, the log-sum-exp merge of all its partials.
         constexpr int KD = HD / 32;  // head dims per lane
+        if (p.pdl_mode == 2) griddep_wait();
+        zero_empty_outputs<HD>(p, cta, C, lane, 32);
         for (int k = 0;; ++k) {
             if (!mbar_wait_bounded(&epi_full, k & 1, &s_abort, p.status)) break;
             const EpiInfo e = epi;
@@ -704,6 +721,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     const int mi = lane >> 3, r8 = lane & 7;
     const int k_row = (mi & 1) * 8 + r8, k_chunk = mi >> 1;  // QK A operand (K tile)
     const int v_row = (mi >> 1) * 8 + r8, v_chunk = mi & 1;  // PV A operand (V^T tile)
+    if (p.pdl_mode == 2) griddep_wait();
     uint32_t qf[KSTEPS][2];
     uint32_t fin_phase = 0;
     int chunk_idx = 0;  // chunks handed to the epilogue so far
@@ -914,7 +932,7 @@ int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const v
     if (rc) return rc;
     const int mode = dependent_launch_mode();
     DecodeParams prm2 = prm;
-    prm2.early_setup = mode == 2;
+    prm2.pdl_mode = mode;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);

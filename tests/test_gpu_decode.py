@@ -215,3 +215,11 @@ def test_flash_decoding_reference_shape():
         ref = O.flash_decoding(case.q[0], case.k_pool, case.v_pool, case.tables[0], case.layer,
                                hq, hkv, hd, pos, case.num_layers)
         assert max_err(from_device(out), ref) <= ATTN_ATOL
+
+
+def test_decode_all_sequences_empty():
+    case = make_case(5, 14, 2, 64, [0, 0, 0, 0, 0], seed=2)
+    d = dev_case(case)
+    out = torch.full((5, 14 * 64), 7.0, dtype=torch.bfloat16, device="cuda")
+    gpu_decode(case, d=d, out=out)
+    assert not out.any()
