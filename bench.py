@@ -128,9 +128,12 @@ class ClockSampler:
 class Workload:
     """Synthetic paged decode batch for one rank, resident on the GPU."""
 
-    def __init__(self, cfg_name: str, rank: int, world: int, device, seed: int = 1234):
+    def __init__(self, cfg_name: str, rank: int, world: int, device, seed: int = 1234,
+                 layers: int | None = None):
         (self.label, self.batch_per_rank, self.hq, self.hkv, self.hd, self.layers, ctx_spec,
          self.ptok) = CONFIGS[cfg_name]
+        if layers:
+            self.layers = layers
         self.cfg_name = cfg_name
         rng = np.random.default_rng(seed)
         global_batch = self.batch_per_rank * world
@@ -316,7 +319,7 @@ def run_ours(args, rank, world, local):
                                 device_id=device)
     import lucciola as L
     L.set_dependent_launch(args.pdl)
-    w = Workload(args.config, rank, world, device)
+    w = Workload(args.config, rank, world, device, layers=args.layers)
     if args.partition is not None:
         w.ptok = args.partition
     runner = OursStep(w, fused=not args.unfused)
@@ -435,7 +438,11 @@ def run_ours(args, rank, world, local):
                          "traffic": TRAFFIC.get(args.config),
                          "kernel": "paged_decode_kernel<%d,%s>" % (w.hd, "fused" if runner.fused else "plain"),
                          "peak_kind": f"{peak_kind} (burst copy)",
-                         "launch_ms": round(dec_ms, 5)},
+                         "launch_ms": round(dec_ms, 5),
+                         "launch_timing": "CUDA events around single launches (no overlap "
+                                          "with the neighbouring layers)",
+                         "achieved_in_step": round(w.kv_bytes_per_step / (ms_step * 1e-3) / 1e9, 1),
+                         "frac_in_step": round(w.kv_bytes_per_step / (ms_step * 1e-3) / 1e9 / peak, 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(w.h2d_bytes), "d2h_bytes_per_step": int(w.d2h_bytes),
                     "ms_per_step": round(e2e_ms_step, 5)},
@@ -453,9 +460,10 @@ def run_ours(args, rank, world, local):
         dist.destroy_process_group()
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per paged_decode launch from the
-# committed ncu capture (profiles/), scaled to the bench's launch; None until captured.
-TRAFFIC: dict = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one fused decode launch of the
+# bench workload, from the ncu captures summarised in profiles/paged_decode_c2.md
+# and profiles/paged_decode_c3.md (same per-launch work as the bench's launches).
+TRAFFIC: dict = {"c2": 76229632, "c3": 543334400}
 
 
 # ------------------------------------------------------------ reference arm --
@@ -563,6 +571,8 @@ def main():
                     help="programmatic dependent launch mode (lc_set_dependent_launch); the "
                          "step satisfies mode 2's contract: between layers nothing writes the "
                          "context lengths, tables or the next layer's cached pages")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="kernel mode only: fewer layers (smaller pools) for profiler captures")
     ap.add_argument("--unfused", action="store_true",
                     help="two launches per layer (lc_rope_append, lc_paged_decode)")
     ap.add_argument("--partition", type=int, default=None,
@@ -570,6 +580,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.layers is not None and args.mode != "kernel":
+        ap.error("--layers changes the workload; it is for --mode kernel (profiling) only")
     rank, world, local = env_dist()
     if args.impl == "reference":
         run_reference(args, rank, world, local)
