@@ -171,3 +171,25 @@ extern "C" int lc_set_dependent_launch(int mode) {
     if (mode < 0 || mode > 2) return -1;
     return lc::g_dependent_launch.exchange(mode);
 }
+
+namespace lc {
+
+// 2-D bf16 tensor map [rows][inner] (row pitch `row_bytes`), box {box_inner,
+// box_rows}, 128-byte swizzle, zero fill out of bounds. Not cached.
+int tensor_map_2d_sw128(const void *base, int64_t inner, int64_t rows, int64_t row_bytes,
+                        int box_inner, int box_rows, CUtensorMap *out) {
+    if (!aligned16(base) || (row_bytes & 15)) return LC_ERR_MISALIGNED;
+    if (inner <= 0 || rows <= 0 || rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
+    auto fn = encode_fn();
+    if (!fn) return LC_ERR_NOT_SUPPORTED;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? LC_OK : LC_ERR_CUDA;
+}
+
+}  // namespace lc

@@ -28,6 +28,11 @@ int pool_tensor_map(const void *pool, int64_t rows, int head_dim, CUtensorMap *o
 // The same map encoded without the cache (no host allocation).
 int pool_tensor_map_nocache(const void *pool, int64_t rows, int head_dim, CUtensorMap *out);
 
+// 2-D bf16 tensor map [rows][inner] with row pitch `row_bytes`, box
+// {box_inner, box_rows}, 128-byte swizzle, zero fill out of bounds (uncached).
+int tensor_map_2d_sw128(const void *base, int64_t inner, int64_t rows, int64_t row_bytes,
+                        int box_inner, int box_rows, CUtensorMap *out);
+
 // Applies cudaFuncAttributeMaxDynamicSharedMemorySize once per (function, device).
 int ensure_smem_attr(const void *func, int bytes);
 

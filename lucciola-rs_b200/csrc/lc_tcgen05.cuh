@@ -1,0 +1,127 @@
+// lc_tcgen05.cuh - 5th-generation tensor core (tcgen05) and tensor memory
+// (TMEM) helpers for sm_100a: allocation, shared-memory matrix descriptors,
+// the bf16 MMA with fp32 accumulation in TMEM, commits to mbarriers, and
+// TMEM <-> register moves. Used by the causal prefill kernel.
+#pragma once
+
+#include "lc_common.cuh"
+
+namespace lc {
+
+// ------------------------------------------------------------------ TMEM ----
+// Allocates `ncols` TMEM columns (power of two >= 32) for this CTA; one whole
+// warp executes it; the TMEM address is written to *smem_dst.
+__device__ inline void tmem_alloc(uint32_t *smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ inline void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ inline void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
+// Orders tcgen05 operations around thread synchronisation (mbarrier waits,
+// barriers): "before" ahead of the arrive, "after" behind the wait.
+__device__ inline void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ inline void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (tensor-core operand reads, TMA).
+__device__ inline void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------- descriptors --
+// Shared-memory matrix descriptor for a 128-byte-swizzled operand tile (the
+// layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B; tiles 1024-byte aligned).
+//   K-major (rows of 64 bf16 = 128 B, 8-row groups 1024 B apart):
+//       lbo = 16, sbo = 1024
+//   MN-major (64 contiguous elements = 128 B per K row; 8 K rows per 1024 B
+//   group; the next 64-element MN block `lbo` bytes further):
+//       lbo = distance between MN blocks, sbo = 1024
+// Fields: start address >> 4 (bits 0-13), leading byte offset >> 4 (16-29),
+// stride byte offset >> 4 (32-45), version 1 (46-47), base offset 0,
+// layout type 2 = 128-byte swizzle (61-63).
+__device__ inline uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: bf16 A and B, fp32 D,
+// M x N, A K-major, B K-major (b_mn_major = 0) or MN-major (1).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int b_mn_major) {
+    return (1u << 4)                            // D format: f32
+           | (1u << 7)                          // A format: bf16
+           | (1u << 10)                         // B format: bf16
+           | ((uint32_t)b_mn_major << 16)       // B major
+           | ((uint32_t)(N >> 3) << 17)         // N / 8
+           | ((uint32_t)(M >> 4) << 24);        // M / 16
+}
+
+// ------------------------------------------------------------------- MMA ----
+// D[tmem] (+)= A[smem] * B[smem]^T, one elected thread issues it.
+__device__ inline void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                 uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrives (once) on `bar` when every tcgen05 operation this thread issued so
+// far has completed.
+__device__ inline void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+// ------------------------------------------------------ TMEM <-> registers --
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane
+// (quadrant base + i), columns [col, col + 32).
+__device__ inline void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+        "%30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ inline void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ inline void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ inline void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+}  // namespace lc
