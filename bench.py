@@ -557,13 +557,116 @@ def run_reference(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------ prefill (c4) --
+
+PREFILL = {"c4": ("qwen2.5-1.5b causal prefill into the paged cache (BASELINE config 4)",
+                  4, 12, 2, 128, 28, 4096)}
+
+
+def causal_flops(batch, tokens, hq, hd, start=0):
+    """4*hd flops per (query, visible key, q head): QK^T and PV."""
+    keys = sum(start + i + 1 for i in range(tokens))
+    return 4.0 * batch * keys * hq * hd
+
+
+def run_prefill_bench(args, rank, world, local):
+    import lucciola as L
+    label, B, hq, hkv, hd, layers, T = PREFILL[args.config]
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4321)
+    pages = (T + 15) // 16
+    nb = B * pages + 1
+    perm = torch.randperm(nb, generator=gen, device=device).to(torch.int32)
+    tables = perm[:B * pages].reshape(B, pages).contiguous()
+    shape = (nb, layers, hkv, 16, hd)
+    k_pool = torch.randn(shape, generator=gen, device=device).to(torch.bfloat16)
+    v_pool = torch.randn(shape, generator=gen, device=device).to(torch.bfloat16)
+    row = (hq + 2 * hkv) * hd
+    qkv = torch.randn((layers, B * T, row), generator=gen, device=device).to(torch.bfloat16)
+    bias = (torch.randn((layers, row), generator=gen, device=device) * 0.01).to(torch.bfloat16)
+    qb, kb, vb = (bias[:, :hq * hd].contiguous(), bias[:, hq * hd:(hq + hkv) * hd].contiguous(),
+                  bias[:, (hq + hkv) * hd:].contiguous())
+    cos, sin = (torch.from_numpy(x).to(device) for x in L.rope_table_host(T + 16, hd, 1e6))
+    positions = torch.arange(T, dtype=torch.int32, device=device).repeat(B)
+    start = torch.zeros(B, dtype=torch.int32, device=device)
+    out = torch.empty((layers, B * T, hq * hd), dtype=torch.bfloat16, device=device)
+
+    def layer(l, ev=None):
+        L.rope_append(qkv[l], positions, qb[l], kb[l], vb[l], cos, sin, k_pool, v_pool, nb, layers,
+                      l, hq, hkv, hd, tables, tokens_per_seq=T)
+        if ev is not None:
+            ev[0].record()
+        L.paged_prefill(out[l], qkv[l], k_pool, v_pool, nb, layers, l, hq, hkv, hd, tables, start,
+                        T, 0)
+        if ev is not None:
+            ev[1].record()
+
+    def step():
+        for l in range(layers):
+            layer(l)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=device)):
+        step()
+    sampler = ClockSampler(local)
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        graph.replay()
+        torch.cuda.synchronize()
+    ms_step = time_graph(graph, args.steps, args.warmup, torch.cuda.current_stream()) / args.steps
+    clocks = sampler.stop()
+    # per-launch duration of the prefill kernel (events around each launch)
+    pairs = []
+    torch.cuda._sleep(50_000_000)
+    for l in range(min(layers, 8)):
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        layer(l, ev)
+        pairs.append(ev)
+    torch.cuda.synchronize()
+    launch_ms = sum(a.elapsed_time(b) for a, b in pairs) / len(pairs)
+    flops = causal_flops(B, T, hq, hd)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak_burst = float(peaks.get("bf16_tflops", 1590.0))
+    peak_sust = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    kind = "measured" if peaks else "fallback"
+    achieved = flops / (launch_ms * 1e-3) / 1e12
+    step_tflops = flops * layers / (ms_step * 1e-3) / 1e12
+    line = {
+        "metric": "causal prefill attention TFLOP/s (4 x 4096 tokens, per layer)",
+        "value": round(step_tflops, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded bf16 ~N(0,1) Q/K/V, RoPE theta 1e6)",
+        "config": {"workload": label, "sequences": B, "tokens": T, "q_heads": hq,
+                   "kv_heads": hkv, "head_dim": hd, "layers": layers,
+                   "flops_per_layer": flops,
+                   "step": "per layer: lc_rope_append (prompt rows) + lc_paged_prefill; CUDA graph"},
+        "ms_per_layer": round(ms_step / layers, 4),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_sust,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_sust, 4), "traffic": None,
+                     "kernel": f"paged_prefill_kernel<{hd}>",
+                     "peak_kind": f"{kind} (sustained bf16 GEMM; burst {peak_burst})",
+                     "launch_ms": round(launch_ms, 4)},
+        "gpu_launches": 2 * layers * args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    del graph
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
                     help="kernel: eager launches only (for profilers), no JSON metrics")
@@ -583,6 +686,15 @@ def main():
     if args.layers is not None and args.mode != "kernel":
         ap.error("--layers changes the workload; it is for --mode kernel (profiling) only")
     rank, world, local = env_dist()
+    if args.config in PREFILL:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is run on "
+                              "the decode headline (config 2); its prefill is T sequential "
+                              "decode launches per layer"}))
+            return 0
+        if rank == 0:
+            run_prefill_bench(args, rank, world, local)
+        return 0
     if args.impl == "reference":
         run_reference(args, rank, world, local)
     else:

@@ -44,8 +44,8 @@ struct PrefillCfg {
     static constexpr int kPBytes = kBM * kBN * 2;
     static constexpr int kKOff = kQBytes;
     static constexpr int kVOff = kKOff + kStages * kTileBytes;
-    static constexpr int kPOff = kVOff + kStages * kTileBytes;
-    static constexpr int kSmem = kPOff + kPBytes + 1024;
+    static constexpr int kPOff = kVOff + kStages * kTileBytes;  // two P buffers
+    static constexpr int kSmem = kPOff + 2 * kPBytes + 1024;
     static constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);   // B = K tile, K-major
     static constexpr uint32_t kIdescPV = idesc_bf16_f32(kBM, HD, 1);   // B = V tile, MN-major
 };
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t k_full[S], v_full[S], kv_empty[S];
     __shared__ __align__(8) uint64_t s_full[2], s_free[2];
-    __shared__ __align__(8) uint64_t p_full, pv_done;
+    __shared__ __align__(8) uint64_t p_full[2], pv_done[2];  // per P buffer: tile t uses t % 2
     __shared__ uint32_t tmem_base_sh;
     __shared__ int s_abort;
     extern __shared__ uint8_t smem_raw[];
@@ -118,8 +118,10 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], kBM);
         }
-        mbar_init(&p_full, kBM);
-        mbar_init(&pv_done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&p_full[i], kBM);
+            mbar_init(&pv_done[i], 1);
+        }
         s_abort = 0;
         fence_barrier_init();
     }
@@ -201,18 +203,18 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             };
             auto issue_pv = [&](int t) -> bool {
                 const int s = t % S;
-                if (!mbar_wait_bounded(&p_full, t & 1, &s_abort, p.status)) return false;
+                if (!mbar_wait_bounded(&p_full[t & 1], (t >> 1) & 1, &s_abort, p.status)) return false;
                 if (!mbar_wait_bounded(&v_full[s], (t / S) & 1, &s_abort, p.status)) return false;
                 tc_fence_after();
                 const uint32_t vt = sV + s * Cfg::kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk) {
                     const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16(tmem + 2 * kBN, sw128_desc(sP + aoff, 16, 1024),
+                    umma_bf16(tmem + 2 * kBN, sw128_desc(sP + (t & 1) * Cfg::kPBytes + aoff, 16, 1024),
                               sw128_desc(vt + kk * 2048, 16384, 1024), Cfg::kIdescPV,
                               (t > 0 || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(&pv_done);
+                umma_commit(&pv_done[t & 1]);
                 umma_commit(&kv_empty[s]);
                 return true;
             };
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             for (int j = 1; j < nkv && ok; ++j) ok = issue_s(j) && issue_pv(j - 1);
             if (ok) ok = issue_pv(nkv - 1);
             // Let every MMA this thread issued finish before the teardown.
-            if (ok) mbar_wait_bounded(&pv_done, (nkv - 1) & 1, &s_abort, p.status);
+            if (ok) mbar_wait_bounded(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, &s_abort, p.status);
         }
     } else {
         // -------------------------------------------------------- softmax --
@@ -238,64 +240,87 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             }
             tc_fence_after();
             float sv[kBN];
+            {
+                uint32_t r[kBN / 32][32];
 #pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tl + (j & 1) * kBN + 32 * c, r);
+                for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tl + (j & 1) * kBN + 32 * c, r[c]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; ++i) sv[32 * c + i] = u2f(r[i]);
+                for (int c = 0; c < kBN / 32; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) sv[32 * c + i] = u2f(r[c][i]);
             }
             tc_fence_before();
             mbar_arrive(&s_free[j & 1]);
             const int key0 = j * kBN;
-            float mt = -INFINITY;
+            // Causal mask only on tiles that reach past the tile's first query.
+            if (key0 + kBN - 1 > start + q0) {
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) {
-                const float x = key0 + c <= q_pos ? sv[c] * p.scale_log2 : -INFINITY;
-                sv[c] = x;
-                mt = fmaxf(mt, x);
+                for (int c = 0; c < kBN; ++c)
+                    if (key0 + c > q_pos) sv[c] = -INFINITY;
             }
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+            for (int c = 0; c < kBN; ++c) mx[c & 3] = fmaxf(mx[c & 3], sv[c]);
+            // raw scores: scale > 0 keeps the order, so scale the max only
+            const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
+            // Running max with lazy rescaling: keep the reference max unless the
+            // tile's max exceeds it by more than 2^8; then O and l are rescaled.
+            float alpha = 1.f;
+            bool rescale = false;
             if (j == 0) {
                 m_ref = mt;
-            } else {
-                if (!mbar_wait_bounded(&pv_done, (j - 1) & 1, &s_abort, p.status)) {
+            } else if (mt > m_ref + kRescaleLog2) {
+                alpha = fast_exp2f(m_ref - mt);
+                m_ref = mt;
+                rescale = true;
+            }
+            // P = 2^(s * scale - m_ref) (masked keys give 0): one FFMA and one
+            // ex2 per score, computed before any wait.
+            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+            const float neg_m = -m_ref;
+#pragma unroll
+            for (int c = 0; c < kBN; ++c) {
+                sv[c] = fast_exp2f(fmaf(sv[c], p.scale_log2, neg_m));
+                rs[c & 3] += sv[c];
+            }
+            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            // P buffer j % 2 is free once PV_{j-2} is done; O may be rescaled
+            // only after PV_{j-1}.
+            if (j >= 2 &&
+                !mbar_wait_bounded(&pv_done[j & 1], ((j - 2) >> 1) & 1, &s_abort, p.status)) {
+                ok = false;
+                break;
+            }
+            const bool warp_rescale = __any_sync(0xffffffffu, rescale);
+            if (warp_rescale) {
+                if (!mbar_wait_bounded(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &s_abort,
+                                       p.status)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const bool need = mt > m_ref + kRescaleLog2;
-                if (__any_sync(0xffffffffu, need)) {
-                    const float m_new = need ? mt : m_ref;
-                    const float alpha = fast_exp2f(m_ref - m_new);
 #pragma unroll
-                    for (int c = 0; c < HD / 32; ++c) {
-                        uint32_t r[32];
-                        tmem_ld32(tl + 2 * kBN + 32 * c, r);
-                        tmem_wait_ld();
+                for (int c = 0; c < HD / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tl + 2 * kBN + 32 * c, r);
+                    tmem_wait_ld();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) r[i] = f2u(u2f(r[i]) * alpha);
-                        tmem_st32(tl + 2 * kBN + 32 * c, r);
-                    }
-                    tmem_wait_st();
-                    l *= alpha;
-                    m_ref = m_new;
+                    for (int i = 0; i < 32; ++i) r[i] = f2u(u2f(r[i]) * alpha);
+                    tmem_st32(tl + 2 * kBN + 32 * c, r);
                 }
+                tmem_wait_st();
             }
-            // P row = 2^(s - m_ref) in bf16, 128-byte swizzled, K-major (keys).
+            // P row in bf16, 128-byte swizzled, K-major (keys).
+            uint8_t *pb = gen + Cfg::kPOff + (j & 1) * Cfg::kPBytes;
 #pragma unroll
             for (int c16 = 0; c16 < kBN / 8; ++c16) {
                 uint32_t w[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = fast_exp2f(sv[8 * c16 + 2 * e] - m_ref);
-                    const float p1 = fast_exp2f(sv[8 * c16 + 2 * e + 1] - m_ref);
-                    l += p0 + p1;
-                    w[e] = pack_bf16(p0, p1);
-                }
+                for (int e = 0; e < 4; ++e) w[e] = pack_bf16(sv[8 * c16 + 2 * e], sv[8 * c16 + 2 * e + 1]);
                 const int hh = c16 >> 3, cc = c16 & 7;
-                *reinterpret_cast<uint4 *>(gen + Cfg::kPOff + hh * 16384 + row * 128 +
-                                           ((cc ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4 *>(pb + hh * 16384 + row * 128 + ((cc ^ (row & 7)) << 4)) =
+                    make_uint4(w[0], w[1], w[2], w[3]);
             }
             // Keys past the prompt end in the last tile: zero their V rows so
             // that 0 * (stale or non-finite pool contents) cannot reach O.
@@ -317,10 +342,11 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(&p_full);
+            mbar_arrive(&p_full[j & 1]);
         }
         // ----------------------------------------------------- epilogue --
-        if (ok && mbar_wait_bounded(&pv_done, (nkv - 1) & 1, &s_abort, p.status)) {
+        if (ok && mbar_wait_bounded(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, &s_abort,
+                                    p.status)) {
             tc_fence_after();
             const float inv = 1.f / l;
             bf16 *orow = p.out + (int64_t)(b * p.tokens + q_idx) * p.out_stride + (int64_t)h * HD;
