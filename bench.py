@@ -557,6 +557,135 @@ def run_reference(args, rank, world, local):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------- head-sharded decode (c5) --
+
+HEAD_SHARDED = {"c5": ("qwen2.5-72b decode sharded by kv head (BASELINE config 5)", 128, 64, 8,
+                       128, 80, ("uniform", 1024, 32768))}
+
+
+def run_head_sharded(args, rank, world, local):
+    """KV-head sharding: rank r owns kv heads [r*8/N, (r+1)*8/N) of every layer
+    (identical block tables everywhere), runs the fused decode on its heads, and
+    an NCCL all-gather assembles [B][Hq][hd]. Two physical layers alternate;
+    tokens/s is extrapolated to the model's 80 layers (attention only)."""
+    import lucciola as L
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    L.set_dependent_launch(args.pdl)
+    label, B, hq, hkv, hd, model_layers, spec = HEAD_SHARDED[args.config]
+    first, nloc = L.shard_kv_heads(hq, hkv, world, rank)
+    hq_loc = nloc * (hq // hkv)
+    rng = np.random.default_rng(5150)            # identical lengths and tables on every rank
+    ctx = rng.integers(spec[1], spec[2] + 1, B).astype(np.int32)
+    pages = (ctx + 1 + 15) // 16
+    nb = int(pages.sum()) + 1
+    perm = rng.permutation(nb).astype(np.int32)
+    tables_np = np.full((B, int(pages.max())), -1, np.int32)
+    off = 0
+    for b, n in enumerate(pages):
+        tables_np[b, :n] = perm[off:off + n]
+        off += n
+    tables = torch.from_numpy(tables_np).to(device)
+    positions = torch.from_numpy(ctx).to(device)
+    layers = 2
+    gen = torch.Generator(device=device)
+    gen.manual_seed(77 + rank)
+    shape = (nb, layers, nloc, 16, hd)
+    k_pool = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    v_pool = torch.empty(shape, dtype=torch.bfloat16, device=device)
+    for t in (k_pool, v_pool):
+        flat = t.view(-1)
+        for i in range(0, flat.numel(), 1 << 28):
+            chunk = flat[i:i + (1 << 28)]
+            chunk.copy_(torch.randn(chunk.numel(), generator=gen, device=device).to(torch.bfloat16))
+    row = (hq_loc + 2 * nloc) * hd
+    qkv = torch.randn((layers, B, row), generator=gen, device=device).to(torch.bfloat16)
+    bias = (torch.randn((layers, row), generator=gen, device=device) * 0.01).to(torch.bfloat16)
+    qb = bias[:, :hq_loc * hd].contiguous()
+    kb = bias[:, hq_loc * hd:(hq_loc + nloc) * hd].contiguous()
+    vb = bias[:, (hq_loc + nloc) * hd:].contiguous()
+    cos, sin = (torch.from_numpy(x).to(device) for x in L.rope_table_host(32768 + 16, hd, 1e6))
+    out_loc = torch.empty((layers, B, hq_loc * hd), dtype=torch.bfloat16, device=device)
+    gathered = torch.empty((layers, world * B, hq_loc * hd), dtype=torch.bfloat16, device=device)
+    full = torch.empty((layers, B, hq * hd), dtype=torch.bfloat16, device=device)
+    ws = L.alloc_decode_workspace(B, hq_loc, nloc, hd, device=device)
+    max_ctx = int(ctx.max()) + 1
+
+    def step():
+        for l in range(layers):
+            L.rope_append_decode(out_loc[l], qkv[l], positions, qb[l], kb[l], vb[l], cos, sin,
+                                 k_pool, v_pool, nb, layers, l, hq_loc, nloc, hd, tables, max_ctx,
+                                 workspace=ws)
+            if dist:
+                dist.all_gather_into_tensor(gathered[l], out_loc[l])
+                full[l].copy_(L.assemble_head_shards(gathered[l], world))
+            else:
+                full[l].copy_(out_loc[l])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    t_end = time.perf_counter() + 1.0  # clocks settle under this load; sampled meanwhile
+    while time.perf_counter() < t_end:
+        step()
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_step = e0.elapsed_time(e1) / args.steps
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    kv_bytes_rank = float((ctx.astype(np.int64) + 1).sum()) * nloc * hd * 2 * 2 * layers
+    vals = torch.tensor([ms_step, kv_bytes_rank], dtype=torch.float64, device=device)
+    if dist:
+        mx = vals[:1].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = vals[1:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms_step, kv_bytes_all = mx.item(), tot.item()
+    else:
+        kv_bytes_all = kv_bytes_rank
+    if rank == 0:
+        peak, kind = measured_peak()
+        t_layer = ms_step / layers
+        value = kv_bytes_all / (ms_step * 1e-3) / 1e9
+        print(json.dumps({
+            "metric": "decode-attn KV GB/s (KV-head sharded) and tokens/s, attention-only, "
+                      "80-layer extrapolated",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded bf16 ~N(0,1), uniform context lengths)",
+            "config": {"workload": label, "batch": B, "q_heads": hq, "kv_heads": hkv,
+                       "head_dim": hd, "kv_heads_per_gpu": nloc, "physical_layers": layers,
+                       "kv_tokens": int(ctx.sum() + B),
+                       "parallelism": f"kv-head sharded x{world}, NCCL all-gather of outputs",
+                       "step": "per layer: lc_rope_append_decode on local heads, "
+                               "all_gather_into_tensor, permute to [B][Hq][hd]"},
+            "ms_per_layer": round(t_layer, 4),
+            "tokens_per_s_80_layers": round(B / (model_layers * t_layer * 1e-3), 1),
+            "pct_hbm_per_gpu": round(100 * value / world / peak, 2),
+            "clocks": clocks,
+        }), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------ prefill (c4) --
 
 PREFILL = {"c4": ("qwen2.5-1.5b causal prefill into the paged cache (BASELINE config 4)",
@@ -666,7 +795,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL), default="c2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(HEAD_SHARDED),
+                    default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
                     help="kernel: eager launches only (for profilers), no JSON metrics")
@@ -686,6 +816,14 @@ def main():
     if args.layers is not None and args.mode != "kernel":
         ap.error("--layers changes the workload; it is for --mode kernel (profiling) only")
     rank, world, local = env_dist()
+    if args.config in HEAD_SHARDED:
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference is "
+                                  "single-GPU; its arm is run on the decode headline (config 2)"}))
+            return 0
+        run_head_sharded(args, rank, world, local)
+        return 0
     if args.config in PREFILL:
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference arm is run on "
