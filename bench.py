@@ -631,11 +631,20 @@ def run_head_sharded(args, rank, world, local):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # Clocks settle under this load for about a second, sampled meanwhile. Every
+    # rank runs the same number of steps (each holds a collective): the count
+    # comes from the slowest rank's step time.
+    t0 = time.perf_counter()
+    step()
+    torch.cuda.synchronize()
+    t_one = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(t_one, op=dist.ReduceOp.MAX)
+    n_settle = max(1, min(2000, int(1.0 / max(t_one.item(), 1e-4))))
     sampler = ClockSampler(local) if rank == 0 else None
-    t_end = time.perf_counter() + 1.0  # clocks settle under this load; sampled meanwhile
-    while time.perf_counter() < t_end:
+    for _ in range(n_settle):
         step()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
