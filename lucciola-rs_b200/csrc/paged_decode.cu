@@ -49,11 +49,12 @@ constexpr int kHeadsPerCta = 8;
 constexpr int kPagesPerStage = kConsumerWarps;  // one page per consumer warp per stage
 constexpr int kMinPagesPerCta = 8;               // auto split: two stages per CTA at least
 
-enum : int { kFirst = 1, kLast = 2, kDone = 4 };
+// kFinal marks the last stage of the CTA's whole range.
+enum : int { kFirst = 1, kLast = 2, kDone = 4, kFinal = 8 };
 
 struct StageMeta {
     int b, g, page0, np;    // sequence, segment-in-sequence, first page of the stage, pages
-    int n, pages_b, flags;  // tokens of the sequence, its pages, kFirst/kLast/kDone
+    int n, pages_b, flags;  // tokens of the sequence, its pages, kFirst/kLast/kDone/kFinal
     int chunk_p0, take;     // chunk = pages [chunk_p0, chunk_p0 + take) of the segment
     int pos;                // fused: the new token's position (unclamped)
     long long seg_start;    // global index of the segment's first page
@@ -61,7 +62,7 @@ struct StageMeta {
 
 // Finished chunk handed from the consumer warps to the epilogue warp.
 struct EpiInfo {
-    int b, seg, nh, head0, pages_b, whole, done;
+    int b, seg, nh, head0, pages_b, whole, done, final;
     long long seg_start;
 };
 
@@ -118,127 +119,20 @@ __device__ __forceinline__ uint32_t tile_addr(uint32_t page, int r, int kc) {
     return page + ((kc >> 3) << 11) + (r << 7) + ((((kc & 7) ^ (r & 7))) << 4);
 }
 
-// Fused mode, consumer warp: the B fragments of Q^T for this lane's query head,
-// biased and rotated (rope_math.cuh, the arithmetic of rope_append.cu) straight
-// from the qkv row. A lane's fragments hold dims {16j + 2c, +1, +8, +9} of every
-// 16-dim step j, so the rotation partners d and d + hd/2 (same residue mod 16)
-// are both in the lane: no data moves between lanes.
-template <int HD>
-__device__ __forceinline__ void rope_q_fragments(const DecodeParams &p, int b, int head, bool hv,
-                                                 int pos, int c4, uint32_t (&qf)[HD / 16][2]) {
-    constexpr int half = HD / 2, KH = HD / 32;  // fragment steps per half
-    if (!hv) {
-#pragma unroll
-        for (int j = 0; j < HD / 16; ++j) qf[j][0] = qf[j][1] = 0u;
-        return;
-    }
-    const bf16 *row = p.qkv + (int64_t)b * p.q_stride + (int64_t)head * HD;
-    const bf16 *bias = p.q_bias + (int64_t)head * HD;
-    const bool pos_ok = pos >= 0 && pos < p.rope_rows;
-    const float *ct = p.cos_t + (int64_t)(pos_ok ? pos : 0) * half;
-    const float *st = p.sin_t + (int64_t)(pos_ok ? pos : 0) * half;
-#pragma unroll
-    for (int j = 0; j < KH; ++j) {
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int d = 16 * j + 8 * r + 2 * c4;  // this lane's pair (d, d+1), d < half
-            const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162 *>(row + d);
-            const __nv_bfloat162 x2 = *reinterpret_cast<const __nv_bfloat162 *>(row + d + half);
-            const __nv_bfloat162 b1 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d));
-            const __nv_bfloat162 b2 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d + half));
-            const float2 c = pos_ok ? __ldg(reinterpret_cast<const float2 *>(ct + d)) : make_float2(1.f, 1.f);
-            const float2 sn = pos_ok ? __ldg(reinterpret_cast<const float2 *>(st + d)) : make_float2(0.f, 0.f);
-            const float a0 = __fadd_rn(__low2float(x1), __low2float(b1));
-            const float a1 = __fadd_rn(__high2float(x1), __high2float(b1));
-            const float e0 = __fadd_rn(__low2float(x2), __low2float(b2));
-            const float e1 = __fadd_rn(__high2float(x2), __high2float(b2));
-            const __nv_bfloat162 lo =
-                __halves2bfloat162(__float2bfloat16(rot_sub(a0, c.x, e0, sn.x)),
-                                   __float2bfloat16(rot_sub(a1, c.y, e1, sn.y)));
-            const __nv_bfloat162 hi =
-                __halves2bfloat162(__float2bfloat16(rot_add(a0, sn.x, e0, c.x)),
-                                   __float2bfloat16(rot_add(a1, sn.y, e1, c.y)));
-            qf[j][r] = *reinterpret_cast<const uint32_t *>(&lo);
-            qf[j + KH][r] = *reinterpret_cast<const uint32_t *>(&hi);
-        }
-    }
-}
-
-// Fused mode: raw inputs of the new token's K/V row for one kv head, loaded by
-// the consumer warp that will process its page well before it is needed.
-template <int HD>
-struct NewKvInputs {
-    static constexpr int kPairs = HD / 64;  // rotation pairs per lane
-    __nv_bfloat16 k1[kPairs], k2[kPairs], v1[kPairs], v2[kPairs];
-    __nv_bfloat16 kb1[kPairs], kb2[kPairs], vb1[kPairs], vb2[kPairs];
-    float c[kPairs], s[kPairs];
-    int phys;
-
-    __device__ __forceinline__ void load(const DecodeParams &p, int b, int kvh, int pos,
-                                         int page, int lane) {
-        constexpr int half = HD / 2;
-        const bf16 *row = p.qkv + (int64_t)b * p.q_stride;
-        const int ko = p.num_q_heads * HD + kvh * HD, vo = ko + p.num_kv_heads * HD;
-        const bool pos_ok = pos < p.rope_rows;
-#pragma unroll
-        for (int i = 0; i < kPairs; ++i) {
-            const int d = lane + 32 * i;
-            k1[i] = row[ko + d];
-            k2[i] = row[ko + d + half];
-            v1[i] = row[vo + d];
-            v2[i] = row[vo + d + half];
-            kb1[i] = p.k_bias[kvh * HD + d];
-            kb2[i] = p.k_bias[kvh * HD + d + half];
-            vb1[i] = p.v_bias[kvh * HD + d];
-            vb2[i] = p.v_bias[kvh * HD + d + half];
-            c[i] = pos_ok ? __ldg(p.cos_t + (int64_t)pos * half + d) : 1.f;
-            s[i] = pos_ok ? __ldg(p.sin_t + (int64_t)pos * half + d) : 0.f;
-        }
-        phys = __ldg(p.tables + (int64_t)b * p.table_stride + page);
-    }
-
-    // Rotated k and v + bias (the arithmetic of rope_append.cu): patched into
-    // row `r` of the page tiles in shared memory and, when `append`, written to
-    // the pools at position `pos`.
-    __device__ __forceinline__ void apply(const DecodeParams &p, int kvh, int pos, bool append,
-                                          uint8_t *smem_gen, uint32_t smem_base, uint32_t kpage,
-                                          uint32_t vpage, int r, int lane) {
-        constexpr int half = HD / 2;
-        const bool ph_ok = phys >= 0 && phys < p.num_blocks;
-        const int64_t dst = page_row(ph_ok ? phys : 0, p.layer, kvh, p.num_layers,
-                                     p.num_kv_heads) * HD + (int64_t)(pos % kBlockSize) * HD;
-#pragma unroll
-        for (int i = 0; i < kPairs; ++i) {
-            const int d = lane + 32 * i;
-            const float a1 = __fadd_rn(__bfloat162float(k1[i]), __bfloat162float(kb1[i]));
-            const float a2 = __fadd_rn(__bfloat162float(k2[i]), __bfloat162float(kb2[i]));
-            const bf16 rk1 = __float2bfloat16(rot_sub(a1, c[i], a2, s[i]));
-            const bf16 rk2 = __float2bfloat16(rot_add(a1, s[i], a2, c[i]));
-            const bf16 rv1 = __float2bfloat16(__fadd_rn(__bfloat162float(v1[i]), __bfloat162float(vb1[i])));
-            const bf16 rv2 = __float2bfloat16(__fadd_rn(__bfloat162float(v2[i]), __bfloat162float(vb2[i])));
-            // element d of row r sits in 16-byte chunk d/8 of the swizzled tile
-            auto put = [&](uint32_t tile, int dd, bf16 v) {
-                *reinterpret_cast<bf16 *>(smem_gen + (tile_addr(tile, r, dd >> 3) - smem_base) +
-                                          (dd & 7) * 2) = v;
-            };
-            put(kpage, d, rk1);
-            put(kpage, d + half, rk2);
-            put(vpage, d, rv1);
-            put(vpage, d + half, rv2);
-            if (append && ph_ok) {
-                p.k_pool_w[dst + d] = rk1;
-                p.k_pool_w[dst + d + half] = rk2;
-                p.v_pool_w[dst + d] = rv1;
-                p.v_pool_w[dst + d + half] = rv2;
-            }
-        }
-    }
-};
-
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+__device__ __forceinline__ int atom_add_acquire_gpu(int *addr, int v) {
+    int old;
+    asm volatile("atom.acquire.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
 }
 
 __device__ __forceinline__ int seq_tokens(const DecodeParams &p, int b, bool report) {
@@ -250,6 +144,173 @@ __device__ __forceinline__ int seq_tokens(const DecodeParams &p, int b, bool rep
         n = cap;
     }
     return n;
+}
+
+// One chunk: the pages [p0, p0 + take) of segment g of sequence b that a CTA's
+// range covers.
+struct Chunk {
+    int b, g, p0, take, n, pages_b;
+    long long seg_start;  // global index of the segment's first page
+};
+
+// Walks the chunks of the range [start, end) of the global page stream in
+// order. The producer warp and, in the fused kernel, the epilogue warp each run
+// one, so both see the same chunk sequence.
+struct ChunkCursor {
+    int b, g, pg, n, pages_b;
+    long long glob;
+
+    __device__ __forceinline__ void init(const DecodeParams &p, long long start, int b0,
+                                         long long pref_b0, bool report) {
+        b = b0;
+        n = seq_tokens(p, b, report);
+        pages_b = (n + kBlockSize - 1) / kBlockSize;  // > 0: b0 holds page `start`
+        const long long off = start - pref_b0;
+        g = (int)(off / pages_b);
+        pg = (int)(off - (long long)g * pages_b);
+        glob = start;
+    }
+
+    __device__ __forceinline__ bool next(const DecodeParams &p, long long end, bool report,
+                                         Chunk &c) {
+        while (glob < end) {
+            if (pages_b == 0) {  // empty sequence: owns no pages
+                ++b;
+                n = seq_tokens(p, b, report);
+                pages_b = (n + kBlockSize - 1) / kBlockSize;
+                continue;
+            }
+            c.b = b;
+            c.g = g;
+            c.p0 = pg;
+            c.n = n;
+            c.pages_b = pages_b;
+            c.take = (int)min((long long)(pages_b - pg), end - glob);
+            c.seg_start = glob - pg;
+            glob += c.take;
+            pg = 0;
+            if (++g == p.seg_per_seq) {
+                g = 0;
+                ++b;
+                if (glob < end) {
+                    n = seq_tokens(p, b, report);
+                    pages_b = (n + kBlockSize - 1) / kBlockSize;
+                }
+            }
+            return true;
+        }
+        return false;
+    }
+};
+
+// Fused mode, epilogue warp: everything a chunk needs from the qkv rows, made
+// ahead of the consumer warps (signalled on `ready`):
+//  * q of the chunk's <= 8 query heads, bias added and rotated, bf16 [8][HD]
+//    in `qs` (zeros for heads past the group);
+//  * when the chunk ends with the sequence's new token: its rotated K row and
+//    V + bias row, bf16 [2][HD] in `nk`, which the consumer warp holding that
+//    page writes over the tile row; the first 8-head slice of the kv head also
+//    appends both rows to the pools here.
+// The arithmetic is that of rope_append.cu (rope_math.cuh), so q, the tile
+// rows and the pool writes equal the two-launch path's bit for bit.
+template <int HD>
+__device__ __forceinline__ void prepare_chunk(const DecodeParams &p, const Chunk &c, bf16 *qs,
+                                              bf16 *nk, uint64_t *ready, int lane) {
+    constexpr int half = HD / 2;
+    const int kvh = c.g / p.ctas_per_kv;
+    const int hsub = c.g - kvh * p.ctas_per_kv;
+    const int head0 = kvh * p.group + hsub * kHeadsPerCta;
+    const int nh = min(kHeadsPerCta, p.group - hsub * kHeadsPerCta);
+    const int pos = __ldg(p.ctx_lens + c.b) + p.len_offset - 1;
+    const bool pos_ok = pos >= 0 && pos < p.rope_rows;
+    const float *ct = p.cos_t + (int64_t)(pos_ok ? pos : 0) * half;
+    const float *sn = p.sin_t + (int64_t)(pos_ok ? pos : 0) * half;
+    const bf16 *qkv_row = p.qkv + (int64_t)c.b * p.q_stride;
+    {
+        // lane -> head lane / 4, rotation pairs (d, d + half) for d in its quarter
+        constexpr int kPer = half / 4;
+        const int h = lane >> 2, d0 = (lane & 3) * kPer;
+        bf16 *dst = qs + h * HD;
+        if (h < nh) {
+            const bf16 *row = qkv_row + (int64_t)(head0 + h) * HD;
+            const bf16 *bias = p.q_bias + (int64_t)(head0 + h) * HD;
+#pragma unroll
+            for (int i = 0; i < kPer; i += 2) {
+                const int d = d0 + i;
+                const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162 *>(row + d);
+                const __nv_bfloat162 x2 = *reinterpret_cast<const __nv_bfloat162 *>(row + d + half);
+                const __nv_bfloat162 b1 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d));
+                const __nv_bfloat162 b2 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d + half));
+                const float2 cs = pos_ok ? __ldg(reinterpret_cast<const float2 *>(ct + d)) : make_float2(1.f, 1.f);
+                const float2 sv = pos_ok ? __ldg(reinterpret_cast<const float2 *>(sn + d)) : make_float2(0.f, 0.f);
+                const float a0 = __fadd_rn(__low2float(x1), __low2float(b1));
+                const float a1 = __fadd_rn(__high2float(x1), __high2float(b1));
+                const float e0 = __fadd_rn(__low2float(x2), __low2float(b2));
+                const float e1 = __fadd_rn(__high2float(x2), __high2float(b2));
+                *reinterpret_cast<__nv_bfloat162 *>(dst + d) =
+                    __halves2bfloat162(__float2bfloat16(rot_sub(a0, cs.x, e0, sv.x)),
+                                       __float2bfloat16(rot_sub(a1, cs.y, e1, sv.y)));
+                *reinterpret_cast<__nv_bfloat162 *>(dst + d + half) =
+                    __halves2bfloat162(__float2bfloat16(rot_add(a0, sv.x, e0, cs.x)),
+                                       __float2bfloat16(rot_add(a1, sv.y, e1, cs.y)));
+            }
+        } else {
+            const __nv_bfloat162 z = __float2bfloat162_rn(0.f);
+#pragma unroll
+            for (int i = 0; i < kPer; i += 2) {
+                *reinterpret_cast<__nv_bfloat162 *>(dst + d0 + i) = z;
+                *reinterpret_cast<__nv_bfloat162 *>(dst + d0 + i + half) = z;
+            }
+        }
+    }
+    if (pos == c.n - 1 && c.p0 + c.take == c.pages_b) {
+        const int ko = p.num_q_heads * HD + kvh * HD, vo = ko + p.num_kv_heads * HD;
+        const bool append = hsub == 0;
+        const int phys = __ldg(p.tables + (int64_t)c.b * p.table_stride + c.pages_b - 1);
+        const bool ph_ok = phys >= 0 && phys < p.num_blocks;
+        const int64_t dst = page_row(ph_ok ? phys : 0, p.layer, kvh, p.num_layers, p.num_kv_heads) * HD +
+                            (int64_t)(pos % kBlockSize) * HD;
+#pragma unroll
+        for (int i = 0; i < HD / 64; ++i) {
+            const int d = lane + 32 * i;
+            const float a1 = __fadd_rn(__bfloat162float(qkv_row[ko + d]), __bfloat162float(p.k_bias[kvh * HD + d]));
+            const float a2 = __fadd_rn(__bfloat162float(qkv_row[ko + d + half]),
+                                       __bfloat162float(p.k_bias[kvh * HD + d + half]));
+            const float cv = pos_ok ? __ldg(ct + d) : 1.f, sv = pos_ok ? __ldg(sn + d) : 0.f;
+            const bf16 rk1 = __float2bfloat16(rot_sub(a1, cv, a2, sv));
+            const bf16 rk2 = __float2bfloat16(rot_add(a1, sv, a2, cv));
+            const bf16 rv1 = __float2bfloat16(__fadd_rn(__bfloat162float(qkv_row[vo + d]),
+                                                        __bfloat162float(p.v_bias[kvh * HD + d])));
+            const bf16 rv2 = __float2bfloat16(__fadd_rn(__bfloat162float(qkv_row[vo + d + half]),
+                                                        __bfloat162float(p.v_bias[kvh * HD + d + half])));
+            nk[d] = rk1;
+            nk[d + half] = rk2;
+            nk[HD + d] = rv1;
+            nk[HD + d + half] = rv2;
+            if (append && ph_ok) {
+                p.k_pool_w[dst + d] = rk1;
+                p.k_pool_w[dst + d + half] = rk2;
+                p.v_pool_w[dst + d] = rv1;
+                p.v_pool_w[dst + d + half] = rv2;
+            }
+        }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(ready);
+}
+
+// Fused mode, consumer warp: the new token's K and V rows (bf16 [2][HD] at
+// `nk`) over row r of the page tiles. Lane l copies 16-byte chunk l of each.
+template <int HD>
+__device__ __forceinline__ void patch_new_row(const bf16 *nk, uint8_t *smem_gen, uint32_t smem_base,
+                                              uint32_t kpage, uint32_t vpage, int r, int lane) {
+    constexpr int kChunks = HD / 8;
+    if (lane < kChunks) {
+        const uint4 kv = reinterpret_cast<const uint4 *>(nk)[lane];
+        const uint4 vv = reinterpret_cast<const uint4 *>(nk + HD)[lane];
+        *reinterpret_cast<uint4 *>(smem_gen + (tile_addr(kpage, r, lane) - smem_base)) = kv;
+        *reinterpret_cast<uint4 *>(smem_gen + (tile_addr(vpage, r, lane) - smem_base)) = vv;
+    }
 }
 
 // Sequences without cached tokens own no pages: their output rows are zero.
@@ -339,6 +400,146 @@ __device__ __forceinline__ void state_combine(WarpState<HD> &st, const float *re
         }
 }
 
+// Value of per-head array `a` for the head of lane's float4 f = lane + 32q in a
+// [8][HD] slot, with register-only (static) indexing.
+template <int HD>
+__device__ __forceinline__ float head_of_f4(const float (&a)[kHeadsPerCta], int q, int lane) {
+    if constexpr (HD == 128) return a[q];      // 32 float4s per head
+    else return (lane & 16) ? a[2 * q + 1] : a[2 * q];  // 16 float4s per head
+}
+
+// Log-sum-exp weights of a batch of up to 32 partials, lane j owning partial j:
+// lv[h] holds its log2-sum-exp on entry (-inf on lanes past the batch) and its
+// weight 2^(lse - M[h]) on exit. M and S (warp-uniform) are the running max and
+// weight sum per head; alpha[h] rescales the sums accumulated before the batch.
+__device__ __forceinline__ void merge_weights(float (&lv)[kHeadsPerCta], float (&M)[kHeadsPerCta],
+                                              float (&S)[kHeadsPerCta],
+                                              float (&alpha)[kHeadsPerCta]) {
+#pragma unroll
+    for (int h = 0; h < kHeadsPerCta; ++h) {
+        float mb = lv[h];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        const float mn = fmaxf(M[h], mb);  // finite: every partial has l > 0
+        alpha[h] = fast_exp2(M[h] - mn);
+        M[h] = mn;
+        lv[h] = fast_exp2(lv[h] - mn);
+        float sw = lv[h];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sw += __shfl_xor_sync(0xffffffffu, sw, o);
+        S[h] = S[h] * alpha[h] + sw;
+    }
+}
+
+// Partial slots the stage ring holds at once for the merge: each a [8][HD] row
+// of O/l and 8 log2-sum-exps (at most 32: one per lane).
+template <int HD>
+__host__ __device__ constexpr int kMergeRingSlots() {
+    return DecodeCfg<HD>::kStages * DecodeCfg<HD>::kStageBytes /
+                       ((kHeadsPerCta * HD + kHeadsPerCta) * 4) < 32
+               ? DecodeCfg<HD>::kStages * DecodeCfg<HD>::kStageBytes /
+                     ((kHeadsPerCta * HD + kHeadsPerCta) * 4)
+               : 32;
+}
+
+// Merge of a split segment's partials by the epilogue warp of the last CTA to
+// finish it, when that chunk is the CTA's final one: the stage ring is idle, so
+// the nch partial rows (contiguous slots from slot0) and their log2-sum-exps
+// are bulk-copied into it (in batches that fit), and the log-sum-exp weighted
+// sum runs from shared memory. Lane l owns float4 f = l + 32q (q < HD/16) of
+// the [8][HD] slot: head f / (HD/4), dims 4 * (f % (HD/4)) .. +3. Returns false
+// when a wait gave up (abort flag set; the copies in flight have landed).
+template <int HD>
+__device__ __forceinline__ bool merge_from_ring(bf16 *orow, int nh, const float *ws_o,
+                                             const float *ws_lse, long long slot0, int nch,
+                                             uint8_t *ring, uint64_t *bar, uint32_t phase,
+                                             volatile int *abort_flag, int *status, int lane) {
+    constexpr int kSlotFloats = kHeadsPerCta * HD;
+    constexpr int kMaxSlots = kMergeRingSlots<HD>();
+    constexpr int kQ = HD / 16;   // float4s per lane per slot
+    constexpr int kF4 = HD / 4;   // float4s per head
+    const float *mo = reinterpret_cast<const float *>(ring);
+    float *ml = reinterpret_cast<float *>(ring) + kMaxSlots * kSlotFloats;
+    // Partials written by other CTAs (generic proxy, published through the
+    // arrival counter) are read here by the bulk-copy (async) proxy.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    // Per head: running max M and weight sum S (warp-uniform); per lane: its
+    // kQ float4s of the weighted sum.
+    float M[kHeadsPerCta], S[kHeadsPerCta], O[kQ][4];
+#pragma unroll
+    for (int h = 0; h < kHeadsPerCta; ++h) {
+        M[h] = -INFINITY;
+        S[h] = 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) O[q][0] = O[q][1] = O[q][2] = O[q][3] = 0.f;
+    for (int jb = 0; jb < nch; jb += kMaxSlots) {
+        const int cnt = min(kMaxSlots, nch - jb);
+        if (lane == 0) {
+            const uint32_t ob = (uint32_t)(cnt * kSlotFloats * 4), lb = (uint32_t)(cnt * kHeadsPerCta * 4);
+            mbar_arrive_expect_tx(bar, ob + lb);
+            bulk_load(ring, ws_o + (slot0 + jb) * kSlotFloats, ob, bar);
+            bulk_load(ml, ws_lse + (slot0 + jb) * kHeadsPerCta, lb, bar);
+        }
+        if (!mbar_wait_bounded(bar, phase & 1, abort_flag, status)) {
+            if (lane == 0) mbar_wait_drain(bar, phase & 1);
+            __syncwarp();
+            return false;
+        }
+        ++phase;
+        // Weights: lane j (< cnt) takes slot j's log2-sum-exps and leaves its
+        // weights in their place for every lane to read.
+        float lv[kHeadsPerCta], alpha[kHeadsPerCta];
+        if (lane < cnt) {
+            const float4 a = reinterpret_cast<const float4 *>(ml + lane * kHeadsPerCta)[0];
+            const float4 b = reinterpret_cast<const float4 *>(ml + lane * kHeadsPerCta)[1];
+            lv[0] = a.x, lv[1] = a.y, lv[2] = a.z, lv[3] = a.w;
+            lv[4] = b.x, lv[5] = b.y, lv[6] = b.z, lv[7] = b.w;
+        } else {
+#pragma unroll
+            for (int h = 0; h < kHeadsPerCta; ++h) lv[h] = -INFINITY;
+        }
+        merge_weights(lv, M, S, alpha);
+        __syncwarp();  // every lane has read the log2-sum-exps
+        if (lane < cnt) {
+            reinterpret_cast<float4 *>(ml + lane * kHeadsPerCta)[0] = make_float4(lv[0], lv[1], lv[2], lv[3]);
+            reinterpret_cast<float4 *>(ml + lane * kHeadsPerCta)[1] = make_float4(lv[4], lv[5], lv[6], lv[7]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < kQ; ++q) {
+            const float a = head_of_f4<HD>(alpha, q, lane);
+            O[q][0] *= a;
+            O[q][1] *= a;
+            O[q][2] *= a;
+            O[q][3] *= a;
+        }
+#pragma unroll 2
+        for (int j = 0; j < cnt; ++j) {
+#pragma unroll
+            for (int q = 0; q < kQ; ++q) {
+                const int f = lane + 32 * q;
+                const float w = ml[j * kHeadsPerCta + f / kF4];
+                const float4 v = reinterpret_cast<const float4 *>(mo + j * kSlotFloats)[f];
+                O[q][0] += w * v.x;
+                O[q][1] += w * v.y;
+                O[q][2] += w * v.z;
+                O[q][3] += w * v.w;
+            }
+        }
+        __syncwarp();  // every lane is done with the batch before the next copy
+    }
+#pragma unroll
+    for (int q = 0; q < kQ; ++q) {
+        const int f = lane + 32 * q, h = f / kF4, d = 4 * (f % kF4);
+        if (h >= nh) continue;
+        const float inv = 1.f / head_of_f4<HD>(S, q, lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) orow[h * HD + d + k] = __float2bfloat16(O[q][k] * inv);
+    }
+    return true;
+}
+
 template <int HD, bool FUSED>
 __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
@@ -351,6 +552,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     __shared__ __align__(8) uint64_t fin_bar;    // consumer-warp sync (bounded)
     __shared__ __align__(8) uint64_t epi_full;   // consumers -> epilogue: slots hold a chunk
     __shared__ __align__(8) uint64_t epi_empty;  // epilogue -> consumers: slots free again
+    __shared__ __align__(8) uint64_t merge_bar;  // epilogue: partials copied into the ring
+    __shared__ __align__(8) uint64_t q_full[2];  // fused: epilogue -> consumers, chunk inputs ready
     __shared__ StageMeta meta[Cfg::kStages];
     __shared__ EpiInfo epi;
     __shared__ long long s_total;
@@ -371,6 +574,12 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     uint8_t *smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
     // Set-up scan scratch: the head of the stage ring, free until the first TMA.
     long long *s_part = reinterpret_cast<long long *>(smem_gen);
+    // Fused: the q slots hold the epilogue's prepared chunk inputs instead,
+    // double-buffered by chunk parity: q [2][8][HD], new K/V rows [2][2][HD].
+    bf16 *q_prep = reinterpret_cast<bf16 *>(smem_gen + Cfg::kQOffset);
+    bf16 *nk_rows = q_prep + 2 * kHeadsPerCta * HD;
+    static_assert(Cfg::kStages * Cfg::kQBytes >= 2 * (kHeadsPerCta + 2) * HD * 2,
+                  "prepared chunk inputs must fit the q slots");
 
     // ---- 1. total pages T and empty-sequence outputs ------------------------
     const int per = (p.batch + kThreads - 1) / kThreads;
@@ -452,6 +661,9 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         mbar_init(&fin_bar, kConsumerWarps * 32);
         mbar_init(&epi_full, 2);
         mbar_init(&epi_empty, 1);
+        mbar_init(&merge_bar, 1);
+        mbar_init(&q_full[0], 1);
+        mbar_init(&q_full[1], 1);
         s_abort = 0;
         fence_barrier_init();
     }
@@ -464,24 +676,14 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
             prefetch_tensormap(&tmap_k);
             prefetch_tensormap(&tmap_v);
         }
-        int b = s_b0;
-        int n = seq_tokens(p, b, lane == 0);
-        int pages_b = (n + kBlockSize - 1) / kBlockSize;
-        const long long off = start - s_pref_b0;
-        int g = (int)(off / pages_b);
-        int pg = (int)(off - (long long)g * pages_b);
-        long long glob = start;
+        ChunkCursor cur;
+        cur.init(p, start, s_b0, s_pref_b0, lane == 0);
+        Chunk ch;
         int it = 0;
         bool ok = true;
-        while (glob < end && ok) {
-            if (pages_b == 0) {  // empty sequence: owns no pages
-                ++b;
-                n = seq_tokens(p, b, lane == 0);
-                pages_b = (n + kBlockSize - 1) / kBlockSize;
-                continue;
-            }
-            const int take = (int)min((long long)(pages_b - pg), end - glob);
-            const long long seg_start = glob - pg;
+        while (ok && cur.next(p, end, lane == 0, ch)) {
+            const int b = ch.b, g = ch.g, pg = ch.p0, take = ch.take;
+            const bool final_chunk = cur.glob >= end;
             const int kvh = g / p.ctas_per_kv;
             const int hsub = g - kvh * p.ctas_per_kv;
             const int *trow = p.tables + (int64_t)b * p.table_stride;
@@ -536,29 +738,21 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                         m.g = g;
                         m.page0 = pg + base + j;
                         m.np = np;
-                        m.n = n;
-                        m.pages_b = pages_b;
-                        m.flags = (first ? kFirst : 0) | (base + j + np == take ? kLast : 0);
+                        m.n = ch.n;
+                        m.pages_b = ch.pages_b;
+                        const bool last_stage = base + j + np == take;
+                        m.flags = (first ? kFirst : 0) | (last_stage ? kLast : 0) |
+                                  (last_stage && final_chunk ? kFinal : 0);
                         m.chunk_p0 = pg;
                         m.take = take;
                         m.pos = FUSED ? __ldg(p.ctx_lens + b) + p.len_offset - 1 : -1;
-                        m.seg_start = seg_start;
+                        m.seg_start = ch.seg_start;
                         // Copies may have landed already: the transaction count of a
                         // phase may run below zero until this arrival states it.
                         mbar_arrive_expect_tx(&full_bar[s],
                                               (uint32_t)(np * 2 * Cfg::kPageBytes) + qbytes);
                     }
                     ++it;
-                }
-            }
-            glob += take;
-            pg = 0;
-            if (++g == G) {
-                g = 0;
-                ++b;
-                if (glob < end) {
-                    n = seq_tokens(p, b, lane == 0);
-                    pages_b = (n + kBlockSize - 1) / kBlockSize;
                 }
             }
         }
@@ -587,9 +781,34 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         // bf16 output (whole segment) or a partial plus, for the last chunk of a
         // split segment to arrive, the log-sum-exp merge of all its partials.
         constexpr int KD = HD / 32;  // head dims per lane
+        uint32_t merge_phase = 0;
+        // Segments this CTA merges (it was the last to finish them): at most
+        // its first and its final chunk, merged once the consumers are done.
+        struct PendingMerge {
+            int b, head0, nh, seg, c_first, nch;
+        } pend[2];
+        int npend = 0;
         if (p.pdl_mode == 2) griddep_wait();
-        zero_empty_outputs<HD>(p, cta, C, lane, 32);
+        // Fused: chunk j's inputs go to buffer j & 1. Before waiting for chunk k
+        // to finish, chunks up to k + 1 are prepared; buffer (k + 1) & 1 was
+        // last read by chunk k - 1, which has finished.
+        ChunkCursor pcur;
+        int prepared = 0;
+        bool more = true;
+        if constexpr (FUSED) pcur.init(p, start, s_b0, s_pref_b0, false);
         for (int k = 0;; ++k) {
+            if constexpr (FUSED) {
+                Chunk c;
+                while (more && prepared <= k + 1) {
+                    more = pcur.next(p, end, false, c);
+                    if (!more) break;
+                    const int qb = prepared & 1;
+                    prepare_chunk<HD>(p, c, q_prep + qb * kHeadsPerCta * HD, nk_rows + qb * 2 * HD,
+                                      &q_full[qb], lane);
+                    ++prepared;
+                }
+            }
+            if (k == 0) zero_empty_outputs<HD>(p, cta, C, lane, 32);
             if (!mbar_wait_bounded(&epi_full, k & 1, &s_abort, p.status)) break;
             const EpiInfo e = epi;
             if (e.done) break;
@@ -634,84 +853,35 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                 if (lane == h) p.ws_lse[slot * kHeadsPerCta + h] = Mh[h] + __log2f(Lh[h]);
             }
             // Publish the partial, then count it; the last CTA to arrive merges.
-            __threadfence();
+            // Release pattern: every lane's stores, an acq_rel fence, the warp
+            // sync, then lane 0's atomic, an acquire for the merge (the one
+            // thread that issues its copies).
+            fence_acq_rel_gpu();
             __syncwarp();
             const int c_first = owner_cta(e.seg_start, T, C);
             const int nch = owner_cta(e.seg_start + e.pages_b - 1, T, C) - c_first + 1;
             int last = 0;
-            if (lane == 0) last = atomicAdd(p.ws_cnt + e.seg, 1) == nch - 1;
+            if (lane == 0) last = atom_add_acquire_gpu(p.ws_cnt + e.seg, 1) == nch - 1;
             if (!__shfl_sync(0xffffffffu, last, 0)) continue;
-            __threadfence();
-            // Merge: weights 2^(lse_j - max_j lse_j) per head, loads in parallel.
-            const long long slot0 = (long long)e.seg + c_first;
-            float Mx[kHeadsPerCta];
+            // This CTA merges the segment, after its final chunk: then the stage
+            // ring is idle and takes all the partials in one round of bulk
+            // copies. Split chunks are a CTA's first and final ones only.
+            const PendingMerge pm = {e.b, e.head0, e.nh, e.seg, c_first, nch};
+            if (npend == 0) pend[0] = pm;
+            else pend[1] = pm;
+            ++npend;
+        }
 #pragma unroll
-            for (int h = 0; h < kHeadsPerCta; ++h) Mx[h] = -INFINITY;
-            for (int jb = 0; jb < nch; jb += 32) {
-                const int j = jb + lane;
-                if (j < nch) {
-                    const float4 *row = reinterpret_cast<const float4 *>(p.ws_lse + (slot0 + j) * kHeadsPerCta);
-                    const float4 a = __ldcg(row), b4 = __ldcg(row + 1);
-                    const float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-                    for (int h = 0; h < kHeadsPerCta; ++h) Mx[h] = fmaxf(Mx[h], v[h]);
-                }
-            }
-#pragma unroll
-            for (int h = 0; h < kHeadsPerCta; ++h)
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1)
-                    Mx[h] = fmaxf(Mx[h], __shfl_xor_sync(0xffffffffu, Mx[h], o));
-            float S[kHeadsPerCta];
-#pragma unroll
-            for (int h = 0; h < kHeadsPerCta; ++h) {
-                S[h] = 0.f;
-#pragma unroll
-                for (int kk = 0; kk < KD; ++kk) O[h][kk] = 0.f;
-            }
-            // Partials in groups of kMergeGroup with predicated loads: a group's
-            // loads are all in flight together, whatever nch is.
-            constexpr int kMergeGroup = 2;
-            for (int jb = 0; jb < nch; jb += kMergeGroup) {
-                float w[kMergeGroup][kHeadsPerCta];
-                float vals[kMergeGroup][kHeadsPerCta][KD];
-#pragma unroll
-                for (int u = 0; u < kMergeGroup; ++u) {
-                    const int j = jb + u;
-                    const bool in = j < nch;
-                    const long long sl = slot0 + (in ? j : 0);
-                    const float4 *row = reinterpret_cast<const float4 *>(p.ws_lse + sl * kHeadsPerCta);
-                    const float4 a = __ldcg(row), b4 = __ldcg(row + 1);
-                    const float v[8] = {a.x, a.y, a.z, a.w, b4.x, b4.y, b4.z, b4.w};
-                    const float *src = p.ws_o + sl * kHeadsPerCta * HD;
-#pragma unroll
-                    for (int h = 0; h < kHeadsPerCta; ++h) {
-                        w[u][h] = in ? v[h] : -INFINITY;
-#pragma unroll
-                        for (int kk = 0; kk < KD; ++kk)
-                            vals[u][h][kk] = h < e.nh ? __ldcg(src + h * HD + kk * 32 + lane) : 0.f;
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < kMergeGroup; ++u)
-#pragma unroll
-                    for (int h = 0; h < kHeadsPerCta; ++h) {
-                        const float wt = fast_exp2(w[u][h] - Mx[h]);  // 0 for padding
-                        S[h] += wt;
-#pragma unroll
-                        for (int kk = 0; kk < KD; ++kk) O[h][kk] += wt * vals[u][h][kk];
-                    }
-            }
-            bf16 *orow = p.out + (int64_t)e.b * p.out_stride + (int64_t)e.head0 * HD;
-#pragma unroll
-            for (int h = 0; h < kHeadsPerCta; ++h) {
-                if (h >= e.nh) break;
-                const float inv = 1.f / S[h];
-#pragma unroll
-                for (int kk = 0; kk < KD; ++kk)
-                    orow[h * HD + kk * 32 + lane] = __float2bfloat16(O[h][kk] * inv);
-            }
-            if (lane == 0) p.ws_cnt[e.seg] = 0;  // ready for the next call
+        for (int i = 0; i < 2; ++i) {
+            if (i >= npend || s_abort) break;
+            const PendingMerge &m = pend[i];
+            const bool ok = merge_from_ring<HD>(
+                p.out + (int64_t)m.b * p.out_stride + (int64_t)m.head0 * HD, m.nh, p.ws_o, p.ws_lse,
+                (long long)m.seg + m.c_first, m.nch, smem_gen, &merge_bar, merge_phase, &s_abort,
+                p.status, lane);
+            merge_phase += (m.nch + kMergeRingSlots<HD>() - 1) / kMergeRingSlots<HD>();
+            if (!ok) break;
+            if (lane == 0) p.ws_cnt[m.seg] = 0;  // ready for the next call
         }
         return;
     }
@@ -726,7 +896,6 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     uint32_t fin_phase = 0;
     int chunk_idx = 0;  // chunks handed to the epilogue so far
     int nk_it = -1, nk_warp = -1;  // fused: stage and warp of the new token's page
-    NewKvInputs<HD> nk_in;
     WarpState<HD> st;
     st.reset();
     for (int it = 0;; ++it) {
@@ -749,8 +918,15 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         if (m.flags & kFirst) {
             const bool hv = g8 < nh;
             if constexpr (FUSED) {
-                rope_q_fragments<HD>(p, m.b, kvh * p.group + hsub * kHeadsPerCta + g8, hv, m.pos,
-                                     c4, qf);
+                // q comes biased and rotated from the epilogue warp.
+                const int qb = chunk_idx & 1;
+                if (!mbar_wait_bounded(&q_full[qb], (chunk_idx >> 1) & 1, &s_abort, p.status)) break;
+                const bf16 *qs = q_prep + qb * kHeadsPerCta * HD + g8 * HD + 2 * c4;
+#pragma unroll
+                for (int j = 0; j < KSTEPS; ++j) {
+                    qf[j][0] = *reinterpret_cast<const uint32_t *>(qs + 16 * j);
+                    qf[j][1] = *reinterpret_cast<const uint32_t *>(qs + 16 * j + 8);
+                }
                 // Does this chunk end with the new token's page, and which warp
                 // and stage will hold it? Stages start at the chunk's first page.
                 nk_it = -1;
@@ -758,7 +934,6 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                     const int k = m.pages_b - 1 - m.chunk_p0;
                     nk_it = it + k / kPagesPerStage;
                     nk_warp = k % kPagesPerStage;
-                    if (warp == nk_warp) nk_in.load(p, m.b, kvh, m.pos, m.pages_b - 1, lane);
                 }
             } else {
                 const uint8_t *qs = smem_gen + Cfg::kQOffset + s * Cfg::kQBytes;
@@ -776,11 +951,13 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
             const uint32_t kpage = smem_base + s * Cfg::kStageBytes + warp * Cfg::kPageBytes;
             const uint32_t vpage = kpage + kPagesPerStage * Cfg::kPageBytes;
             if (FUSED && it == nk_it && warp == nk_warp) {
-                // The new token: its rotated K and V + bias replace the tile row
-                // (loaded before the append) and are appended to the pools by the
-                // first 8-head slice of the kv head.
-                nk_in.apply(p, kvh, m.pos, hsub == 0, smem_gen, smem_base, kpage, vpage,
-                            m.pos % kBlockSize, lane);
+                // The new token: its rotated K and V + bias (prepared by the
+                // epilogue warp, which also appends them to the pools) replace
+                // the tile row, which may have been loaded before the append.
+                patch_new_row<HD>(nk_rows + (chunk_idx & 1) * 2 * HD, smem_gen, smem_base, kpage,
+                                  vpage, m.pos % kBlockSize, lane);
+                // Later bulk/TMA writes into this stage are async-proxy accesses.
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
             }
             float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -854,6 +1031,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                 epi.whole = m.chunk_p0 == 0 && m.take == m.pages_b;
                 epi.done = 0;
                 epi.seg_start = m.seg_start;
+                epi.final = (m.flags & kFinal) != 0;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&epi_full);
