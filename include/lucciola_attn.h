@@ -70,11 +70,13 @@ const char *lc_version(void);
  *     scheduled while the preceding grid in the stream retires and waits for
  *     it (griddepcontrol.wait) before reading or writing any memory;
  *   2 as 1, but the grid reads the context lengths and computes its split
- *     before that wait, and lc_rope_append_decode also reads block tables and
- *     starts loading this layer's cached K/V pages before it. The kernel
- *     launched just before on the same stream must then not write the context
- *     lengths, the block tables, or this layer's cached K/V (a decode step's
- *     QKV projection or another layer's attention qualifies).
+ *     before that wait, and lc_rope_append_decode also reads block tables,
+ *     the positions, the q/k/v biases and the RoPE cos/sin rows, and starts
+ *     loading this layer's cached K/V pages before it; only the qkv rows are
+ *     read after it. The kernel launched just before on the same stream must
+ *     then not write the context lengths/positions, the block tables, the
+ *     biases, the RoPE tables, or this layer's cached K/V (a decode step's QKV
+ *     projection or another layer's attention qualifies).
  * Returns the previous mode, or -1 for an invalid mode. */
 int lc_set_dependent_launch(int mode);
 

@@ -98,7 +98,9 @@ struct DecodeParams {
     // waits for the preceding grid first; 2 = set-up (context lengths, split)
     // runs before that wait, and in the fused kernel the producer warp, which
     // only reads context lengths, block tables and this layer's cached pages,
-    // never waits: its first stages land while the preceding grid drains.
+    // never waits: its first stages land while the preceding grid drains; the
+    // epilogue warp reads the first chunk's position, rope rows and biases
+    // before it and only the qkv rows after.
     int pdl_mode;
     float *ws_o;       // [slots][8][HD]
     float *ws_lse;     // [slots][8]
@@ -211,93 +213,121 @@ struct ChunkCursor {
 //    V + bias row, bf16 [2][HD] in `nk`, which the consumer warp holding that
 //    page writes over the tile row; the first 8-head slice of the kv head also
 //    appends both rows to the pools here.
-// The arithmetic is that of rope_append.cu (rope_math.cuh), so q, the tile
-// rows and the pool writes equal the two-launch path's bit for bit.
+// load_static() reads what no preceding kernel of a decode step writes (the
+// position, rope rows, biases, block table), so for the first chunk it runs
+// before the programmatic-dependency wait; finish() reads the qkv row. The
+// arithmetic is that of rope_append.cu (rope_math.cuh), so q, the tile rows and
+// the pool writes equal the two-launch path's bit for bit.
 template <int HD>
-__device__ __forceinline__ void prepare_chunk(const DecodeParams &p, const Chunk &c, bf16 *qs,
-                                              bf16 *nk, uint64_t *ready, int lane) {
-    constexpr int half = HD / 2;
-    const int kvh = c.g / p.ctas_per_kv;
-    const int hsub = c.g - kvh * p.ctas_per_kv;
-    const int head0 = kvh * p.group + hsub * kHeadsPerCta;
-    const int nh = min(kHeadsPerCta, p.group - hsub * kHeadsPerCta);
-    const int pos = __ldg(p.ctx_lens + c.b) + p.len_offset - 1;
-    const bool pos_ok = pos >= 0 && pos < p.rope_rows;
-    const float *ct = p.cos_t + (int64_t)(pos_ok ? pos : 0) * half;
-    const float *sn = p.sin_t + (int64_t)(pos_ok ? pos : 0) * half;
-    const bf16 *qkv_row = p.qkv + (int64_t)c.b * p.q_stride;
-    {
-        // lane -> head lane / 4, rotation pairs (d, d + half) for d in its quarter
-        constexpr int kPer = half / 4;
+struct ChunkPrep {
+    static constexpr int kHalf = HD / 2;
+    static constexpr int kPer = kHalf / 4;  // q dims per lane (lane: head lane / 4, quarter lane % 4)
+    static constexpr int kNk = HD / 64;     // new-token rotation pairs per lane
+    int pos, head0, nh, kvh, hsub, phys;
+    bool pos_ok, has_nk;
+    float2 cs[kPer / 2], sv[kPer / 2];
+    __nv_bfloat162 b1[kPer / 2], b2[kPer / 2];
+    float kc[kNk], ks[kNk];
+    bf16 kb1[kNk], kb2[kNk], vb1[kNk], vb2[kNk];
+
+    __device__ __forceinline__ void load_static(const DecodeParams &p, const Chunk &c, int lane) {
+        kvh = c.g / p.ctas_per_kv;
+        hsub = c.g - kvh * p.ctas_per_kv;
+        head0 = kvh * p.group + hsub * kHeadsPerCta;
+        nh = min(kHeadsPerCta, p.group - hsub * kHeadsPerCta);
+        pos = __ldg(p.ctx_lens + c.b) + p.len_offset - 1;
+        pos_ok = pos >= 0 && pos < p.rope_rows;
+        const float *ct = p.cos_t + (int64_t)(pos_ok ? pos : 0) * kHalf;
+        const float *sn = p.sin_t + (int64_t)(pos_ok ? pos : 0) * kHalf;
+        const int h = lane >> 2, d0 = (lane & 3) * kPer;
+        const bf16 *bias = p.q_bias + (int64_t)(head0 + min(h, nh - 1)) * HD;
+#pragma unroll
+        for (int i = 0; i < kPer / 2; ++i) {
+            const int d = d0 + 2 * i;
+            b1[i] = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d));
+            b2[i] = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d + kHalf));
+            cs[i] = pos_ok ? __ldg(reinterpret_cast<const float2 *>(ct + d)) : make_float2(1.f, 1.f);
+            sv[i] = pos_ok ? __ldg(reinterpret_cast<const float2 *>(sn + d)) : make_float2(0.f, 0.f);
+        }
+        has_nk = pos == c.n - 1 && c.p0 + c.take == c.pages_b;
+        if (has_nk) {
+            phys = __ldg(p.tables + (int64_t)c.b * p.table_stride + c.pages_b - 1);
+#pragma unroll
+            for (int i = 0; i < kNk; ++i) {
+                const int d = lane + 32 * i;
+                kb1[i] = p.k_bias[kvh * HD + d];
+                kb2[i] = p.k_bias[kvh * HD + d + kHalf];
+                vb1[i] = p.v_bias[kvh * HD + d];
+                vb2[i] = p.v_bias[kvh * HD + d + kHalf];
+                kc[i] = pos_ok ? __ldg(ct + d) : 1.f;
+                ks[i] = pos_ok ? __ldg(sn + d) : 0.f;
+            }
+        }
+    }
+
+    __device__ __forceinline__ void finish(const DecodeParams &p, const Chunk &c, bf16 *qs, bf16 *nk,
+                                           uint64_t *ready, int lane) const {
+        const bf16 *qkv_row = p.qkv + (int64_t)c.b * p.q_stride;
         const int h = lane >> 2, d0 = (lane & 3) * kPer;
         bf16 *dst = qs + h * HD;
         if (h < nh) {
             const bf16 *row = qkv_row + (int64_t)(head0 + h) * HD;
-            const bf16 *bias = p.q_bias + (int64_t)(head0 + h) * HD;
 #pragma unroll
-            for (int i = 0; i < kPer; i += 2) {
-                const int d = d0 + i;
+            for (int i = 0; i < kPer / 2; ++i) {
+                const int d = d0 + 2 * i;
                 const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162 *>(row + d);
-                const __nv_bfloat162 x2 = *reinterpret_cast<const __nv_bfloat162 *>(row + d + half);
-                const __nv_bfloat162 b1 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d));
-                const __nv_bfloat162 b2 = __ldg(reinterpret_cast<const __nv_bfloat162 *>(bias + d + half));
-                const float2 cs = pos_ok ? __ldg(reinterpret_cast<const float2 *>(ct + d)) : make_float2(1.f, 1.f);
-                const float2 sv = pos_ok ? __ldg(reinterpret_cast<const float2 *>(sn + d)) : make_float2(0.f, 0.f);
-                const float a0 = __fadd_rn(__low2float(x1), __low2float(b1));
-                const float a1 = __fadd_rn(__high2float(x1), __high2float(b1));
-                const float e0 = __fadd_rn(__low2float(x2), __low2float(b2));
-                const float e1 = __fadd_rn(__high2float(x2), __high2float(b2));
+                const __nv_bfloat162 x2 = *reinterpret_cast<const __nv_bfloat162 *>(row + d + kHalf);
+                const float a0 = __fadd_rn(__low2float(x1), __low2float(b1[i]));
+                const float a1 = __fadd_rn(__high2float(x1), __high2float(b1[i]));
+                const float e0 = __fadd_rn(__low2float(x2), __low2float(b2[i]));
+                const float e1 = __fadd_rn(__high2float(x2), __high2float(b2[i]));
                 *reinterpret_cast<__nv_bfloat162 *>(dst + d) =
-                    __halves2bfloat162(__float2bfloat16(rot_sub(a0, cs.x, e0, sv.x)),
-                                       __float2bfloat16(rot_sub(a1, cs.y, e1, sv.y)));
-                *reinterpret_cast<__nv_bfloat162 *>(dst + d + half) =
-                    __halves2bfloat162(__float2bfloat16(rot_add(a0, sv.x, e0, cs.x)),
-                                       __float2bfloat16(rot_add(a1, sv.y, e1, cs.y)));
+                    __halves2bfloat162(__float2bfloat16(rot_sub(a0, cs[i].x, e0, sv[i].x)),
+                                       __float2bfloat16(rot_sub(a1, cs[i].y, e1, sv[i].y)));
+                *reinterpret_cast<__nv_bfloat162 *>(dst + d + kHalf) =
+                    __halves2bfloat162(__float2bfloat16(rot_add(a0, sv[i].x, e0, cs[i].x)),
+                                       __float2bfloat16(rot_add(a1, sv[i].y, e1, cs[i].y)));
             }
         } else {
             const __nv_bfloat162 z = __float2bfloat162_rn(0.f);
 #pragma unroll
             for (int i = 0; i < kPer; i += 2) {
                 *reinterpret_cast<__nv_bfloat162 *>(dst + d0 + i) = z;
-                *reinterpret_cast<__nv_bfloat162 *>(dst + d0 + i + half) = z;
+                *reinterpret_cast<__nv_bfloat162 *>(dst + d0 + i + kHalf) = z;
             }
         }
-    }
-    if (pos == c.n - 1 && c.p0 + c.take == c.pages_b) {
-        const int ko = p.num_q_heads * HD + kvh * HD, vo = ko + p.num_kv_heads * HD;
-        const bool append = hsub == 0;
-        const int phys = __ldg(p.tables + (int64_t)c.b * p.table_stride + c.pages_b - 1);
-        const bool ph_ok = phys >= 0 && phys < p.num_blocks;
-        const int64_t dst = page_row(ph_ok ? phys : 0, p.layer, kvh, p.num_layers, p.num_kv_heads) * HD +
-                            (int64_t)(pos % kBlockSize) * HD;
+        if (has_nk) {
+            const int ko = p.num_q_heads * HD + kvh * HD, vo = ko + p.num_kv_heads * HD;
+            const bool append = hsub == 0;
+            const bool ph_ok = phys >= 0 && phys < p.num_blocks;
+            const int64_t prow =
+                page_row(ph_ok ? phys : 0, p.layer, kvh, p.num_layers, p.num_kv_heads) * HD +
+                (int64_t)(pos % kBlockSize) * HD;
 #pragma unroll
-        for (int i = 0; i < HD / 64; ++i) {
-            const int d = lane + 32 * i;
-            const float a1 = __fadd_rn(__bfloat162float(qkv_row[ko + d]), __bfloat162float(p.k_bias[kvh * HD + d]));
-            const float a2 = __fadd_rn(__bfloat162float(qkv_row[ko + d + half]),
-                                       __bfloat162float(p.k_bias[kvh * HD + d + half]));
-            const float cv = pos_ok ? __ldg(ct + d) : 1.f, sv = pos_ok ? __ldg(sn + d) : 0.f;
-            const bf16 rk1 = __float2bfloat16(rot_sub(a1, cv, a2, sv));
-            const bf16 rk2 = __float2bfloat16(rot_add(a1, sv, a2, cv));
-            const bf16 rv1 = __float2bfloat16(__fadd_rn(__bfloat162float(qkv_row[vo + d]),
-                                                        __bfloat162float(p.v_bias[kvh * HD + d])));
-            const bf16 rv2 = __float2bfloat16(__fadd_rn(__bfloat162float(qkv_row[vo + d + half]),
-                                                        __bfloat162float(p.v_bias[kvh * HD + d + half])));
-            nk[d] = rk1;
-            nk[d + half] = rk2;
-            nk[HD + d] = rv1;
-            nk[HD + d + half] = rv2;
-            if (append && ph_ok) {
-                p.k_pool_w[dst + d] = rk1;
-                p.k_pool_w[dst + d + half] = rk2;
-                p.v_pool_w[dst + d] = rv1;
-                p.v_pool_w[dst + d + half] = rv2;
+            for (int i = 0; i < kNk; ++i) {
+                const int d = lane + 32 * i;
+                const float a1 = __fadd_rn(__bfloat162float(qkv_row[ko + d]), __bfloat162float(kb1[i]));
+                const float a2 = __fadd_rn(__bfloat162float(qkv_row[ko + d + kHalf]), __bfloat162float(kb2[i]));
+                const bf16 rk1 = __float2bfloat16(rot_sub(a1, kc[i], a2, ks[i]));
+                const bf16 rk2 = __float2bfloat16(rot_add(a1, ks[i], a2, kc[i]));
+                const bf16 rv1 = __float2bfloat16(__fadd_rn(__bfloat162float(qkv_row[vo + d]), __bfloat162float(vb1[i])));
+                const bf16 rv2 = __float2bfloat16(__fadd_rn(__bfloat162float(qkv_row[vo + d + kHalf]), __bfloat162float(vb2[i])));
+                nk[d] = rk1;
+                nk[d + kHalf] = rk2;
+                nk[HD + d] = rv1;
+                nk[HD + d + kHalf] = rv2;
+                if (append && ph_ok) {
+                    p.k_pool_w[prow + d] = rk1;
+                    p.k_pool_w[prow + d + kHalf] = rk2;
+                    p.v_pool_w[prow + d] = rv1;
+                    p.v_pool_w[prow + d + kHalf] = rv2;
+                }
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ready);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(ready);
-}
+};
 
 // Fused mode, consumer warp: the new token's K and V rows (bf16 [2][HD] at
 // `nk`) over row r of the page tiles. Lane l copies 16-byte chunk l of each.
@@ -788,10 +818,12 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
             int b, head0, nh, seg, c_first, nch;
         } pend[2];
         int npend = 0;
-        if (p.pdl_mode == 2) griddep_wait();
         // Fused: chunk j's inputs go to buffer j & 1. Before waiting for chunk k
         // to finish, chunks up to k + 1 are prepared; buffer (k + 1) & 1 was
-        // last read by chunk k - 1, which has finished.
+        // last read by chunk k - 1, which has finished. The dependency wait
+        // sits inside the first chunk's preparation.
+        bool waited = !(FUSED && p.pdl_mode == 2);
+        if (p.pdl_mode == 2 && !FUSED) griddep_wait();
         ChunkCursor pcur;
         int prepared = 0;
         bool more = true;
@@ -803,9 +835,19 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                     more = pcur.next(p, end, false, c);
                     if (!more) break;
                     const int qb = prepared & 1;
-                    prepare_chunk<HD>(p, c, q_prep + qb * kHeadsPerCta * HD, nk_rows + qb * 2 * HD,
-                                      &q_full[qb], lane);
+                    ChunkPrep<HD> cp;
+                    cp.load_static(p, c, lane);
+                    if (!waited) {
+                        griddep_wait();
+                        waited = true;
+                    }
+                    cp.finish(p, c, q_prep + qb * kHeadsPerCta * HD, nk_rows + qb * 2 * HD,
+                              &q_full[qb], lane);
                     ++prepared;
+                }
+                if (!waited) {
+                    griddep_wait();
+                    waited = true;
                 }
             }
             if (k == 0) zero_empty_outputs<HD>(p, cta, C, lane, 32);
@@ -840,6 +882,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                     for (int kk = 0; kk < KD; ++kk)
                         orow[h * HD + kk * 32 + lane] = __float2bfloat16(O[h][kk] * il);
                 }
+                if (e.final) break;  // the consumers' end-of-range message is not needed
                 continue;
             }
             // Partial of a split segment: slot = segment + this CTA.
@@ -862,7 +905,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
             const int nch = owner_cta(e.seg_start + e.pages_b - 1, T, C) - c_first + 1;
             int last = 0;
             if (lane == 0) last = atom_add_acquire_gpu(p.ws_cnt + e.seg, 1) == nch - 1;
-            if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+            if (!__shfl_sync(0xffffffffu, last, 0)) {
+                if (e.final) break;
+                continue;
+            }
             // This CTA merges the segment, after its final chunk: then the stage
             // ring is idle and takes all the partials in one round of bulk
             // copies. Split chunks are a CTA's first and final ones only.
@@ -870,6 +916,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
             if (npend == 0) pend[0] = pm;
             else pend[1] = pm;
             ++npend;
+            if (e.final) break;
         }
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
