@@ -84,6 +84,18 @@ __device__ inline void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T: A (M rows = TMEM lanes, K-major, two bf16
+// per 32-bit column) read from tensor memory.
+__device__ inline void umma_bf16_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrives (once) on `bar` when every tcgen05 operation this thread issued so
 // far has completed.
 __device__ inline void umma_commit(uint64_t *bar) {
@@ -118,6 +130,17 @@ __device__ inline void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
         "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
         "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
         "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns from registers.
+__device__ inline void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15])
         : "memory");
 }
 

@@ -8,18 +8,25 @@
 //   out[b, i, h] = softmax_{t <= start_b + i}(q_i . k_t * scale) . v_t
 // over cache positions 0..start_b + i (prior context plus the prompt so far).
 //
-// One CTA per (128-query tile, query head, sequence), heaviest tiles first.
-//   warp 0    TMA: the Q tile once; K and V tiles of 128 keys = 8 pages each,
-//             page by page through the block table, into a 2-3 stage ring
-//             (128-byte swizzle, completion on mbarriers).
-//   warp 1    MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S
-//             buffers (128 x 128 fp32), then O += P_j V_j into TMEM O
-//             (128 x hd fp32); both bf16 x bf16 -> fp32 tcgen05.mma, M = 128.
-//             S_{j+1} is issued before PV_j so softmax j+1 overlaps PV_j.
-//   warps 2-5 softmax, one thread per query row (its TMEM lane): scale, causal
-//             mask, running max with lazy rescaling (O is rescaled in TMEM only
-//             when a row max grows by more than 2^8), P_j = 2^(s - m) as bf16
-//             into shared memory for the PV MMA, then O / l -> bf16 output.
+// One CTA per (256-query block, query head, sequence), heaviest blocks first.
+// The block is two 128-query tiles that share every K/V tile:
+//   warp 0     TMA: both Q tiles once; K and V tiles of 128 keys = 8 pages
+//              each, page by page through the block table, into a 2-4 stage
+//              ring (128-byte swizzle, completion on mbarriers).
+//   warp 1     MMA issuer (one thread), bf16 x bf16 -> fp32 tcgen05.mma, M = 128:
+//              S_t = Q_t K_j^T into TMEM (128 columns per tile t), and
+//              O_t += P_t V_j with P_t read from TMEM, where softmax wrote it
+//              as bf16 over the first 64 columns of S_t. Per K/V tile the
+//              order is PV_0, S_0 (next tile), PV_1, S_1 (next tile), so while
+//              one softmax warpgroup works the tensor core runs the other
+//              tile's products (ping-pong).
+//   warps 2-5  softmax warpgroup of Q tile 0, warps 6-9 of Q tile 1: one
+//              thread per query row (its TMEM lane): scale, causal mask,
+//              running max with lazy rescaling (O is rescaled in TMEM only when
+//              a row max grows by more than 2^8), P = 2^(s - m) into TMEM,
+//              and at the end O / l -> bf16 output.
+// TMEM (512 columns): S/P of tile t at [128 t, 128 t + 128), O of tile t at
+// [256 + hd t, 256 + hd (t + 1)).
 // GQA: the CTAs of the q heads of one kv head read the same K/V tiles; they
 // fit in L2 (a 4 x 4096-token 1.5B prompt holds 16 MB of K/V per layer).
 #include "lc_common.cuh"
@@ -29,25 +36,26 @@
 namespace lc {
 namespace {
 
-constexpr int kBM = 128;  // queries per CTA
-constexpr int kBN = 128;  // keys per tile (8 pages)
-constexpr int kThreadsPf = 192;
-constexpr uint32_t kTmemCols = 512;       // S0 [0,128) S1 [128,256) O [256, 256+hd)
-constexpr float kRescaleLog2 = 8.f;       // rescale O only when a row max grows by > 2^8
+constexpr int kBM = 128;  // queries per Q tile (one TMEM lane each)
+constexpr int kQT = 2;    // Q tiles per CTA
+constexpr int kBN = 128;  // keys per K/V tile (8 pages)
+constexpr int kThreadsPf = (2 + 4 * kQT) * 32;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.f;  // rescale O only when a row max grows by > 2^8
 
 template <int HD>
 struct PrefillCfg {
     static constexpr int kHalves = HD / 64;
-    static constexpr int kQBytes = kBM * HD * 2;
+    static constexpr int kQBytes = kBM * HD * 2;     // one Q tile
     static constexpr int kTileBytes = kBN * HD * 2;  // one K or V tile
-    static constexpr int kStages = HD == 64 ? 3 : 2;
-    static constexpr int kPBytes = kBM * kBN * 2;
-    static constexpr int kKOff = kQBytes;
+    static constexpr int kStages = HD == 64 ? 4 : 2;
+    static constexpr int kKOff = kQT * kQBytes;
     static constexpr int kVOff = kKOff + kStages * kTileBytes;
-    static constexpr int kPOff = kVOff + kStages * kTileBytes;  // two P buffers
-    static constexpr int kSmem = kPOff + 2 * kPBytes + 1024;
+    static constexpr int kSmem = kVOff + kStages * kTileBytes + 1024;
     static constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);   // B = K tile, K-major
     static constexpr uint32_t kIdescPV = idesc_bf16_f32(kBM, HD, 1);   // B = V tile, MN-major
+    static constexpr uint32_t kOCol = kQT * kBN;                       // first O column
+    static_assert(kOCol + kQT * HD <= kTmemCols, "TMEM budget");
 };
 
 struct PrefillParams {
@@ -58,7 +66,7 @@ struct PrefillParams {
     const int *start_pos;
     int batch, tokens;
     int64_t pool_rows, num_blocks;
-    int num_layers, layer, num_q_heads, num_kv_heads, group, n_qtiles;
+    int num_layers, layer, num_q_heads, num_kv_heads, group, n_qblocks;
     float scale_log2;
     int *status;
 };
@@ -80,32 +88,41 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
     constexpr int S = Cfg::kStages;
     __shared__ __align__(8) uint64_t q_full;
     __shared__ __align__(8) uint64_t k_full[S], v_full[S], kv_empty[S];
-    __shared__ __align__(8) uint64_t s_full[2], s_free[2];
-    __shared__ __align__(8) uint64_t p_full[2], pv_done[2];  // per P buffer: tile t uses t % 2
+    __shared__ __align__(8) uint64_t s_full[kQT], p_full[kQT], pv_done[kQT];
     __shared__ uint32_t tmem_base_sh;
     __shared__ int s_abort;
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // heaviest query tiles (most key tiles) first
-    const int per_tile = p.num_q_heads * p.batch;
-    const int m = p.n_qtiles - 1 - (int)blockIdx.x / per_tile;
-    const int rem = (int)blockIdx.x % per_tile;
+    // heaviest query blocks (most key tiles) first
+    const int per_blk = p.num_q_heads * p.batch;
+    const int m = p.n_qblocks - 1 - (int)blockIdx.x / per_blk;
+    const int rem = (int)blockIdx.x % per_blk;
     const int h = rem % p.num_q_heads, b = rem / p.num_q_heads;
     const int kvh = h / p.group;
     int start = __ldg(p.start_pos + b);
-    const int q0 = m * kBM;
-    const int q_rows = min(kBM, p.tokens - q0);
     if (start < 0 || (long long)start + p.tokens > (long long)p.table_stride * kBlockSize) {
         if (tid == 0 && m == 0 && h == 0) set_status(p.status, LC_DEV_BAD_POS);
         start = max(0, min(start, p.table_stride * kBlockSize - p.tokens));
     }
-    const int kv_end = start + q0 + q_rows;  // keys [0, kv_end) are needed
-    const int nkv = (kv_end + kBN - 1) / kBN;
+    const int q0 = m * kQT * kBM;
+    // per Q tile: query rows, keys [0, kv_end) needed, K/V tiles
+    int rows[kQT], nkv[kQT];
+    int nkv_all = 0, kv_end_all = 0;
+#pragma unroll
+    for (int t = 0; t < kQT; ++t) {
+        rows[t] = max(0, min(kBM, p.tokens - (q0 + t * kBM)));
+        const int kv_end = rows[t] > 0 ? start + q0 + t * kBM + rows[t] : 0;
+        nkv[t] = (kv_end + kBN - 1) / kBN;
+        if (rows[t] > 0) {
+            nkv_all = nkv[t];
+            kv_end_all = kv_end;
+        }
+    }
 
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *gen = smem_raw + (base - smem_u32(smem_raw));
-    const uint32_t sQ = base, sK = base + Cfg::kKOff, sV = base + Cfg::kVOff, sP = base + Cfg::kPOff;
+    const uint32_t sQ = base, sK = base + Cfg::kKOff, sV = base + Cfg::kVOff;
 
     if (tid == 0) {
         mbar_init(&q_full, 1);
@@ -114,13 +131,10 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             mbar_init(&v_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], kBM);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&p_full[i], kBM);
-            mbar_init(&pv_done[i], 1);
+        for (int t = 0; t < kQT; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&p_full[t], kBM);
+            mbar_init(&pv_done[t], 1);
         }
         s_abort = 0;
         fence_barrier_init();
@@ -140,27 +154,34 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             prefetch_tensormap(&tm_q);
             prefetch_tensormap(&tm_k);
             prefetch_tensormap(&tm_v);
-            mbar_arrive_expect_tx(&q_full, Cfg::kQBytes);
+            int nq = 0;
 #pragma unroll
-            for (int hh = 0; hh < Cfg::kHalves; ++hh)
-                tma_load_2d(gen + hh * 16384, &tm_q, h * HD + hh * 64, b * p.tokens + q0, &q_full);
+            for (int t = 0; t < kQT; ++t) nq += rows[t] > 0;
+            mbar_arrive_expect_tx(&q_full, (uint32_t)(nq * Cfg::kQBytes));
+#pragma unroll
+            for (int t = 0; t < kQT; ++t)
+                if (rows[t] > 0)
+#pragma unroll
+                    for (int hh = 0; hh < Cfg::kHalves; ++hh)
+                        tma_load_2d(gen + t * Cfg::kQBytes + hh * 16384, &tm_q, h * HD + hh * 64,
+                                    b * p.tokens + q0 + t * kBM, &q_full);
             const int *trow = p.tables + (int64_t)b * p.table_stride;
-            const int pages_needed = (kv_end + kBlockSize - 1) / kBlockSize;
-            for (int j = 0; j < nkv; ++j) {
+            const int pages_needed = (kv_end_all + kBlockSize - 1) / kBlockSize;
+            for (int j = 0; j < nkv_all; ++j) {
                 const int s = j % S;
                 if (j >= S &&
                     !mbar_wait_bounded(&kv_empty[s], ((j / S) - 1) & 1, &s_abort, p.status))
                     break;
-                int64_t rows[kBN / kBlockSize];
+                int64_t prow[kBN / kBlockSize];
 #pragma unroll
                 for (int pg = 0; pg < kBN / kBlockSize; ++pg) {
                     const int logical = j * (kBN / kBlockSize) + pg;
                     const int phys = logical < pages_needed ? __ldg(trow + logical) : -1;
                     if (phys >= 0 && phys < p.num_blocks) {
-                        rows[pg] = page_row(phys, p.layer, kvh, p.num_layers, p.num_kv_heads);
+                        prow[pg] = page_row(phys, p.layer, kvh, p.num_layers, p.num_kv_heads);
                     } else {
                         if (logical < pages_needed) set_status(p.status, LC_DEV_BAD_BLOCK);
-                        rows[pg] = p.pool_rows;  // wholly out of bounds: zero fill
+                        prow[pg] = p.pool_rows;  // wholly out of bounds: zero fill
                     }
                 }
                 mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
@@ -169,99 +190,120 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
 #pragma unroll
                     for (int hh = 0; hh < Cfg::kHalves; ++hh)
                         tma_load_2d(gen + Cfg::kKOff + s * Cfg::kTileBytes + hh * 16384 + pg * 2048,
-                                    &tm_k, hh * 64, (int)rows[pg], &k_full[s]);
+                                    &tm_k, hh * 64, (int)prow[pg], &k_full[s]);
                 mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
 #pragma unroll
                 for (int pg = 0; pg < kBN / kBlockSize; ++pg)
 #pragma unroll
                     for (int hh = 0; hh < Cfg::kHalves; ++hh)
                         tma_load_2d(gen + Cfg::kVOff + s * Cfg::kTileBytes + hh * 16384 + pg * 2048,
-                                    &tm_v, hh * 64, (int)rows[pg], &v_full[s]);
+                                    &tm_v, hh * 64, (int)prow[pg], &v_full[s]);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA --
         if (lane == 0) {
             bool ok = mbar_wait_bounded(&q_full, 0, &s_abort, p.status);
-            tc_fence_after();
-            auto issue_s = [&](int j) -> bool {
-                const int s = j % S;
-                if (!mbar_wait_bounded(&k_full[s], (j / S) & 1, &s_abort, p.status)) return false;
-                if (j >= 2 &&
-                    !mbar_wait_bounded(&s_free[j & 1], ((j >> 1) - 1) & 1, &s_abort, p.status))
-                    return false;
+            int k_ready = -1;  // K tiles up to this one have landed
+            auto wait_k = [&](int j) -> bool {
+                if (j <= k_ready) return true;
+                if (!mbar_wait_bounded(&k_full[j % S], (j / S) & 1, &s_abort, p.status)) return false;
+                k_ready = j;
+                return true;
+            };
+            auto issue_s = [&](int t, int j) {
                 tc_fence_after();
-                const uint32_t kt = sK + s * Cfg::kTileBytes;
+                const uint32_t kt = sK + (j % S) * Cfg::kTileBytes, qt = sQ + t * Cfg::kQBytes;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16(tmem + (j & 1) * kBN, sw128_desc(sQ + off, 16, 1024),
+                    umma_bf16(tmem + t * kBN, sw128_desc(qt + off, 16, 1024),
                               sw128_desc(kt + off, 16, 1024), Cfg::kIdescS, kk > 0);
                 }
-                umma_commit(&s_full[j & 1]);
-                return true;
+                umma_commit(&s_full[t]);
             };
-            auto issue_pv = [&](int t) -> bool {
-                const int s = t % S;
-                if (!mbar_wait_bounded(&p_full[t & 1], (t >> 1) & 1, &s_abort, p.status)) return false;
-                if (!mbar_wait_bounded(&v_full[s], (t / S) & 1, &s_abort, p.status)) return false;
+            auto issue_pv = [&](int t, int j) {
                 tc_fence_after();
-                const uint32_t vt = sV + s * Cfg::kTileBytes;
+                const uint32_t vt = sV + (j % S) * Cfg::kTileBytes;
 #pragma unroll
-                for (int kk = 0; kk < kBN / 16; ++kk) {
-                    const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    umma_bf16(tmem + 2 * kBN, sw128_desc(sP + (t & 1) * Cfg::kPBytes + aoff, 16, 1024),
-                              sw128_desc(vt + kk * 2048, 16384, 1024), Cfg::kIdescPV,
-                              (t > 0 || kk > 0) ? 1u : 0u);
-                }
-                umma_commit(&pv_done[t & 1]);
-                umma_commit(&kv_empty[s]);
-                return true;
+                for (int kk = 0; kk < kBN / 16; ++kk)
+                    umma_bf16_tmem_a(tmem + Cfg::kOCol + t * HD, tmem + t * kBN + kk * 8,
+                                     sw128_desc(vt + kk * 2048, 16384, 1024), Cfg::kIdescPV,
+                                     (j > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&pv_done[t]);
             };
-            if (ok) ok = issue_s(0);
-            for (int j = 1; j < nkv && ok; ++j) ok = issue_s(j) && issue_pv(j - 1);
-            if (ok) ok = issue_pv(nkv - 1);
-            // Let every MMA this thread issued finish before the teardown.
-            if (ok) mbar_wait_bounded(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, &s_abort, p.status);
+            if (ok && nkv_all > 0) ok = wait_k(0);
+#pragma unroll
+            for (int t = 0; t < kQT; ++t)
+                if (ok && nkv[t] > 0) issue_s(t, 0);
+            for (int j = 0; j < nkv_all && ok; ++j) {
+                bool v_ready = false;
+#pragma unroll
+                for (int t = 0; t < kQT; ++t) {
+                    if (!ok || j >= nkv[t]) continue;
+                    if (!mbar_wait_bounded(&p_full[t], j & 1, &s_abort, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (!v_ready) {
+                        if (!mbar_wait_bounded(&v_full[j % S], (j / S) & 1, &s_abort, p.status)) {
+                            ok = false;
+                            break;
+                        }
+                        v_ready = true;
+                    }
+                    // PV_t reads P_t from the columns S_t(j + 1) then overwrites;
+                    // MMAs of one thread run in issue order.
+                    issue_pv(t, j);
+                    if (j + 1 < nkv[t]) {
+                        if (!wait_k(j + 1)) {
+                            ok = false;
+                            break;
+                        }
+                        issue_s(t, j + 1);
+                    }
+                }
+                if (ok) umma_commit(&kv_empty[j % S]);
+            }
         }
     } else {
         // -------------------------------------------------------- softmax --
-        const int quad = warp & 3;
+        const int t = (warp - 2) >> 2;  // Q tile of this warpgroup
+        static_assert(kQT == 2, "per-tile values below are selected for two tiles");
+        const int my_rows = t ? rows[1] : rows[0];
+        const int my_nkv = t ? nkv[1] : nkv[0];
+        const int quad = warp & 3;       // TMEM lane quadrant this warp may access
         const int row = quad * 32 + lane;
         const uint32_t tl = tmem + ((uint32_t)(quad * 32) << 16);
-        const int q_idx = q0 + row;
+        const uint32_t tS = tl + t * kBN, tO = tl + Cfg::kOCol + t * HD;
+        const int q_idx = q0 + t * kBM + row;
         const int q_pos = start + q_idx;
+        const int first_q = start + q0 + t * kBM;  // position of the tile's first query
         float m_ref = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int j = 0; j < nkv && ok; ++j) {
-            if (!mbar_wait_bounded(&s_full[j & 1], (j >> 1) & 1, &s_abort, p.status)) {
+        bool ok = my_rows > 0;
+        for (int j = 0; j < my_nkv && ok; ++j) {
+            if (!mbar_wait_bounded(&s_full[t], j & 1, &s_abort, p.status)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float sv[kBN];
-            {
-                uint32_t r[kBN / 32][32];
-#pragma unroll
-                for (int c = 0; c < kBN / 32; ++c) tmem_ld32(tl + (j & 1) * kBN + 32 * c, r[c]);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < kBN / 32; ++c)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) sv[32 * c + i] = u2f(r[c][i]);
-            }
-            tc_fence_before();
-            mbar_arrive(&s_free[j & 1]);
             const int key0 = j * kBN;
             // Causal mask only on tiles that reach past the tile's first query.
-            if (key0 + kBN - 1 > start + q0) {
-#pragma unroll
-                for (int c = 0; c < kBN; ++c)
-                    if (key0 + c > q_pos) sv[c] = -INFINITY;
-            }
+            const bool diag = key0 + kBN - 1 > first_q;
+            // Pass 1: the row max, 32 columns of S at a time (registers stay
+            // within what ten warps per SM allow).
             float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) mx[c & 3] = fmaxf(mx[c & 3], sv[c]);
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tS + 32 * c, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float v = (diag && key0 + 32 * c + i > q_pos) ? -INFINITY : u2f(r[i]);
+                    mx[i & 3] = fmaxf(mx[i & 3], v);
+                }
+            }
             // raw scores: scale > 0 keeps the order, so scale the max only
             const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
             // Running max with lazy rescaling: keep the reference max unless the
@@ -275,27 +317,34 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
                 m_ref = mt;
                 rescale = true;
             }
-            // P = 2^(s * scale - m_ref) (masked keys give 0): one FFMA and one
-            // ex2 per score, computed before any wait.
+            // Pass 2: P = 2^(s * scale - m_ref) (masked keys give 0), one FFMA
+            // and one ex2 per score, written back as bf16 pairs over the first
+            // 64 columns of S (keys 2c, 2c + 1 in column c: the A operand of
+            // PV). P chunk c lands in columns [16c, 16c + 16), below every S
+            // chunk still to be read.
             float rs[4] = {0.f, 0.f, 0.f, 0.f};
             const float neg_m = -m_ref;
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tS + 32 * c, r);
+                tmem_wait_ld();
+                uint32_t w[16];
 #pragma unroll
-            for (int c = 0; c < kBN; ++c) {
-                sv[c] = fast_exp2f(fmaf(sv[c], p.scale_log2, neg_m));
-                rs[c & 3] += sv[c];
+                for (int i = 0; i < 32; i += 2) {
+                    float e0 = fast_exp2f(fmaf(u2f(r[i]), p.scale_log2, neg_m));
+                    float e1 = fast_exp2f(fmaf(u2f(r[i + 1]), p.scale_log2, neg_m));
+                    if (diag && key0 + 32 * c + i > q_pos) e0 = 0.f;
+                    if (diag && key0 + 32 * c + i + 1 > q_pos) e1 = 0.f;
+                    rs[(i >> 1) & 3] += e0 + e1;
+                    w[i >> 1] = pack_bf16(e0, e1);
+                }
+                tmem_st16(tS + 16 * c, w);
             }
             l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
-            // P buffer j % 2 is free once PV_{j-2} is done; O may be rescaled
-            // only after PV_{j-1}.
-            if (j >= 2 &&
-                !mbar_wait_bounded(&pv_done[j & 1], ((j - 2) >> 1) & 1, &s_abort, p.status)) {
-                ok = false;
-                break;
-            }
-            const bool warp_rescale = __any_sync(0xffffffffu, rescale);
-            if (warp_rescale) {
-                if (!mbar_wait_bounded(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, &s_abort,
-                                       p.status)) {
+            if (__any_sync(0xffffffffu, rescale)) {
+                // O may be rescaled once PV(j - 1) is done with it.
+                if (!mbar_wait_bounded(&pv_done[t], (j - 1) & 1, &s_abort, p.status)) {
                     ok = false;
                     break;
                 }
@@ -303,34 +352,23 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
 #pragma unroll
                 for (int c = 0; c < HD / 32; ++c) {
                     uint32_t r[32];
-                    tmem_ld32(tl + 2 * kBN + 32 * c, r);
+                    tmem_ld32(tO + 32 * c, r);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) r[i] = f2u(u2f(r[i]) * alpha);
-                    tmem_st32(tl + 2 * kBN + 32 * c, r);
+                    tmem_st32(tO + 32 * c, r);
                 }
-                tmem_wait_st();
             }
-            // P row in bf16, 128-byte swizzled, K-major (keys).
-            uint8_t *pb = gen + Cfg::kPOff + (j & 1) * Cfg::kPBytes;
-#pragma unroll
-            for (int c16 = 0; c16 < kBN / 8; ++c16) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) w[e] = pack_bf16(sv[8 * c16 + 2 * e], sv[8 * c16 + 2 * e + 1]);
-                const int hh = c16 >> 3, cc = c16 & 7;
-                *reinterpret_cast<uint4 *>(pb + hh * 16384 + row * 128 + ((cc ^ (row & 7)) << 4)) =
-                    make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            // Keys past the prompt end in the last tile: zero their V rows so
-            // that 0 * (stale or non-finite pool contents) cannot reach O.
-            if (j == nkv - 1 && kv_end < key0 + kBN) {
+            // Keys past the prompt end in the CTA's last K/V tile: zero their V
+            // rows so that 0 * (stale or non-finite pool contents) cannot reach
+            // O. Each warpgroup that uses the tile does so before its PV.
+            if (j == nkv_all - 1 && kv_end_all < key0 + kBN) {
                 const int s = j % S;
                 if (!mbar_wait_bounded(&v_full[s], (j / S) & 1, &s_abort, p.status)) {
                     ok = false;
                     break;
                 }
-                if (row >= kv_end - key0) {
+                if (row >= kv_end_all - key0) {
 #pragma unroll
                     for (int hh = 0; hh < Cfg::kHalves; ++hh)
 #pragma unroll
@@ -339,21 +377,21 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
                                                        hh * 16384 + row * 128 + c * 16) =
                                 make_uint4(0, 0, 0, 0);
                 }
+                fence_proxy_async_smem();
             }
-            fence_proxy_async_smem();
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[j & 1]);
+            mbar_arrive(&p_full[t]);
         }
         // ----------------------------------------------------- epilogue --
-        if (ok && mbar_wait_bounded(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, &s_abort,
-                                    p.status)) {
+        if (ok && mbar_wait_bounded(&pv_done[t], (my_nkv - 1) & 1, &s_abort, p.status)) {
             tc_fence_after();
             const float inv = 1.f / l;
             bf16 *orow = p.out + (int64_t)(b * p.tokens + q_idx) * p.out_stride + (int64_t)h * HD;
-#pragma unroll
+#pragma unroll 1
             for (int c = 0; c < HD / 32; ++c) {
                 uint32_t r[32];
-                tmem_ld32(tl + 2 * kBN + 32 * c, r);
+                tmem_ld32(tO + 32 * c, r);
                 tmem_wait_ld();
                 if (q_idx < p.tokens) {
 #pragma unroll
@@ -396,7 +434,7 @@ int launch_prefill(const PrefillParams &prm, const void *q, int64_t q_stride,
     const int smem = PrefillCfg<HD>::kSmem;
     rc = ensure_smem_attr((const void *)paged_prefill_kernel<HD>, smem);
     if (rc) return rc;
-    const unsigned grid = (unsigned)prm.n_qtiles * prm.num_q_heads * prm.batch;
+    const unsigned grid = (unsigned)prm.n_qblocks * prm.num_q_heads * prm.batch;
     paged_prefill_kernel<HD><<<grid, kThreadsPf, smem, stream>>>(mq, mk, mv, prm);
     return launch_status();
 }
@@ -431,8 +469,8 @@ extern "C" int lc_paged_prefill(void *out, int64_t out_stride, const void *q, in
         return LC_ERR_INVALID_ARGUMENT;
     const int64_t pool_rows = num_blocks * num_layers * num_kv_heads * kBlockSize;
     if (pool_rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
-    const int64_t n_qtiles = (tokens_per_seq + kBM - 1) / kBM;
-    if (n_qtiles * num_q_heads * num_seqs >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
+    const int64_t n_qblocks = (tokens_per_seq + kQT * kBM - 1) / (kQT * kBM);
+    if (n_qblocks * num_q_heads * num_seqs >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
 
     PrefillParams prm{};
     prm.out = (bf16 *)out;
@@ -449,7 +487,7 @@ extern "C" int lc_paged_prefill(void *out, int64_t out_stride, const void *q, in
     prm.num_q_heads = num_q_heads;
     prm.num_kv_heads = num_kv_heads;
     prm.group = num_q_heads / num_kv_heads;
-    prm.n_qtiles = (int)n_qtiles;
+    prm.n_qblocks = (int)n_qblocks;
     prm.scale_log2 = sm_scale * 1.4426950408889634f;
     prm.status = dev_status;
     cudaStream_t s = as_stream(stream);
