@@ -127,15 +127,156 @@ __global__ void __launch_bounds__(256) rope_append_kernel(RopeAppendParams p) {
     }
 }
 
+// 8 consecutive bf16 (16 bytes) as floats, and back with RNE rounding.
+__device__ __forceinline__ void load8(const bf16 *src, float (&f)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(src);
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __low2float(h[i]);
+        f[2 * i + 1] = __high2float(h[i]);
+    }
+}
+__device__ __forceinline__ void store8(bf16 *dst, const float (&f)[8]) {
+    uint4 u;
+    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(dst) = u;
+}
+__device__ __forceinline__ void load8f(const float *src, float (&f)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(src)[0];
+    const float4 b = reinterpret_cast<const float4 *>(src)[1];
+    f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w, f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
+}
+
+// The same items with eight dims each (16-byte loads and stores), for callers
+// whose rows, biases, RoPE tables and pools are 16-byte aligned: item (head,
+// chunk) covers dims [8 chunk, 8 chunk + 8) of the first half and their
+// partners in the second. Per element the arithmetic is that of the kernel
+// above.
+__global__ void __launch_bounds__(256) rope_append_vec_kernel(RopeAppendParams p) {
+    const int half = p.head_dim >> 1;
+    const int cph = half >> 3;  // chunks of 8 dims per half
+    const int items_a = p.rope_q_heads * cph;
+    const int items_b = p.append ? p.num_kv_heads * cph : 0;
+    const int per_row = items_a + items_b;
+    const int64_t total = (int64_t)p.rows * per_row;
+    const int64_t stride_blk = (int64_t)kBlockSize * p.head_dim;  // between kv heads of a page
+    for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < total;
+         gi += (int64_t)gridDim.x * blockDim.x) {
+        const int row = (int)(gi / per_row);
+        const int item = (int)(gi - (int64_t)row * per_row);
+        const int pos = p.positions[row];
+        if (pos < 0) {
+            if (item == 0) set_status(p.status, LC_DEV_BAD_POS);
+            continue;
+        }
+        const int64_t roff = (int64_t)row * p.row_stride;
+        if (item < items_a) {
+            const int head = item / cph, d = (item - head * cph) * 8;
+            if (p.rope_rows >= 0 && pos >= p.rope_rows) {
+                if (item == 0) set_status(p.status, LC_DEV_BAD_POS);
+                continue;
+            }
+            float c[8], sn[8], x1[8], x2[8], b1[8], b2[8];
+            load8f(p.cos_t + (int64_t)pos * half + d, c);
+            load8f(p.sin_t + (int64_t)pos * half + d, sn);
+            const int i1 = head * p.head_dim + d, i2 = i1 + half;
+            bf16 *q = p.q + roff;
+            load8(q + i1, x1);
+            load8(q + i2, x2);
+            load8(p.q_bias + i1, b1);
+            load8(p.q_bias + i2, b2);
+            float o1[8], o2[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float v1 = __fadd_rn(x1[e], b1[e]), v2 = __fadd_rn(x2[e], b2[e]);
+                o1[e] = rot_sub(v1, c[e], v2, sn[e]);
+                o2[e] = rot_add(v1, sn[e], v2, c[e]);
+            }
+            store8(q + i1, o1);
+            store8(q + i2, o2);
+            if (head < p.rope_k_heads) {
+                bf16 *k = p.k + roff;
+                load8(k + i1, x1);
+                load8(k + i2, x2);
+                load8(p.k_bias + i1, b1);
+                load8(p.k_bias + i2, b2);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float k1 = __fadd_rn(x1[e], b1[e]), k2 = __fadd_rn(x2[e], b2[e]);
+                    o1[e] = rot_sub(k1, c[e], k2, sn[e]);
+                    o2[e] = rot_add(k1, sn[e], k2, c[e]);
+                }
+                store8(k + i1, o1);
+                store8(k + i2, o2);
+                if (p.append) {
+                    const int64_t base = append_base(p, row, pos);
+                    if (base >= 0) {
+                        bf16 *dst = p.k_pool + base + head * stride_blk;
+                        store8(dst + d, o1);
+                        store8(dst + d + half, o2);
+                    }
+                }
+            }
+        } else {
+            const int j = item - items_a;
+            const int head = j / cph, d = (j - head * cph) * 8;
+            const int64_t base = append_base(p, row, pos);
+            if (base < 0) continue;
+            const int i1 = head * p.head_dim + d, i2 = i1 + half;
+            const bf16 *v = p.v + roff;
+            const int64_t o = base + head * stride_blk;
+            float x1[8], x2[8], b1[8], b2[8];
+            load8(v + i1, x1);
+            load8(v + i2, x2);
+            load8(p.v_bias + i1, b1);
+            load8(p.v_bias + i2, b2);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                x1[e] = __fadd_rn(x1[e], b1[e]);
+                x2[e] = __fadd_rn(x2[e], b2[e]);
+            }
+            store8(p.v_pool + o + d, x1);
+            store8(p.v_pool + o + d + half, x2);
+            if (p.rope_k_heads == 0) {
+                const bf16 *k = p.k + roff;
+                *reinterpret_cast<uint4 *>(p.k_pool + o + d) = *reinterpret_cast<const uint4 *>(k + i1);
+                *reinterpret_cast<uint4 *>(p.k_pool + o + d + half) =
+                    *reinterpret_cast<const uint4 *>(k + i2);
+            }
+        }
+    }
+}
+
+bool vec_ok(const RopeAppendParams &p) {
+    auto a16 = [](const void *x) { return !x || ((uintptr_t)x & 15) == 0; };
+    return (p.head_dim & 15) == 0 && (p.row_stride & 7) == 0 && a16(p.q) && a16(p.k) &&
+           a16(p.v) && a16(p.q_bias) && a16(p.k_bias) && a16(p.v_bias) && a16(p.cos_t) &&
+           a16(p.sin_t) && a16(p.k_pool) && a16(p.v_pool);
+}
+
 int launch(const RopeAppendParams &p, cudaStream_t stream) {
+    const int threads = 256;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    if (vec_ok(p)) {
+        const int cph = p.head_dim / 16;
+        const int64_t per_row =
+            (int64_t)p.rope_q_heads * cph + (p.append ? (int64_t)p.num_kv_heads * cph : 0);
+        const int64_t total = per_row * p.rows;
+        if (total == 0) return LC_OK;
+        int64_t blocks = (total + threads - 1) / threads;
+        if (blocks > cap) blocks = cap;
+        rope_append_vec_kernel<<<(unsigned)blocks, threads, 0, stream>>>(p);
+        return launch_status();
+    }
     const int half = p.head_dim / 2;
     const int64_t per_row =
         (int64_t)p.rope_q_heads * half + (p.append ? (int64_t)p.num_kv_heads * half : 0);
     const int64_t total = per_row * p.rows;
     if (total == 0) return LC_OK;
-    const int threads = 256;
     int64_t blocks = (total + threads - 1) / threads;
-    const int64_t cap = (int64_t)sm_count() * 16;
     if (blocks > cap) blocks = cap;
     rope_append_kernel<<<(unsigned)blocks, threads, 0, stream>>>(p);
     return launch_status();

@@ -18,14 +18,18 @@ def biases(rng, hq, hkv, hd):
     return randn_bf16(rng, (hq * hd,)), randn_bf16(rng, (hkv * hd,)), randn_bf16(rng, (hkv * hd,))
 
 
-@pytest.mark.parametrize("hq,hkv,hd,T", [(14, 2, 64, 1), (28, 4, 128, 1), (12, 2, 128, 37),
-                                         (64, 8, 128, 1), (16, 2, 64, 20)])
-def test_rope_append_bit_exact(hq, hkv, hd, T):
+# pad 8 keeps rows 16-byte aligned (the 16-byte vector kernel); pad 4 does not
+# (the element-wise kernel). Both must write the same bits.
+@pytest.mark.parametrize("hq,hkv,hd,T,pad", [(14, 2, 64, 1, 8), (28, 4, 128, 1, 8),
+                                             (12, 2, 128, 37, 8), (64, 8, 128, 1, 8),
+                                             (16, 2, 64, 20, 8), (12, 2, 128, 37, 4),
+                                             (14, 2, 64, 9, 4)])
+def test_rope_append_bit_exact(hq, hkv, hd, T, pad):
     rng = np.random.default_rng(hq + T)
     B = 5
     start = rng.integers(0, 3000, B).astype(np.int32)
     case = make_case(B, hq, hkv, hd, start + T, seed=hq + T + 1)
-    row = (hq + 2 * hkv) * hd + 8  # padded row stride
+    row = (hq + 2 * hkv) * hd + pad  # padded row stride
     qkv = randn_bf16(rng, (B * T, row))
     qb, kb, vb = biases(rng, hq, hkv, hd)
     cos, sin = O.rope_table(4096, hd, 1e6)
