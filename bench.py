@@ -733,6 +733,8 @@ def causal_flops(batch, tokens, hq, hd, start=0):
 def run_prefill_bench(args, rank, world, local):
     import lucciola as L
     label, B, hq, hkv, hd, layers, T = PREFILL[args.config]
+    if args.layers:  # fewer layers for profiling captures; per-layer work unchanged
+        layers = args.layers
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     gen = torch.Generator(device=device)
@@ -837,7 +839,8 @@ def main():
                          "step satisfies mode 2's contract: between layers nothing writes the "
                          "context lengths, tables or the next layer's cached pages")
     ap.add_argument("--layers", type=int, default=None,
-                    help="kernel mode only: fewer layers (smaller pools) for profiler captures")
+                    help="kernel mode and the prefill config only: fewer layers (smaller "
+                         "pools) for profiler captures")
     ap.add_argument("--unfused", action="store_true",
                     help="two launches per layer (lc_rope_append, lc_paged_decode)")
     ap.add_argument("--partition", type=int, default=None,
@@ -845,8 +848,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.layers is not None and args.mode != "kernel":
-        ap.error("--layers changes the workload; it is for --mode kernel (profiling) only")
+    if args.layers is not None and args.mode != "kernel" and args.config not in PREFILL:
+        ap.error("--layers changes the workload; it is for --mode kernel and the prefill "
+                 "config (profiling) only")
     rank, world, local = env_dist()
     if args.config in HEAD_SHARDED:
         if args.impl == "reference":

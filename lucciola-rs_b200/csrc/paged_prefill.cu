@@ -79,6 +79,54 @@ __device__ __forceinline__ float fast_exp2f(float x) {
     return y;
 }
 
+// Softmax helpers, one thread per query row over the 128 columns of its S
+// row in TMEM (32 at a time). Keys with index > kq are masked when DIAG.
+// row_max: the raw (unscaled) row max.
+template <bool DIAG>
+__device__ __forceinline__ float row_max(uint32_t tS, int kq) {
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+    for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + 32 * c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float v = (DIAG && 32 * c + i > kq) ? -INFINITY : u2f(r[i]);
+            mx[i & 3] = fmaxf(mx[i & 3], v);
+        }
+    }
+    return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// row_exp: P = 2^(s * scale - m) with one FFMA and one ex2 per score (masked
+// scores are -inf and give 0), packed as bf16 pairs into w (keys 2c, 2c + 1 in
+// w[c]); `sum` gets their fp32 sum. Returns the raw row max.
+template <bool DIAG>
+__device__ __forceinline__ float row_exp(uint32_t tS, int kq, float scale, float neg_m,
+                                         uint32_t (&w)[kBN / 2], float &sum) {
+    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + 32 * c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+            const float s0 = (DIAG && 32 * c + i > kq) ? -INFINITY : u2f(r[i]);
+            const float s1 = (DIAG && 32 * c + i + 1 > kq) ? -INFINITY : u2f(r[i + 1]);
+            mx[(i >> 1) & 3] = fmaxf(mx[(i >> 1) & 3], fmaxf(s0, s1));
+            const float e0 = fast_exp2f(fmaf(s0, scale, neg_m));
+            const float e1 = fast_exp2f(fmaf(s1, scale, neg_m));
+            rs[(i >> 1) & 3] += e0 + e1;
+            w[16 * c + (i >> 1)] = pack_bf16(e0, e1);
+        }
+    }
+    sum = (rs[0] + rs[1]) + (rs[2] + rs[3]);
+    return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kThreadsPf, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -290,58 +338,32 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             const int key0 = j * kBN;
             // Causal mask only on tiles that reach past the tile's first query.
             const bool diag = key0 + kBN - 1 > first_q;
-            // Pass 1: the row max, 32 columns of S at a time (registers stay
-            // within what ten warps per SM allow).
-            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tS + 32 * c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float v = (diag && key0 + 32 * c + i > q_pos) ? -INFINITY : u2f(r[i]);
-                    mx[i & 3] = fmaxf(mx[i & 3], v);
-                }
-            }
-            // raw scores: scale > 0 keeps the order, so scale the max only
-            const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * p.scale_log2;
-            // Running max with lazy rescaling: keep the reference max unless the
-            // tile's max exceeds it by more than 2^8; then O and l are rescaled.
-            float alpha = 1.f;
-            bool rescale = false;
+            const int kq = q_pos - key0;  // keys of the tile past this index are masked
+            // The tile's first tile has no reference max yet: take the row max
+            // first. Later tiles exponentiate against the running reference max
+            // in one pass and redo the row only when its max grew by > 2^8.
             if (j == 0) {
-                m_ref = mt;
-            } else if (mt > m_ref + kRescaleLog2) {
-                alpha = fast_exp2f(m_ref - mt);
-                m_ref = mt;
-                rescale = true;
+                const float mraw = diag ? row_max<true>(tS, kq) : row_max<false>(tS, kq);
+                m_ref = mraw * p.scale_log2;
             }
-            // Pass 2: P = 2^(s * scale - m_ref) (masked keys give 0), one FFMA
-            // and one ex2 per score, written back as bf16 pairs over the first
-            // 64 columns of S (keys 2c, 2c + 1 in column c: the A operand of
-            // PV). P chunk c lands in columns [16c, 16c + 16), below every S
-            // chunk still to be read.
-            float rs[4] = {0.f, 0.f, 0.f, 0.f};
-            const float neg_m = -m_ref;
+            uint32_t w[kBN / 2];
+            float sum = 0.f, alpha = 1.f;
+            bool rescale = false;
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tS + 32 * c, r);
-                tmem_wait_ld();
-                uint32_t w[16];
-#pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    float e0 = fast_exp2f(fmaf(u2f(r[i]), p.scale_log2, neg_m));
-                    float e1 = fast_exp2f(fmaf(u2f(r[i + 1]), p.scale_log2, neg_m));
-                    if (diag && key0 + 32 * c + i > q_pos) e0 = 0.f;
-                    if (diag && key0 + 32 * c + i + 1 > q_pos) e1 = 0.f;
-                    rs[(i >> 1) & 3] += e0 + e1;
-                    w[i >> 1] = pack_bf16(e0, e1);
+            for (int pass = 0; pass < 2; ++pass) {
+                const float mraw = diag ? row_exp<true>(tS, kq, p.scale_log2, -m_ref, w, sum)
+                                        : row_exp<false>(tS, kq, p.scale_log2, -m_ref, w, sum);
+                if (pass) break;
+                const float mt = mraw * p.scale_log2;
+                if (mt > m_ref + kRescaleLog2) {
+                    alpha = fast_exp2f(m_ref - mt);
+                    m_ref = mt;
+                    rescale = true;
                 }
-                tmem_st16(tS + 16 * c, w);
+                if (!__any_sync(0xffffffffu, rescale)) break;  // else redo: S is intact
             }
-            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            l = l * alpha + sum;
+
             if (__any_sync(0xffffffffu, rescale)) {
                 // O may be rescaled once PV(j - 1) is done with it.
                 if (!mbar_wait_bounded(&pv_done[t], (j - 1) & 1, &s_abort, p.status)) {
@@ -379,6 +401,10 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
                 }
                 fence_proxy_async_smem();
             }
+            // P as bf16 pairs over the first 64 columns of S (keys 2c, 2c + 1 in
+            // column c): the A operand of PV.
+            tmem_st32(tS, *reinterpret_cast<const uint32_t(*)[32]>(&w[0]));
+            tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&w[32]));
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&p_full[t]);
