@@ -41,7 +41,9 @@ constexpr int kQT = 2;    // Q tiles per CTA
 constexpr int kBN = 128;  // keys per K/V tile (8 pages)
 constexpr int kThreadsPf = (2 + 4 * kQT) * 32;
 constexpr uint32_t kTmemCols = 512;
-constexpr float kRescaleLog2 = 8.f;  // rescale O only when a row max grows by > 2^8
+// A row is rescaled only when its scores outgrow the reference max by more than
+// 2^kGrowLog2: P then stays below 2^64 in bf16, and O and l (fp32) below 2^100.
+constexpr float kGrowSum = 18446744073709551616.f;  // 2^64
 
 template <int HD>
 struct PrefillCfg {
@@ -101,30 +103,34 @@ __device__ __forceinline__ float row_max(uint32_t tS, int kq) {
 
 // row_exp: P = 2^(s * scale - m) with one FFMA and one ex2 per score (masked
 // scores are -inf and give 0), packed as bf16 pairs into w (keys 2c, 2c + 1 in
-// w[c]); `sum` gets their fp32 sum. Returns the raw row max.
+// w[c]). Returns their fp32 sum.
+template <bool DIAG>
+__device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], int c, int kq, float scale,
+                                          float neg_m, uint32_t (&w)[kBN / 2], float (&rs)[4]) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+        const float s0 = (DIAG && 32 * c + i > kq) ? -INFINITY : u2f(r[i]);
+        const float s1 = (DIAG && 32 * c + i + 1 > kq) ? -INFINITY : u2f(r[i + 1]);
+        const float e0 = fast_exp2f(fmaf(s0, scale, neg_m));
+        const float e1 = fast_exp2f(fmaf(s1, scale, neg_m));
+        rs[(i >> 1) & 3] += e0 + e1;
+        w[16 * c + (i >> 1)] = pack_bf16(e0, e1);
+    }
+}
+
 template <bool DIAG>
 __device__ __forceinline__ float row_exp(uint32_t tS, int kq, float scale, float neg_m,
-                                         uint32_t (&w)[kBN / 2], float &sum) {
-    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                                         uint32_t (&w)[kBN / 2]) {
+    static_assert(kBN == 128, "four 32-column chunks");
     float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < kBN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tS + 32 * c, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-            const float s0 = (DIAG && 32 * c + i > kq) ? -INFINITY : u2f(r[i]);
-            const float s1 = (DIAG && 32 * c + i + 1 > kq) ? -INFINITY : u2f(r[i + 1]);
-            mx[(i >> 1) & 3] = fmaxf(mx[(i >> 1) & 3], fmaxf(s0, s1));
-            const float e0 = fast_exp2f(fmaf(s0, scale, neg_m));
-            const float e1 = fast_exp2f(fmaf(s1, scale, neg_m));
-            rs[(i >> 1) & 3] += e0 + e1;
-            w[16 * c + (i >> 1)] = pack_bf16(e0, e1);
-        }
+        tmem_wait_ld_regs(r);
+        exp_chunk<DIAG>(r, c, kq, scale, neg_m, w, rs);
     }
-    sum = (rs[0] + rs[1]) + (rs[2] + rs[3]);
-    return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+    return (rs[0] + rs[1]) + (rs[2] + rs[3]);
 }
 
 template <int HD>
@@ -339,28 +345,32 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             // Causal mask only on tiles that reach past the tile's first query.
             const bool diag = key0 + kBN - 1 > first_q;
             const int kq = q_pos - key0;  // keys of the tile past this index are masked
-            // The tile's first tile has no reference max yet: take the row max
-            // first. Later tiles exponentiate against the running reference max
-            // in one pass and redo the row only when its max grew by > 2^8.
-            if (j == 0) {
-                const float mraw = diag ? row_max<true>(tS, kq) : row_max<false>(tS, kq);
-                m_ref = mraw * p.scale_log2;
-            }
+            // The first tile sets the reference max m_ref (a max pass first).
+            // Later tiles exponentiate against it in one pass with no max at
+            // all: a row whose scores outgrew m_ref by more than 2^kGrowLog2
+            // shows it in its sum (inf included); then its true max is taken,
+            // O and l are rescaled and the row is redone (S is intact in TMEM).
             uint32_t w[kBN / 2];
-            float sum = 0.f, alpha = 1.f;
-            bool rescale = false;
+            float alpha = 1.f, sum = 0.f;
+            bool rescale = false, grew = false, need_max = j == 0;
 #pragma unroll 1
             for (int pass = 0; pass < 2; ++pass) {
-                const float mraw = diag ? row_exp<true>(tS, kq, p.scale_log2, -m_ref, w, sum)
-                                        : row_exp<false>(tS, kq, p.scale_log2, -m_ref, w, sum);
-                if (pass) break;
-                const float mt = mraw * p.scale_log2;
-                if (mt > m_ref + kRescaleLog2) {
-                    alpha = fast_exp2f(m_ref - mt);
-                    m_ref = mt;
-                    rescale = true;
+                if (need_max) {
+                    const float mt =
+                        (diag ? row_max<true>(tS, kq) : row_max<false>(tS, kq)) * p.scale_log2;
+                    if (j == 0) {
+                        m_ref = mt;
+                    } else if (grew) {
+                        alpha = fast_exp2f(m_ref - mt);
+                        m_ref = mt;
+                        rescale = true;
+                    }
                 }
-                if (!__any_sync(0xffffffffu, rescale)) break;  // else redo: S is intact
+                sum = diag ? row_exp<true>(tS, kq, p.scale_log2, -m_ref, w)
+                           : row_exp<false>(tS, kq, p.scale_log2, -m_ref, w);
+                grew = !(sum <= kGrowSum);
+                if (!__any_sync(0xffffffffu, grew)) break;
+                need_max = true;
             }
             l = l * alpha + sum;
 

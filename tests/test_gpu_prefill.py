@@ -56,6 +56,34 @@ def test_prefill_matches_per_token_reference(hq, hkv, hd, T, start):
     assert max_err(out, ref) <= ATTN_ATOL
 
 
+def test_prefill_score_growth_rescales():
+    """Keys whose scores outgrow the running reference max by far more than the
+    rescale bound (K of tokens >= 300 scaled by 100): the kernel must notice it
+    from the row sums, rescale O and l, and still match the oracle."""
+    hq, hkv, hd, T = 12, 2, 128, 520
+    start = np.array([0], np.int32)
+    case = make_case(1, hq, hkv, hd, start + T, seed=21)
+    kf = O.bf16_to_f32(case.k_pool)
+    for tok in range(300, T):
+        blk = case.tables[0, tok // 16]
+        kf[blk, case.layer, :, tok % 16, :] *= 100.0
+    case.k_pool = O.f32_to_bf16(kf)
+    rng = np.random.default_rng(22)
+    q = randn_bf16(rng, (T, hq * hd))
+    out = torch.full((T, hq * hd), float("nan"), dtype=torch.bfloat16, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    L.paged_prefill(out, to_device(q), to_device(case.k_pool), to_device(case.v_pool),
+                    case.num_blocks, case.num_layers, case.layer, hq, hkv, hd,
+                    to_device(case.tables), to_device(start), T, 0, dev_status=st)
+    torch.cuda.synchronize()
+    ref = O.paged_prefill(q, case.k_pool, case.v_pool, case.layer, hq, hkv, hd, case.tables,
+                          start, T, case.num_layers, threads=8)
+    got = from_device(out)
+    assert int(st.item()) == 0
+    assert np.isfinite(O.bf16_to_f32(got)).all()
+    assert max_err(got, ref) <= ATTN_ATOL
+
+
 def test_prefill_strided_q_rows():
     out, ref, st = run_prefill(12, 2, 128, 140, [0, 9], seed=3, q_stride_pad=4 * 128)
     assert st == 0 and max_err(out, ref) <= ATTN_ATOL
