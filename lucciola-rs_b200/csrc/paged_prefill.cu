@@ -39,7 +39,8 @@ namespace {
 constexpr int kBM = 128;  // queries per Q tile (one TMEM lane each)
 constexpr int kQT = 2;    // Q tiles per CTA
 constexpr int kBN = 128;  // keys per K/V tile (8 pages)
-constexpr int kThreadsPf = (2 + 4 * kQT) * 32;
+constexpr int kThreadsPf = (3 + 4 * kQT) * 32;  // K/Q TMA, MMA, softmax x 8, V TMA
+constexpr int kVWarp = 2 + 4 * kQT;               // warp 10: V TMA
 constexpr uint32_t kTmemCols = 512;
 // A row is rescaled only when its scores outgrow the reference max by more than
 // 2^kGrowLog2: P then stays below 2^64 in bf16, and O and l (fp32) below 2^100.
@@ -50,10 +51,13 @@ struct PrefillCfg {
     static constexpr int kHalves = HD / 64;
     static constexpr int kQBytes = kBM * HD * 2;     // one Q tile
     static constexpr int kTileBytes = kBN * HD * 2;  // one K or V tile
-    static constexpr int kStages = HD == 64 ? 4 : 2;
+    // K is released as soon as both S products of a tile are done, V only
+    // after both PV products: K gets the deeper ring.
+    static constexpr int kKStages = HD == 64 ? 4 : 3;
+    static constexpr int kVStages = HD == 64 ? 4 : 2;
     static constexpr int kKOff = kQT * kQBytes;
-    static constexpr int kVOff = kKOff + kStages * kTileBytes;
-    static constexpr int kSmem = kVOff + kStages * kTileBytes + 1024;
+    static constexpr int kVOff = kKOff + kKStages * kTileBytes;
+    static constexpr int kSmem = kVOff + kVStages * kTileBytes + 1024;
     static constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, 0);   // B = K tile, K-major
     static constexpr uint32_t kIdescPV = idesc_bf16_f32(kBM, HD, 1);   // B = V tile, MN-major
     static constexpr uint32_t kOCol = kQT * kBN;                       // first O column
@@ -139,9 +143,9 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const PrefillParams p) {
     using Cfg = PrefillCfg<HD>;
-    constexpr int S = Cfg::kStages;
+    constexpr int SK = Cfg::kKStages, SV = Cfg::kVStages;
     __shared__ __align__(8) uint64_t q_full;
-    __shared__ __align__(8) uint64_t k_full[S], v_full[S], kv_empty[S];
+    __shared__ __align__(8) uint64_t k_full[SK], k_empty[SK], v_full[SV], v_empty[SV];
     __shared__ __align__(8) uint64_t s_full[kQT], p_full[kQT], pv_done[kQT];
     __shared__ uint32_t tmem_base_sh;
     __shared__ int s_abort;
@@ -180,10 +184,13 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
 
     if (tid == 0) {
         mbar_init(&q_full, 1);
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < SK; ++s) {
             mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < SV; ++s) {
             mbar_init(&v_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&v_empty[s], 1);
         }
         for (int t = 0; t < kQT; ++t) {
             mbar_init(&s_full[t], 1);
@@ -202,29 +209,38 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
 
-    if (warp == 0) {
+    if (warp == 0 || warp == kVWarp) {
         // ------------------------------------------------------------ TMA --
+        // Warp 0 loads both Q tiles and the K tiles, warp 10 the V tiles; each
+        // K or V tile is 8 pages found through the block table.
         if (lane == 0) {
-            prefetch_tensormap(&tm_q);
-            prefetch_tensormap(&tm_k);
-            prefetch_tensormap(&tm_v);
-            int nq = 0;
+            const bool is_k = warp == 0;
+            const CUtensorMap *tm = is_k ? &tm_k : &tm_v;
+            prefetch_tensormap(tm);
+            if (is_k) {
+                prefetch_tensormap(&tm_q);
+                int nq = 0;
 #pragma unroll
-            for (int t = 0; t < kQT; ++t) nq += rows[t] > 0;
-            mbar_arrive_expect_tx(&q_full, (uint32_t)(nq * Cfg::kQBytes));
+                for (int t = 0; t < kQT; ++t) nq += rows[t] > 0;
+                mbar_arrive_expect_tx(&q_full, (uint32_t)(nq * Cfg::kQBytes));
 #pragma unroll
-            for (int t = 0; t < kQT; ++t)
-                if (rows[t] > 0)
+                for (int t = 0; t < kQT; ++t)
+                    if (rows[t] > 0)
 #pragma unroll
-                    for (int hh = 0; hh < Cfg::kHalves; ++hh)
-                        tma_load_2d(gen + t * Cfg::kQBytes + hh * 16384, &tm_q, h * HD + hh * 64,
-                                    b * p.tokens + q0 + t * kBM, &q_full);
+                        for (int hh = 0; hh < Cfg::kHalves; ++hh)
+                            tma_load_2d(gen + t * Cfg::kQBytes + hh * 16384, &tm_q, h * HD + hh * 64,
+                                        b * p.tokens + q0 + t * kBM, &q_full);
+            }
+            const int ns = is_k ? SK : SV;
+            uint64_t *full = is_k ? k_full : v_full;
+            uint64_t *empty = is_k ? k_empty : v_empty;
+            const int off = is_k ? Cfg::kKOff : Cfg::kVOff;
             const int *trow = p.tables + (int64_t)b * p.table_stride;
             const int pages_needed = (kv_end_all + kBlockSize - 1) / kBlockSize;
             for (int j = 0; j < nkv_all; ++j) {
-                const int s = j % S;
-                if (j >= S &&
-                    !mbar_wait_bounded(&kv_empty[s], ((j / S) - 1) & 1, &s_abort, p.status))
+                const int s = j % ns;
+                if (j >= ns &&
+                    !mbar_wait_bounded(&empty[s], ((j / ns) - 1) & 1, &s_abort, p.status))
                     break;
                 int64_t prow[kBN / kBlockSize];
 #pragma unroll
@@ -234,24 +250,17 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
                     if (phys >= 0 && phys < p.num_blocks) {
                         prow[pg] = page_row(phys, p.layer, kvh, p.num_layers, p.num_kv_heads);
                     } else {
-                        if (logical < pages_needed) set_status(p.status, LC_DEV_BAD_BLOCK);
+                        if (is_k && logical < pages_needed) set_status(p.status, LC_DEV_BAD_BLOCK);
                         prow[pg] = p.pool_rows;  // wholly out of bounds: zero fill
                     }
                 }
-                mbar_arrive_expect_tx(&k_full[s], Cfg::kTileBytes);
+                mbar_arrive_expect_tx(&full[s], Cfg::kTileBytes);
 #pragma unroll
                 for (int pg = 0; pg < kBN / kBlockSize; ++pg)
 #pragma unroll
                     for (int hh = 0; hh < Cfg::kHalves; ++hh)
-                        tma_load_2d(gen + Cfg::kKOff + s * Cfg::kTileBytes + hh * 16384 + pg * 2048,
-                                    &tm_k, hh * 64, (int)prow[pg], &k_full[s]);
-                mbar_arrive_expect_tx(&v_full[s], Cfg::kTileBytes);
-#pragma unroll
-                for (int pg = 0; pg < kBN / kBlockSize; ++pg)
-#pragma unroll
-                    for (int hh = 0; hh < Cfg::kHalves; ++hh)
-                        tma_load_2d(gen + Cfg::kVOff + s * Cfg::kTileBytes + hh * 16384 + pg * 2048,
-                                    &tm_v, hh * 64, (int)prow[pg], &v_full[s]);
+                        tma_load_2d(gen + off + s * Cfg::kTileBytes + hh * 16384 + pg * 2048, tm,
+                                    hh * 64, (int)prow[pg], &full[s]);
             }
         }
     } else if (warp == 1) {
@@ -261,13 +270,13 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             int k_ready = -1;  // K tiles up to this one have landed
             auto wait_k = [&](int j) -> bool {
                 if (j <= k_ready) return true;
-                if (!mbar_wait_bounded(&k_full[j % S], (j / S) & 1, &s_abort, p.status)) return false;
+                if (!mbar_wait_bounded(&k_full[j % SK], (j / SK) & 1, &s_abort, p.status)) return false;
                 k_ready = j;
                 return true;
             };
             auto issue_s = [&](int t, int j) {
                 tc_fence_after();
-                const uint32_t kt = sK + (j % S) * Cfg::kTileBytes, qt = sQ + t * Cfg::kQBytes;
+                const uint32_t kt = sK + (j % SK) * Cfg::kTileBytes, qt = sQ + t * Cfg::kQBytes;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -278,7 +287,7 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             };
             auto issue_pv = [&](int t, int j) {
                 tc_fence_after();
-                const uint32_t vt = sV + (j % S) * Cfg::kTileBytes;
+                const uint32_t vt = sV + (j % SV) * Cfg::kTileBytes;
 #pragma unroll
                 for (int kk = 0; kk < kBN / 16; ++kk)
                     umma_bf16_tmem_a(tmem + Cfg::kOCol + t * HD, tmem + t * kBN + kk * 8,
@@ -290,6 +299,7 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
 #pragma unroll
             for (int t = 0; t < kQT; ++t)
                 if (ok && nkv[t] > 0) issue_s(t, 0);
+            if (ok && nkv_all > 0) umma_commit(&k_empty[0]);  // K(0) is done once both S(0) are
             for (int j = 0; j < nkv_all && ok; ++j) {
                 bool v_ready = false;
 #pragma unroll
@@ -300,7 +310,7 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
                         break;
                     }
                     if (!v_ready) {
-                        if (!mbar_wait_bounded(&v_full[j % S], (j / S) & 1, &s_abort, p.status)) {
+                        if (!mbar_wait_bounded(&v_full[j % SV], (j / SV) & 1, &s_abort, p.status)) {
                             ok = false;
                             break;
                         }
@@ -317,12 +327,14 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
                         issue_s(t, j + 1);
                     }
                 }
-                if (ok) umma_commit(&kv_empty[j % S]);
+                if (!ok) break;
+                umma_commit(&v_empty[j % SV]);                            // both PV(j) issued
+                if (j + 1 < nkv_all) umma_commit(&k_empty[(j + 1) % SK]);  // both S(j + 1) issued
             }
         }
     } else {
         // -------------------------------------------------------- softmax --
-        const int t = (warp - 2) >> 2;  // Q tile of this warpgroup
+        const int t = (warp - 2) >> 2;  // Q tile of this warpgroup (warps 2-9)
         static_assert(kQT == 2, "per-tile values below are selected for two tiles");
         const int my_rows = t ? rows[1] : rows[0];
         const int my_nkv = t ? nkv[1] : nkv[0];
@@ -395,8 +407,8 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             // rows so that 0 * (stale or non-finite pool contents) cannot reach
             // O. Each warpgroup that uses the tile does so before its PV.
             if (j == nkv_all - 1 && kv_end_all < key0 + kBN) {
-                const int s = j % S;
-                if (!mbar_wait_bounded(&v_full[s], (j / S) & 1, &s_abort, p.status)) {
+                const int s = j % SV;
+                if (!mbar_wait_bounded(&v_full[s], (j / SV) & 1, &s_abort, p.status)) {
                     ok = false;
                     break;
                 }
