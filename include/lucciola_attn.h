@@ -49,7 +49,8 @@ enum lc_status {
     LC_ERR_DEVICE_TIMEOUT = 8,      /* a bounded device-side wait gave up                    */
     LC_ERR_OUT_OF_BLOCKS = 9,       /* KV cache free list exhausted (kv_cache.rs:110-113)    */
     LC_ERR_OUT_OF_MEMORY = 10,      /* KV cache does not fit the memory budget (:40-48)      */
-    LC_ERR_NOT_SUPPORTED = 11       /* no sm_100 device / feature unavailable                */
+    LC_ERR_NOT_SUPPORTED = 11,      /* no sm_100 device / feature unavailable                */
+    LC_ERR_NO_FREE_SLOT = 12        /* lc_kv_pool: every sequence slot is in use             */
 };
 
 /* Bits a kernel ORs into the optional device status word. */
@@ -304,6 +305,84 @@ void lc_kv_cache_free(lc_kv_cache *c);
 int lc_apply_flash_decoding(lc_kv_cache *c, lc_stream_t stream, void *output,
                             const void *q, int layer_idx, int pos,
                             const int *pos_ptr, int num_q_heads);
+
+/* ------------------------------------------------------------------------- */
+/* Batched token-step driver: many sequences in one paged pool.               */
+/* ------------------------------------------------------------------------- */
+/* The reference's KVCache holds one sequence (one block table,
+ * kv_cache.rs:12-174) and its decode loop steps one token of one sequence
+ * (models.rs:230-245, attention section :486-550). lc_kv_pool is the batched
+ * replacement of that part: one K and one V pool of num_blocks 16-token pages
+ * ([num_blocks][num_layers][num_kv_heads][16][head_dim] bf16, zeroed) shared
+ * by up to max_seqs sequences, each owning a list of pages; one LIFO free list
+ * (a fresh pool hands out pages 0, 1, 2, ... as kv_cache.rs:73-76 does).
+ *
+ * lc_block_alloc is its page bookkeeping alone, in host memory. */
+typedef struct lc_block_alloc lc_block_alloc;
+int lc_block_alloc_new(int64_t num_blocks, int max_seqs, int max_blocks_per_seq,
+                       lc_block_alloc **out);
+/* Takes the lowest free slot (LC_ERR_NO_FREE_SLOT when none). */
+int lc_block_alloc_add_seq(lc_block_alloc *a, int *slot);
+/* Returns the slot's pages to the free list (handed out again in the same
+ * order) and frees the slot. */
+int lc_block_alloc_release_seq(lc_block_alloc *a, int slot);
+/* Grows the slot's page list to cover `tokens` tokens. LC_ERR_OUT_OF_BLOCKS
+ * when the free list cannot (nothing is taken then); LC_ERR_INVALID_ARGUMENT
+ * beyond max_blocks_per_seq pages. */
+int lc_block_alloc_reserve(lc_block_alloc *a, int slot, int tokens);
+/* Copies up to `capacity` of the slot's pages (logical order) to dst and
+ * returns how many it has (-1 for a bad slot). */
+int lc_block_alloc_row(const lc_block_alloc *a, int slot, int *dst, int capacity);
+int64_t lc_block_alloc_num_free(const lc_block_alloc *a);
+void lc_block_alloc_free(lc_block_alloc *a);
+
+/* The device pool. max_seq_len bounds every sequence (table rows of
+ * ceil(max_seq_len / 16) entries). Creation allocates and zeroes everything it
+ * needs (pools, the step's tables and positions, the split-K workspace, pinned
+ * staging); the step calls below allocate nothing. */
+typedef struct lc_kv_pool lc_kv_pool;
+int lc_kv_pool_new(int num_layers, int num_q_heads, int num_kv_heads, int head_dim,
+                   int max_seqs, int max_seq_len, int64_t num_blocks,
+                   lc_stream_t stream, lc_kv_pool **out);
+int lc_kv_pool_add_sequence(lc_kv_pool *p, int *slot);
+int lc_kv_pool_release_sequence(lc_kv_pool *p, int slot);
+/* One decode step of `batch` distinct sequences: slots[b] is the sequence of
+ * batch row b and positions[b] (host) the position of its new token. Pages are
+ * reserved to cover positions[b] + 1 tokens, and the step's block tables (batch
+ * order) and positions are copied to the pool's device buffers on `stream`.
+ * Those buffers keep their addresses, so the per-layer launches of a step may
+ * be captured once in a CUDA graph and replayed after each prepare_step with
+ * the same batch size. */
+int lc_kv_pool_prepare_step(lc_kv_pool *p, lc_stream_t stream, int batch,
+                            const int *slots, const int *positions);
+/* Layer `layer` of the prepared step: bias + RoPE + append of each row's new
+ * token and attention over its sequence (lc_rope_append_decode, scale
+ * 1/sqrt(head_dim)). qkv rows [q | k | v] in batch order; out [batch][Hq*hd]. */
+int lc_kv_pool_decode_layer(lc_kv_pool *p, lc_stream_t stream, int layer, void *out,
+                            int64_t out_stride, const void *qkv, int64_t row_stride,
+                            const void *q_bias, const void *k_bias, const void *v_bias,
+                            const float *cos_cache, const float *sin_cache, int rope_rows,
+                            int *dev_status);
+/* A prompt of `tokens` tokens of sequence `slot` at positions start_pos.. :
+ * reserves its pages and uploads its table row and positions. */
+int lc_kv_pool_prepare_prefill(lc_kv_pool *p, lc_stream_t stream, int slot, int start_pos,
+                               int tokens);
+/* Layer `layer` of the prepared prompt: lc_rope_append over its qkv rows (q and
+ * k rotated in place, K/V appended), then lc_paged_prefill into out. */
+int lc_kv_pool_prefill_layer(lc_kv_pool *p, lc_stream_t stream, int layer, void *out,
+                             int64_t out_stride, void *qkv, int64_t row_stride,
+                             const void *q_bias, const void *k_bias, const void *v_bias,
+                             const float *cos_cache, const float *sin_cache, int rope_rows,
+                             int *dev_status);
+void *lc_kv_pool_k_pool(lc_kv_pool *p);
+void *lc_kv_pool_v_pool(lc_kv_pool *p);
+const int *lc_kv_pool_step_tables(const lc_kv_pool *p);
+const int *lc_kv_pool_step_positions(const lc_kv_pool *p);
+int lc_kv_pool_table_stride(const lc_kv_pool *p);
+int64_t lc_kv_pool_num_blocks(const lc_kv_pool *p);
+int64_t lc_kv_pool_num_free_blocks(const lc_kv_pool *p);
+int lc_kv_pool_sequence_pages(const lc_kv_pool *p, int slot, int *dst, int capacity);
+void lc_kv_pool_free(lc_kv_pool *p);
 
 /* ------------------------------------------------------------------------- */
 /* Multi-GPU host logic.                                                      */

@@ -22,6 +22,7 @@ extern "C" const char *lc_status_string(int status) {
         case LC_ERR_OUT_OF_BLOCKS: return "KV cache out of memory blocks";
         case LC_ERR_OUT_OF_MEMORY: return "not enough GPU memory for the KV cache";
         case LC_ERR_NOT_SUPPORTED: return "not supported on this device";
+        case LC_ERR_NO_FREE_SLOT: return "every sequence slot of the KV pool is in use";
         default: return "unknown status";
     }
 }

@@ -68,6 +68,31 @@ SIGNATURES = {
     "lc_kv_cache_num_allocated_blocks": (_i32, [_vp]),
     "lc_kv_cache_free": (None, [_vp]),
     "lc_apply_flash_decoding": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _i32]),
+    "lc_block_alloc_new": (_i32, [_i64, _i32, _i32, C.POINTER(_vp)]),
+    "lc_block_alloc_add_seq": (_i32, [_vp, _pi32]),
+    "lc_block_alloc_release_seq": (_i32, [_vp, _i32]),
+    "lc_block_alloc_reserve": (_i32, [_vp, _i32, _i32]),
+    "lc_block_alloc_row": (_i32, [_vp, _i32, _pi32, _i32]),
+    "lc_block_alloc_num_free": (_i64, [_vp]),
+    "lc_block_alloc_free": (None, [_vp]),
+    "lc_kv_pool_new": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i64, _vp, C.POINTER(_vp)]),
+    "lc_kv_pool_add_sequence": (_i32, [_vp, _pi32]),
+    "lc_kv_pool_release_sequence": (_i32, [_vp, _i32]),
+    "lc_kv_pool_prepare_step": (_i32, [_vp, _vp, _i32, _pi32, _pi32]),
+    "lc_kv_pool_decode_layer": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp,
+                                       _vp, _i32, _vp]),
+    "lc_kv_pool_prepare_prefill": (_i32, [_vp, _vp, _i32, _i32, _i32]),
+    "lc_kv_pool_prefill_layer": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp,
+                                        _vp, _i32, _vp]),
+    "lc_kv_pool_k_pool": (_vp, [_vp]),
+    "lc_kv_pool_v_pool": (_vp, [_vp]),
+    "lc_kv_pool_step_tables": (_vp, [_vp]),
+    "lc_kv_pool_step_positions": (_vp, [_vp]),
+    "lc_kv_pool_table_stride": (_i32, [_vp]),
+    "lc_kv_pool_num_blocks": (_i64, [_vp]),
+    "lc_kv_pool_num_free_blocks": (_i64, [_vp]),
+    "lc_kv_pool_sequence_pages": (_i32, [_vp, _i32, _pi32, _i32]),
+    "lc_kv_pool_free": (None, [_vp]),
     "lc_shard_sequences": (_i32, [_pi32, _i32, _i32, _pi32]),
     "lc_shard_kv_heads": (_i32, [_i32, _i32, _i32, _i32, _pi32, _pi32]),
 }
@@ -339,6 +364,142 @@ class KVCache:
     def close(self):
         if self._h:
             lib.lc_kv_cache_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# --------------------------------------------------- batched token-step driver --
+
+def _ints(vals):
+    vals = [int(v) for v in vals]
+    return (C.c_int * max(1, len(vals)))(*vals)
+
+
+class BlockAlloc:
+    """Page bookkeeping of a multi-sequence pool (host only): sequence slots,
+    their page lists, one LIFO free list."""
+
+    def __init__(self, num_blocks, max_seqs, max_blocks_per_seq):
+        h = C.c_void_p()
+        check(lib.lc_block_alloc_new(num_blocks, max_seqs, max_blocks_per_seq, C.byref(h)),
+              "lc_block_alloc_new")
+        self._h = h
+        self.max_blocks_per_seq = max_blocks_per_seq
+
+    def add(self):
+        slot = C.c_int()
+        check(lib.lc_block_alloc_add_seq(self._h, C.byref(slot)), "lc_block_alloc_add_seq")
+        return slot.value
+
+    def release(self, slot):
+        check(lib.lc_block_alloc_release_seq(self._h, slot), "lc_block_alloc_release_seq")
+
+    def reserve(self, slot, tokens):
+        check(lib.lc_block_alloc_reserve(self._h, slot, tokens), "lc_block_alloc_reserve")
+
+    def pages(self, slot):
+        buf = (C.c_int * self.max_blocks_per_seq)()
+        n = lib.lc_block_alloc_row(self._h, slot, buf, self.max_blocks_per_seq)
+        if n < 0:
+            raise LucciolaError(1, "lc_block_alloc_row")
+        return list(buf[:n])
+
+    @property
+    def num_free(self):
+        return lib.lc_block_alloc_num_free(self._h)
+
+    def close(self):
+        if self._h:
+            lib.lc_block_alloc_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class KVPool:
+    """Batched token-step driver: one paged K/V pool shared by many sequences
+    (lc_kv_pool). prepare_step() then decode_layer() per layer runs one decode
+    token of a batch; prepare_prefill() then prefill_layer() per layer runs a
+    prompt of one sequence."""
+
+    def __init__(self, num_layers, num_q_heads, num_kv_heads, head_dim, max_seqs, max_seq_len,
+                 num_blocks, stream=None):
+        h = C.c_void_p()
+        check(lib.lc_kv_pool_new(num_layers, num_q_heads, num_kv_heads, head_dim, max_seqs,
+                                 max_seq_len, num_blocks, _stream(stream), C.byref(h)),
+              "lc_kv_pool_new")
+        self._h = h
+        self.num_layers, self.num_q_heads, self.num_kv_heads = num_layers, num_q_heads, num_kv_heads
+        self.head_dim, self.max_seqs, self.num_blocks = head_dim, max_seqs, num_blocks
+        self.table_stride = lib.lc_kv_pool_table_stride(h)
+
+    def add_sequence(self):
+        slot = C.c_int()
+        check(lib.lc_kv_pool_add_sequence(self._h, C.byref(slot)), "lc_kv_pool_add_sequence")
+        return slot.value
+
+    def release_sequence(self, slot):
+        check(lib.lc_kv_pool_release_sequence(self._h, slot), "lc_kv_pool_release_sequence")
+
+    def prepare_step(self, slots, positions, stream=None):
+        check(lib.lc_kv_pool_prepare_step(self._h, _stream(stream), len(slots), _ints(slots),
+                                          _ints(positions)), "lc_kv_pool_prepare_step")
+
+    def decode_layer(self, layer, out, qkv, q_bias, k_bias, v_bias, cos, sin, dev_status=None,
+                     stream=None):
+        check(lib.lc_kv_pool_decode_layer(self._h, _stream(stream), layer, _p(out), out.stride(0),
+                                          _p(qkv), qkv.stride(0), _p(q_bias), _p(k_bias),
+                                          _p(v_bias), _p(cos), _p(sin), cos.shape[0],
+                                          _p(dev_status)), "lc_kv_pool_decode_layer")
+
+    def prepare_prefill(self, slot, start_pos, tokens, stream=None):
+        check(lib.lc_kv_pool_prepare_prefill(self._h, _stream(stream), slot, start_pos, tokens),
+              "lc_kv_pool_prepare_prefill")
+
+    def prefill_layer(self, layer, out, qkv, q_bias, k_bias, v_bias, cos, sin, dev_status=None,
+                      stream=None):
+        check(lib.lc_kv_pool_prefill_layer(self._h, _stream(stream), layer, _p(out), out.stride(0),
+                                           _p(qkv), qkv.stride(0), _p(q_bias), _p(k_bias),
+                                           _p(v_bias), _p(cos), _p(sin), cos.shape[0],
+                                           _p(dev_status)), "lc_kv_pool_prefill_layer")
+
+    def pages(self, slot):
+        buf = (C.c_int * self.table_stride)()
+        n = lib.lc_kv_pool_sequence_pages(self._h, slot, buf, self.table_stride)
+        if n < 0:
+            raise LucciolaError(1, "lc_kv_pool_sequence_pages")
+        return list(buf[:n])
+
+    def pools(self):
+        """(k_pool, v_pool) as torch bf16 views [num_blocks][L][Hkv][16][hd] (no copy)."""
+        import torch
+        shape = (self.num_blocks, self.num_layers, self.num_kv_heads, 16, self.head_dim)
+        n = 1
+        for d in shape:
+            n *= d
+        out = []
+        for ptr in (lib.lc_kv_pool_k_pool(self._h), lib.lc_kv_pool_v_pool(self._h)):
+            cls = type("_Cai", (), {"__cuda_array_interface__": {
+                "shape": (n,), "typestr": "<i2", "data": (ptr, False), "version": 3}})
+            out.append(torch.as_tensor(cls(), device="cuda").view(torch.bfloat16).view(shape))
+        return tuple(out)
+
+    @property
+    def num_free_blocks(self):
+        return lib.lc_kv_pool_num_free_blocks(self._h)
+
+    def close(self):
+        if self._h:
+            lib.lc_kv_pool_free(self._h)
             self._h = None
 
     def __del__(self):
