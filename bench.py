@@ -499,6 +499,145 @@ def run_ours(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def run_driver(args, rank, world, local):
+    """The decode workload through the batched token-step driver (lc_kv_pool):
+    the pool hands out the pages (all sequences grown together, so each
+    sequence's pages interleave with the others'), and every step is the token
+    loop a server runs: lc_kv_pool_prepare_step on the host (page reservation,
+    table and position upload), then one replay of a CUDA graph holding the
+    layers' lc_kv_pool_decode_layer launches. Positions advance by one token per
+    step, so the context grows and new pages are taken as sequences cross page
+    boundaries. Timed with CUDA events around K steps, host work included."""
+    import lucciola as L
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    L.set_dependent_launch(args.pdl)
+    w = Workload(args.config, rank, world, device)
+    settle_steps = 400
+    total_steps = 2 + settle_steps + args.warmup + args.steps
+    B, ctx = w.batch, w.ctx.astype(np.int64)
+    max_seq_len = int(ctx.max()) + total_steps + 16
+    num_blocks = int(((ctx + total_steps + 15) // 16).sum()) + B
+    del w.k_pool, w.v_pool
+    torch.cuda.empty_cache()
+    pool = L.KVPool(w.layers, w.hq, w.hkv, w.hd, B, max_seq_len, num_blocks)
+    slots = [pool.add_sequence() for _ in range(B)]
+    # reserve the cached context a page round at a time across all sequences
+    for k in range(1, (int(ctx.max()) + 15) // 16 + 1):
+        pos = np.minimum(ctx, 16 * k) - 1
+        pool.prepare_step(slots, pos.tolist())
+    kp, vp = pool.pools()
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4242 + rank)
+    for t in (kp, vp):
+        flat = t.view(-1)
+        for i in range(0, flat.numel(), 1 << 28):
+            chunk = flat[i:i + (1 << 28)]
+            chunk.copy_(torch.randn(chunk.numel(), generator=gen, device=device,
+                                    dtype=torch.float32).to(torch.bfloat16))
+    positions = ctx.copy()
+
+    def prepare():
+        pool.prepare_step(slots, positions.tolist())
+        positions[:] += 1
+
+    def layers():
+        for l in range(w.layers):
+            pool.decode_layer(l, w.out[l], w.qkv[l], w.q_bias[l], w.k_bias[l], w.v_bias[l],
+                              w.cos, w.sin)
+
+    for _ in range(2):  # eager: kernel attributes and tensor maps cached before capture
+        prepare()
+        layers()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        layers()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    for _ in range(settle_steps):
+        prepare()
+        graph.replay()
+    for _ in range(args.warmup):
+        prepare()
+        graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    kv_tokens = 0
+    cur = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(args.steps):
+        kv_tokens += int(positions.sum()) + B  # context + the new token, per kv head
+        prepare()
+        graph.replay()
+    e1.record(cur)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms_step = e0.elapsed_time(e1) / args.steps
+    kv_bytes = float(kv_tokens) * w.hkv * w.hd * 2 * 2 * w.layers  # over the K steps
+    vals = torch.tensor([ms_step, kv_bytes], dtype=torch.float64, device=device)
+    if dist:
+        mx = vals[:1].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = vals[1:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms_step, kv_bytes = mx.item(), tot.item()
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        value = kv_bytes / args.steps / (ms_step * 1e-3) / 1e9
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded bf16 ~N(0,1) K/V/Q, uniform context lengths)",
+            "config": {"workload": w.label + ", through the token-step driver (lc_kv_pool)",
+                       "batch_per_gpu": w.batch_per_rank, "global_batch": w.global_batch,
+                       "q_heads": w.hq, "kv_heads": w.hkv, "head_dim": w.hd,
+                       "layers": w.layers, "page_tokens": 16,
+                       "parallelism": f"sequence-sharded x{world}",
+                       "l2": "no flush: %.1f GB of pools per GPU > 126 MB L2" %
+                             (2 * kp.numel() * 2 / 1e9),
+                       "step": "lc_kv_pool_prepare_step (host: pages, table + position "
+                               "upload) then one CUDA graph replay of the layers' "
+                               "lc_kv_pool_decode_layer launches; positions advance one "
+                               "token per step" +
+                               (f"; programmatic dependent launch mode {args.pdl}"
+                                if args.pdl else "")},
+            "tokens_per_s": round(w.global_batch / (ms_step * 1e-3), 1),
+            "pct_hbm": round(100 * value / world / peak, 2),
+            "peak_kind": f"{peak_kind} (burst copy)",
+            "gpu_launches": w.layers * args.steps,
+            "clocks": clocks,
+            "free_blocks_after": pool.num_free_blocks,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    pool.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # dram__bytes_read.sum + dram__bytes_write.sum of one fused decode launch of the
 # bench workload, from the ncu captures summarised in profiles/paged_decode_c2.md
 # and profiles/paged_decode_c3.md (same per-launch work as the bench's launches).
@@ -859,6 +998,9 @@ def main():
                          "pools) for profiler captures")
     ap.add_argument("--unfused", action="store_true",
                     help="two launches per layer (lc_rope_append, lc_paged_decode)")
+    ap.add_argument("--driver", action="store_true",
+                    help="decode configs: run the workload through the batched token-step "
+                         "driver (lc_kv_pool) with positions advancing every step")
     ap.add_argument("--partition", type=int, default=None,
                     help="override the split-K partition size in tokens (0 = auto)")
     args = ap.parse_args()
@@ -887,6 +1029,8 @@ def main():
         return 0
     if args.impl == "reference":
         run_reference(args, rank, world, local)
+    elif args.driver:
+        run_driver(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
     return 0
