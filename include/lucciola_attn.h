@@ -334,7 +334,27 @@ int lc_block_alloc_reserve(lc_block_alloc *a, int slot, int tokens);
  * returns how many it has (-1 for a bad slot). */
 int lc_block_alloc_row(const lc_block_alloc *a, int slot, int *dst, int capacity);
 int64_t lc_block_alloc_num_free(const lc_block_alloc *a);
+/* 64-bit hash of the whole bookkeeping state (slots, page lists, free list in
+ * hand-out order). Ranks that shard a model by kv head keep one pool each with
+ * identical block tables by issuing the same add/reserve/release calls; equal
+ * fingerprints (one all-reduce of a word) confirm that they still agree. */
+uint64_t lc_block_alloc_fingerprint(const lc_block_alloc *a);
 void lc_block_alloc_free(lc_block_alloc *a);
+
+/* Pool capacity as KVCache::new sizes it (src/layers/kv_cache.rs:37-59):
+ * budget = total * memory_fraction (f32) - (total - free) bytes, over the K+V
+ * bytes of one 16-token page of every layer (2 * L * Hkv * 16 * hd * 2). Unlike
+ * the reference there is no cap at one sequence's pages (the pool is shared);
+ * the result is capped so that pool rows fit an int32 index, and is 0 when
+ * the budget is not above what is already used. Pure arithmetic, no device. */
+int64_t lc_kv_pool_blocks_for_budget(int num_layers, int num_kv_heads, int head_dim,
+                                     uint64_t free_bytes, uint64_t total_bytes,
+                                     float memory_fraction);
+/* The same with free/total from cudaMemGetInfo on the current device;
+ * LC_ERR_OUT_OF_MEMORY when no page fits. Head-sharded ranks pass their local
+ * kv-head count. */
+int lc_kv_pool_capacity(int num_layers, int num_kv_heads, int head_dim, float memory_fraction,
+                        int64_t *num_blocks);
 
 /* The device pool. max_seq_len bounds every sequence (table rows of
  * ceil(max_seq_len / 16) entries). Creation allocates and zeroes everything it
@@ -382,6 +402,8 @@ int lc_kv_pool_table_stride(const lc_kv_pool *p);
 int64_t lc_kv_pool_num_blocks(const lc_kv_pool *p);
 int64_t lc_kv_pool_num_free_blocks(const lc_kv_pool *p);
 int lc_kv_pool_sequence_pages(const lc_kv_pool *p, int slot, int *dst, int capacity);
+/* lc_block_alloc_fingerprint of the pool's page bookkeeping. */
+uint64_t lc_kv_pool_fingerprint(const lc_kv_pool *p);
 void lc_kv_pool_free(lc_kv_pool *p);
 
 /* ------------------------------------------------------------------------- */

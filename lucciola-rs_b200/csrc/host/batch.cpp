@@ -124,6 +124,66 @@ extern "C" int64_t lc_block_alloc_num_free(const lc_block_alloc *a) {
     return a ? (int64_t)a->free_list.size() : 0;
 }
 
+extern "C" uint64_t lc_block_alloc_fingerprint(const lc_block_alloc *a) {
+    if (!a) return 0;
+    // FNV-1a over everything that decides future tables: each slot's state and
+    // pages, then the free list in hand-out order.
+    uint64_t h = 1469598103934665603ull;
+    auto mix = [&h](int64_t v) {
+        for (int i = 0; i < 8; ++i) {
+            h ^= (uint64_t)((v >> (8 * i)) & 0xff);
+            h *= 1099511628211ull;
+        }
+    };
+    mix(a->num_blocks);
+    mix(a->max_seqs);
+    mix(a->max_blocks_per_seq);
+    for (int s = 0; s < a->max_seqs; ++s) {
+        mix(a->live[s]);
+        mix((int64_t)a->pages[s].size());
+        for (int pg : a->pages[s]) mix(pg);
+    }
+    mix((int64_t)a->free_list.size());
+    for (int pg : a->free_list) mix(pg);
+    return h;
+}
+
+// ------------------------------------------------------------- pool sizing --
+
+extern "C" int64_t lc_kv_pool_blocks_for_budget(int num_layers, int num_kv_heads, int head_dim,
+                                                uint64_t free_bytes, uint64_t total_bytes,
+                                                float memory_fraction) {
+    if (num_layers <= 0 || num_kv_heads <= 0 || head_dim <= 0 || !(memory_fraction > 0.0f) ||
+        free_bytes > total_bytes)
+        return 0;
+    // src/layers/kv_cache.rs:37-59: budget = total * fraction (in f32) - used,
+    // divided by the K+V bytes of one 16-token page over all layers. No cap at
+    // one sequence's pages: the pool is shared by many sequences.
+    const uint64_t used = total_bytes - free_bytes;
+    const uint64_t available_total = (uint64_t)((float)total_bytes * memory_fraction);
+    if (available_total <= used) return 0;
+    const uint64_t bytes_per_block =
+        2ull * num_layers * num_kv_heads * kBlockSize * (uint64_t)head_dim * 2;
+    int64_t blocks = (int64_t)((available_total - used) / bytes_per_block);
+    // pool rows (blocks x layers x heads x 16) must fit the kernels' int32 row index
+    const int64_t row_cap = ((int64_t(1) << 31) - 1) / ((int64_t)num_layers * num_kv_heads * kBlockSize);
+    return std::min(blocks, row_cap);
+}
+
+extern "C" int lc_kv_pool_capacity(int num_layers, int num_kv_heads, int head_dim,
+                                   float memory_fraction, int64_t *num_blocks) {
+    if (!num_blocks) return LC_ERR_INVALID_ARGUMENT;
+    *num_blocks = 0;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    *num_blocks = lc_kv_pool_blocks_for_budget(num_layers, num_kv_heads, head_dim, free_b,
+                                               total_b, memory_fraction);
+    return *num_blocks > 0 ? LC_OK : LC_ERR_OUT_OF_MEMORY;
+}
+
 // -------------------------------------------------------------- device pool --
 
 struct lc_kv_pool {
@@ -350,6 +410,10 @@ extern "C" int lc_kv_pool_prefill_layer(lc_kv_pool *p, lc_stream_t stream, int l
                             p->num_layers, layer, p->num_q_heads, p->num_kv_heads, p->head_dim,
                             p->d_pf_table, p->max_blocks, p->d_pf_start, 1, p->pf_tokens,
                             p->pf_start, 1.0f / std::sqrt((float)p->head_dim), dev_status, stream);
+}
+
+extern "C" uint64_t lc_kv_pool_fingerprint(const lc_kv_pool *p) {
+    return p ? lc_block_alloc_fingerprint(p->alloc) : 0;
 }
 
 extern "C" void *lc_kv_pool_k_pool(lc_kv_pool *p) { return p ? p->k_pool : nullptr; }

@@ -74,7 +74,10 @@ SIGNATURES = {
     "lc_block_alloc_reserve": (_i32, [_vp, _i32, _i32]),
     "lc_block_alloc_row": (_i32, [_vp, _i32, _pi32, _i32]),
     "lc_block_alloc_num_free": (_i64, [_vp]),
+    "lc_block_alloc_fingerprint": (C.c_uint64, [_vp]),
     "lc_block_alloc_free": (None, [_vp]),
+    "lc_kv_pool_blocks_for_budget": (_i64, [_i32, _i32, _i32, C.c_uint64, C.c_uint64, _f32]),
+    "lc_kv_pool_capacity": (_i32, [_i32, _i32, _i32, _f32, C.POINTER(_i64)]),
     "lc_kv_pool_new": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i64, _vp, C.POINTER(_vp)]),
     "lc_kv_pool_add_sequence": (_i32, [_vp, _pi32]),
     "lc_kv_pool_release_sequence": (_i32, [_vp, _i32]),
@@ -92,6 +95,7 @@ SIGNATURES = {
     "lc_kv_pool_num_blocks": (_i64, [_vp]),
     "lc_kv_pool_num_free_blocks": (_i64, [_vp]),
     "lc_kv_pool_sequence_pages": (_i32, [_vp, _i32, _pi32, _i32]),
+    "lc_kv_pool_fingerprint": (C.c_uint64, [_vp]),
     "lc_kv_pool_free": (None, [_vp]),
     "lc_shard_sequences": (_i32, [_pi32, _i32, _i32, _pi32]),
     "lc_shard_kv_heads": (_i32, [_i32, _i32, _i32, _i32, _pi32, _pi32]),
@@ -413,6 +417,9 @@ class BlockAlloc:
     def num_free(self):
         return lib.lc_block_alloc_num_free(self._h)
 
+    def fingerprint(self):
+        return lib.lc_block_alloc_fingerprint(self._h)
+
     def close(self):
         if self._h:
             lib.lc_block_alloc_free(self._h)
@@ -423,6 +430,21 @@ class BlockAlloc:
             self.close()
         except Exception:
             pass
+
+
+def pool_blocks_for_budget(num_layers, num_kv_heads, head_dim, free_bytes, total_bytes,
+                           memory_fraction):
+    """Pages a pool gets from a memory budget (src/layers/kv_cache.rs:37-59 rule)."""
+    return lib.lc_kv_pool_blocks_for_budget(num_layers, num_kv_heads, head_dim, free_bytes,
+                                            total_bytes, memory_fraction)
+
+
+def pool_capacity(num_layers, num_kv_heads, head_dim, memory_fraction):
+    """pool_blocks_for_budget with the current device's free/total memory."""
+    n = C.c_int64()
+    check(lib.lc_kv_pool_capacity(num_layers, num_kv_heads, head_dim, memory_fraction,
+                                  C.byref(n)), "lc_kv_pool_capacity")
+    return n.value
 
 
 class KVPool:
@@ -496,6 +518,9 @@ class KVPool:
     @property
     def num_free_blocks(self):
         return lib.lc_kv_pool_num_free_blocks(self._h)
+
+    def fingerprint(self):
+        return lib.lc_kv_pool_fingerprint(self._h)
 
     def close(self):
         if self._h:

@@ -95,3 +95,59 @@ def test_random_walk_matches_a_model():
         for s, pg in pages.items():
             assert a.pages(s) == pg
         assert a.num_free == len(free)
+
+
+def _reference_budget(L_, hkv, hd, free, total, fraction):
+    """src/layers/kv_cache.rs:37-59, restated: budget in f32, K+V bytes per page."""
+    used = total - free
+    available_total = int(np.float32(total) * np.float32(fraction))
+    if available_total <= used:
+        return 0
+    return (available_total - used) // (2 * L_ * hkv * 16 * hd * 2)
+
+
+@pytest.mark.parametrize("L_,hkv,hd,free,total,fraction", [
+    (24, 2, 64, 150 << 30, 183359 << 20, 0.9),     # 0.5B shape on an idle B200
+    (28, 4, 128, 120 << 30, 183359 << 20, 0.85),   # 7B shape, 63 GB already used
+    (80, 1, 128, 170 << 30, 183359 << 20, 0.95),   # 72B shape, one of 8 kv-head shards
+    (24, 2, 64, 10 << 30, 80 << 30, 0.5),          # budget below what is used
+])
+def test_pool_budget_follows_the_reference_rule(L_, hkv, hd, free, total, fraction):
+    got = L.pool_blocks_for_budget(L_, hkv, hd, free, total, fraction)
+    assert got == _reference_budget(L_, hkv, hd, free, total, fraction)
+
+
+def test_pool_budget_caps_at_int32_rows():
+    # a tiny page (1 layer, 1 head, hd 64) and a huge budget: rows = blocks * 16 < 2^31
+    got = L.pool_blocks_for_budget(1, 1, 64, 1 << 50, 1 << 50, 1.0)
+    assert got == ((1 << 31) - 1) // 16
+    assert L.pool_blocks_for_budget(0, 1, 64, 1 << 30, 1 << 30, 1.0) == 0
+
+
+def test_fingerprint_tracks_every_decision():
+    def run(extra):
+        a = L.BlockAlloc(300, 6, 64)
+        rng = np.random.default_rng(11)
+        live = []
+        for _ in range(400):
+            op = rng.integers(0, 3)
+            if op == 0 and len(live) < 6:
+                live.append(a.add())
+            elif op == 1 and live:
+                try:
+                    a.reserve(int(rng.choice(live)), int(rng.integers(0, 1024)))
+                except L.LucciolaError:
+                    pass
+            elif op == 2 and live:
+                s = int(rng.choice(live))
+                a.release(s)
+                live.remove(s)
+        if extra:
+            s = a.add() if not live else live[0]
+            a.reserve(s, len(a.pages(s)) * 16 + 1)
+        return a.fingerprint(), {s: a.pages(s) for s in live}
+    f0, p0 = run(False)
+    f1, p1 = run(False)
+    f2, _ = run(True)
+    assert f0 == f1 and p0 == p1  # the same calls give the same tables and state
+    assert f2 != f0               # one more page taken changes it

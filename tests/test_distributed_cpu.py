@@ -89,7 +89,57 @@ def _head_shard_worker(rank, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("worker", [_sequence_shard_worker, _head_shard_worker])
+def _head_shard_tables_worker(rank, port, q):
+    """KV-head sharding keeps one pool per rank with identical block tables: every
+    rank issues the same allocator calls (no table traffic), and a fingerprint
+    all-reduce confirms the agreement; a rank that diverges is caught."""
+    _setup(rank, port)
+    try:
+        import lucciola as L
+        first, nloc = L.shard_kv_heads(64, 8, WORLD, rank)
+        blocks = L.pool_blocks_for_budget(80, nloc, 128, 170 << 30, 183359 << 20, 0.9)
+        a = L.BlockAlloc(2000, 16, 512)
+        rng = np.random.default_rng(5)  # the scheduler's decisions, the same on every rank
+        live = []
+        for _ in range(300):
+            if len(live) < 16 and rng.random() < 0.3:
+                live.append(a.add())
+            elif live and rng.random() < 0.1:
+                s = live.pop(int(rng.integers(0, len(live))))
+                a.release(s)
+            elif live:
+                s = live[int(rng.integers(0, len(live)))]
+                try:
+                    a.reserve(s, len(a.pages(s)) * 16 + int(rng.integers(1, 64)))
+                except L.LucciolaError:
+                    pass
+
+        def agree():
+            f = torch.tensor([a.fingerprint() & 0x7FFFFFFFFFFFFFFF], dtype=torch.int64)
+            lo, hi = f.clone(), f.clone()
+            dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+            dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+            return bool(lo.item() == hi.item())
+
+        tables = [None] * WORLD
+        dist.all_gather_object(tables, {s: a.pages(s) for s in live})
+        same_before = agree()
+        if rank == 1 and live:
+            s = live[0]
+            a.reserve(s, len(a.pages(s)) * 16 + 1)  # one page more on one rank only
+        same_after = agree()
+        sizes = [None] * WORLD
+        dist.all_gather_object(sizes, (first, nloc, blocks))
+        if rank == 0:
+            ok = (same_before and not same_after and tables[0] == tables[1]
+                  and len({x[2] for x in sizes}) == 1 and sizes[0][2] > 0)
+            q.put(("tables", ok, None))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("worker", [_sequence_shard_worker, _head_shard_worker,
+                                    _head_shard_tables_worker])
 def test_sharded_decode_equals_unsharded(worker):
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
