@@ -307,6 +307,35 @@ int lc_apply_flash_decoding(lc_kv_cache *c, lc_stream_t stream, void *output,
                             const int *pos_ptr, int num_q_heads);
 
 /* ------------------------------------------------------------------------- */
+/* Projections either side of attention (tcgen05 tensor cores).               */
+/* ------------------------------------------------------------------------- */
+/* out[M][N] = x[M][K] . w[N][K]^T, fp32 accumulation, bf16 result: what
+ * Qwen2Model::matmul_bf16 computes with cublasGemmEx (src/models.rs:252-292).
+ * residual == NULL is beta 0 (qkv_proj, models.rs:470-483); otherwise
+ * out = bf16(acc + residual) (o_proj with beta 1 into hidden_states,
+ * models.rs:553-566; residual may be out). Row-major with row strides in
+ * elements; N % 32 == 0, K % 8 == 0, pointers 16-byte aligned, strides
+ * multiples of 8. */
+int lc_proj_gemm(void *out, int64_t out_stride, const void *x, int64_t x_stride,
+                 const void *w, int64_t w_stride, int M, int N, int K,
+                 const void *residual, int64_t res_stride, lc_stream_t stream);
+
+/* The QKV projection of a prompt with lc_rope_append fused into its epilogue:
+ * qkv[t] = x[t] . w_qkv^T (N = (Hq + 2 Hkv) * head_dim, K = hidden) rounded to
+ * bf16, then q and k biased and rotated in place and k / v + bias appended to
+ * the pools, exactly as lc_rope_append over the same rows (arguments as
+ * there). The rows, pools and status are bit-identical to lc_proj_gemm
+ * followed by lc_rope_append. */
+int lc_qkv_proj_rope_append(void *qkv, int64_t row_stride, const void *x, int64_t x_stride,
+                            const void *w_qkv, int64_t w_stride, int hidden, int num_seqs,
+                            int tokens_per_seq, const int *positions, const void *q_bias,
+                            const void *k_bias, const void *v_bias, const float *cos_cache,
+                            const float *sin_cache, int rope_rows, void *k_pool, void *v_pool,
+                            int64_t num_blocks, int num_layers, int layer, int num_q_heads,
+                            int num_kv_heads, int head_dim, const int *block_tables,
+                            int table_stride, int *dev_status, lc_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
 /* Batched token-step driver: many sequences in one paged pool.               */
 /* ------------------------------------------------------------------------- */
 /* The reference's KVCache holds one sequence (one block table,

@@ -1,0 +1,536 @@
+// proj_gemm.cu - the projections on either side of attention, on the 5th-gen
+// tensor cores: out[M][N] = x[M][K] . w[N][K]^T with fp32 accumulation in
+// tensor memory and a bf16 result, as Qwen2Model::matmul_bf16 computes it
+// (src/models.rs:252-292: cublasGemmEx, CUBLAS_COMPUTE_32F, bf16 C). Three
+// epilogues:
+//   plain     out = bf16(acc)                                  (qkv_proj, beta 0)
+//   residual  out = bf16(acc + residual)                       (o_proj, beta 1,
+//             src/models.rs:553-566; residual may be out itself)
+//   qkv rope  the QKV projection followed, in the same kernel, by what
+//             lc_rope_append does to its rows (src/models.rs:500-534): q and
+//             k rounded to bf16, bias added, rotated and stored back; k
+//             rotated and v + bias appended to the paged pools. The result is
+//             bit-identical to lc_proj_gemm then lc_rope_append.
+//
+// Design: a persistent grid of one CTA per SM walks 128 x 256 output tiles
+// (the 256 columns of a tile hold whole heads: head_dim 64 or 128). Warp 0
+// issues TMA loads of 64-wide K blocks (x tile {64 x 128}, w tile {64 x 256},
+// 128-byte swizzle) into a 4-stage ring; warp 1 issues tcgen05.mma
+// (M 128, N 256, K 16, bf16 in, fp32 accumulate) into one of two 256-column
+// TMEM accumulators; warps 2-9 (one output row per thread of a TMEM lane
+// quadrant) drain the other accumulator through the epilogue while the next
+// tile accumulates (two warps per quadrant, each taking every other 32-column
+// chunk or head, so that one warp's loads overlap the other's arithmetic).
+// Every wait is bounded; a timeout sets LC_DEV_TIMEOUT.
+#include <climits>
+
+#include "lc_common.cuh"
+#include "lc_host.h"
+#include "lc_tcgen05.cuh"
+#include "rope_math.cuh"
+
+namespace lc {
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStagesG = 4;
+constexpr int kEpiWarps = 8;    // two per TMEM lane quadrant
+constexpr int kThreadsG = 64 + 32 * kEpiWarps;  // TMA warp, MMA warp, epilogue warps
+constexpr uint32_t kATile = kBM * kBK * 2;  // 16 KiB
+constexpr uint32_t kBTile = kBN * kBK * 2;  // 32 KiB
+constexpr uint32_t kStageBytesG = kATile + kBTile;
+constexpr int kSmemG = kStagesG * kStageBytesG + 1024;  // + 1024-byte alignment slack
+constexpr uint32_t kTmemColsG = 2 * kBN;                 // two accumulators
+constexpr uint32_t kIdescG = idesc_bf16_f32(kBM, kBN, 0);
+
+enum Epilogue { kPlain = 0, kResidual = 1, kQkvRope = 2 };
+
+struct GemmParams {
+    int M, N, K;
+    int m_tiles, n_tiles;
+    bf16 *out;
+    int64_t out_stride;
+    const bf16 *residual;
+    int64_t res_stride;
+    // qkv rope: rows are tokens (row / tokens_per_seq = sequence), columns
+    // [q heads | k heads | v heads] of head_dim each.
+    int tokens_per_seq;
+    const int *positions;
+    const bf16 *q_bias, *k_bias, *v_bias;
+    const float *cos_t, *sin_t;
+    int rope_rows;
+    bf16 *k_pool, *v_pool;
+    int64_t num_blocks;
+    int num_layers, layer, num_q_heads, num_kv_heads, head_dim;
+    const int *tables;
+    int table_stride;
+    int *status;
+};
+
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// bf16(acc) back as a float: the value the reference's qkv buffer holds.
+__device__ __forceinline__ float round_bf16(float x) {
+    return __bfloat162float(__float2bfloat16(x));
+}
+
+// 32 consecutive bf16 from 32 floats (RNE), four 16-byte stores.
+__device__ __forceinline__ void store32(bf16 *dst, const float (&f)[32]) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        uint4 o;
+        o.x = pack_bf16(f[8 * v + 0], f[8 * v + 1]);
+        o.y = pack_bf16(f[8 * v + 2], f[8 * v + 3]);
+        o.z = pack_bf16(f[8 * v + 4], f[8 * v + 5]);
+        o.w = pack_bf16(f[8 * v + 6], f[8 * v + 7]);
+        reinterpret_cast<uint4 *>(dst)[v] = o;
+    }
+}
+
+// 32 consecutive bf16 as floats.
+__device__ __forceinline__ void load32(const bf16 *src, float (&f)[32]) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        const uint4 u = reinterpret_cast<const uint4 *>(src)[v];
+        const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            f[8 * v + 2 * i] = __low2float(h[i]);
+            f[8 * v + 2 * i + 1] = __high2float(h[i]);
+        }
+    }
+}
+
+// Pool offset of (position, kv head 0) for token row `row`, or -1 when the
+// row must not be appended (status bits set), as rope_append.cu does.
+__device__ __forceinline__ int64_t pool_base(const GemmParams &p, int row, int pos) {
+    const int b = row / p.tokens_per_seq;
+    const int logical = pos / kBlockSize;
+    if (logical >= p.table_stride) {
+        set_status(p.status, LC_DEV_BAD_POS);
+        return -1;
+    }
+    const int phys = p.tables[(int64_t)b * p.table_stride + logical];
+    if (phys < 0 || phys >= p.num_blocks) {
+        set_status(p.status, LC_DEV_BAD_BLOCK);
+        return -1;
+    }
+    return page_row(phys, p.layer, 0, p.num_layers, p.num_kv_heads) * p.head_dim +
+           (int64_t)(pos % kBlockSize) * p.head_dim;
+}
+
+// Epilogue of one 256-column tile for the thread owning output row `row`
+// (TMEM lane quadrant base `tacc`): plain / residual; chunks half, half + 2, ...
+template <int EPI>
+__device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc, int row, int col0,
+                                              int half) {
+#pragma unroll 1
+    for (int c = half; c < kBN / 32; c += 2) {
+        const int col = col0 + 32 * c;
+        if (col >= p.N) break;
+        uint32_t r[32];
+        tmem_ld32(tacc + 32 * c, r);
+        tmem_wait_ld_regs(r);
+        if (row >= p.M) continue;
+        float f[32];
+        if constexpr (EPI == kResidual) {
+            float res[32];
+            load32(p.residual + (int64_t)row * p.res_stride + col, res);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = __fadd_rn(u2f(r[i]), res[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = u2f(r[i]);
+        }
+        store32(p.out + (int64_t)row * p.out_stride + col, f);
+    }
+}
+
+// What the QKV epilogue needs of a row besides the accumulator, read while
+// the tile still accumulates: the position, the 32 cos/sin of the row's RoPE
+// chunk (a thread works on one fixed 32-dim chunk of every half head of the
+// tile) and the pool offset when the tile holds k or v heads.
+template <int HD>
+struct QkvRow {
+    int pos;
+    bool live, rope_ok;
+    int64_t base;  // pool offset of (pos, kv head 0), or -1
+    float cs[32], sn[32];
+
+    __device__ __forceinline__ void load(const GemmParams &p, int row, int col0, int half) {
+        constexpr int kHalf = HD / 2;
+        constexpr int kChunks = kHalf / 32;
+        live = row < p.M;
+        pos = live ? p.positions[row] : 0;
+        if (live && pos < 0) set_status(p.status, LC_DEV_BAD_POS);
+        rope_ok = live && pos >= 0 && pos < p.rope_rows;
+        if (live && pos >= p.rope_rows) set_status(p.status, LC_DEV_BAD_POS);
+        base = -1;
+        if (live && pos >= 0 && col0 + kBN > p.num_q_heads * HD) base = pool_base(p, row, pos);
+        const int d0 = 32 * (kChunks == 1 ? 0 : half);
+        const float *ct = p.cos_t + (int64_t)(rope_ok ? pos : 0) * kHalf + d0;
+        const float *st = p.sin_t + (int64_t)(rope_ok ? pos : 0) * kHalf + d0;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const float4 c = reinterpret_cast<const float4 *>(ct)[v];
+            const float4 n = reinterpret_cast<const float4 *>(st)[v];
+            cs[4 * v] = c.x, cs[4 * v + 1] = c.y, cs[4 * v + 2] = c.z, cs[4 * v + 3] = c.w;
+            sn[4 * v] = n.x, sn[4 * v + 1] = n.y, sn[4 * v + 2] = n.z, sn[4 * v + 3] = n.w;
+        }
+    }
+};
+
+// QKV epilogue: head by head over the tile's columns (a warp pair splits them:
+// 32-dim chunks half, half + 2, ... of the tile's half-heads). Per element the
+// arithmetic is that of rope_append_vec_kernel on the bf16-rounded GEMM result.
+template <int HD>
+__device__ __forceinline__ void epilogue_qkv(const GemmParams &p, uint32_t tacc, int row, int col0,
+                                             int half, const QkvRow<HD> &w) {
+    constexpr int kHalf = HD / 2;
+    const int hq = p.num_q_heads, hkv = p.num_kv_heads;
+    const bool live = w.live, rope_ok = w.rope_ok;
+    const int pos = w.pos;
+    const int64_t base = w.base;
+    bf16 *orow = p.out + (int64_t)row * p.out_stride;
+    const int64_t stride_blk = (int64_t)kBlockSize * HD;
+    constexpr int kChunks = kHalf / 32;  // 32-dim chunks per half head
+#pragma unroll 1
+    for (int hcx = half; hcx < (kBN / HD) * kChunks; hcx += 2) {
+        const int h = hcx / kChunks, c = hcx - h * kChunks;
+        const int hc = col0 + h * HD;  // first column of this head
+        if (hc >= p.N) break;
+        const int g = hc / HD;  // head index over [q | k | v]
+        const int kind = g < hq ? 0 : (g < hq + hkv ? 1 : 2);
+        {
+            const int d0 = 32 * c;  // dims [d0, d0 + 32) of the first half, their partners
+            uint32_t r1[32], r2[32];
+            tmem_ld32(tacc + h * HD + d0, r1);
+            tmem_ld32(tacc + h * HD + kHalf + d0, r2);
+            tmem_wait_ld_regs(r1);
+            tmem_wait_ld_regs(r2);
+            if (!live) continue;
+            float x1[32], x2[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                x1[i] = round_bf16(u2f(r1[i]));
+                x2[i] = round_bf16(u2f(r2[i]));
+            }
+            if (pos < 0) {  // the row is left as the projection wrote it
+                store32(orow + hc + d0, x1);
+                store32(orow + hc + kHalf + d0, x2);
+                continue;
+            }
+            if (kind == 2) {
+                // v: the row keeps the projection; the pool gets v + bias.
+                store32(orow + hc + d0, x1);
+                store32(orow + hc + kHalf + d0, x2);
+                if (base < 0) continue;
+                const int vh = g - hq - hkv;
+                const bf16 *vb = p.v_bias + vh * HD;
+                float b1[32], b2[32];
+                load32(vb + d0, b1);
+                load32(vb + kHalf + d0, b2);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    x1[i] = __fadd_rn(x1[i], b1[i]);
+                    x2[i] = __fadd_rn(x2[i], b2[i]);
+                }
+                bf16 *dst = p.v_pool + base + vh * stride_blk;
+                store32(dst + d0, x1);
+                store32(dst + kHalf + d0, x2);
+                continue;
+            }
+            if (!rope_ok) {  // past the RoPE table: q and k stay unrotated, k is not appended
+                store32(orow + hc + d0, x1);
+                store32(orow + hc + kHalf + d0, x2);
+                continue;
+            }
+            const int hh = kind == 0 ? g : g - hq;
+            const bf16 *bias = (kind == 0 ? p.q_bias : p.k_bias) + hh * HD;
+            // rotated in place: element i reads x1[i], x2[i] before writing them
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                float b1[8], b2[8];
+                {
+                    const uint4 u1 = reinterpret_cast<const uint4 *>(bias + d0)[v];
+                    const uint4 u2 = reinterpret_cast<const uint4 *>(bias + kHalf + d0)[v];
+                    const __nv_bfloat162 *h1 = reinterpret_cast<const __nv_bfloat162 *>(&u1);
+                    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&u2);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        b1[2 * i] = __low2float(h1[i]);
+                        b1[2 * i + 1] = __high2float(h1[i]);
+                        b2[2 * i] = __low2float(h2[i]);
+                        b2[2 * i + 1] = __high2float(h2[i]);
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int i = 8 * v + e;
+                    const float v1 = __fadd_rn(x1[i], b1[e]), v2 = __fadd_rn(x2[i], b2[e]);
+                    x1[i] = rot_sub(v1, w.cs[i], v2, w.sn[i]);
+                    x2[i] = rot_add(v1, w.sn[i], v2, w.cs[i]);
+                }
+            }
+            store32(orow + hc + d0, x1);
+            store32(orow + hc + kHalf + d0, x2);
+            if (kind == 1) {
+                if (base >= 0) {
+                    bf16 *dst = p.k_pool + base + hh * stride_blk;
+                    store32(dst + d0, x1);
+                    store32(dst + kHalf + d0, x2);
+                }
+            }
+        }
+    }
+}
+
+template <int EPI, int HD>
+__global__ void __launch_bounds__(kThreadsG, 1)
+    proj_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
+                     const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *gen = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[kStagesG];
+    __shared__ __align__(8) uint64_t empty[kStagesG];
+    __shared__ __align__(8) uint64_t acc_full[2];
+    __shared__ __align__(8) uint64_t acc_empty[2];
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int s_abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStagesG; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 32 * kEpiWarps);
+        }
+        s_abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_sh, kTmemColsG);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    const int tiles = p.m_tiles * p.n_tiles;
+    const int kblocks = (p.K + kBK - 1) / kBK;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA --
+        if (lane == 0) {
+            prefetch_tensormap(&tm_a);
+            prefetch_tensormap(&tm_b);
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStagesG;
+                    if (it >= kStagesG &&
+                        !mbar_wait_bounded(&empty[s], ((it / kStagesG) - 1) & 1, &s_abort, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = gen + s * kStageBytesG;
+                    mbar_arrive_expect_tx(&full[s], kStageBytesG);
+                    tma_load_2d(st, &tm_a, kb * kBK, mt * kBM, &full[s]);
+                    tma_load_2d(st + kATile, &tm_b, kb * kBK, nt * kBN, &full[s]);
+                }
+            }
+            if (!ok) {
+                // let the copies in flight land before the CTA exits
+                for (int k = it - kStagesG; k < it; ++k)
+                    if (k >= 0) mbar_wait_drain(&full[k % kStagesG], (k / kStagesG) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA --
+        if (lane == 0) {
+            int it = 0, tl = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++tl) {
+                const int buf = tl & 1;
+                if (tl >= 2 &&
+                    !mbar_wait_bounded(&acc_empty[buf], ((tl >> 1) - 1) & 1, &s_abort, p.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + buf * kBN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStagesG;
+                    if (!mbar_wait_bounded(&full[s], (it / kStagesG) & 1, &s_abort, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(gen + s * kStageBytesG), b = a + kATile;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_bf16(d, sw128_desc(a + kk * 32, 16, 1024),
+                                  sw128_desc(b + kk * 32, 16, 1024), kIdescG,
+                                  (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&empty[s]);  // the stage is free once these MMAs are done
+                }
+                if (ok) umma_commit(&acc_full[buf]);
+            }
+        }
+    } else {
+        // ----------------------------------------------------------- epilogue --
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int half = (warp - 2) >> 2;
+        const int r = quad * 32 + lane;
+        int tl = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tl) {
+            const int buf = tl & 1;
+            const int mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
+            const int row = mt * kBM + r, col0 = nt * kBN;
+            const uint32_t tacc = tmem + ((uint32_t)(quad * 32) << 16) + buf * kBN;
+            if constexpr (EPI == kQkvRope) {
+                QkvRow<HD> w;
+                w.load(p, row, col0, half);  // overlaps the tile's MMAs
+                if (!mbar_wait_bounded(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status)) break;
+                tc_fence_after();
+                epilogue_qkv<HD>(p, tacc, row, col0, half, w);
+            } else {
+                if (!mbar_wait_bounded(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status)) break;
+                tc_fence_after();
+                epilogue_rows<EPI>(p, tacc, row, col0, half);
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemColsG);
+    }
+}
+
+template <int EPI, int HD>
+int launch_gemm(const GemmParams &prm, const void *x, int64_t x_stride, const void *w,
+                int64_t w_stride, cudaStream_t stream) {
+    CUtensorMap ma, mb;
+    int rc = tensor_map_2d_sw128(x, prm.K, prm.M, x_stride * 2, kBK, kBM, &ma);
+    if (rc) return rc;
+    rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kBK, kBN, &mb);
+    if (rc) return rc;
+    rc = ensure_smem_attr((const void *)proj_gemm_kernel<EPI, HD>, kSmemG);
+    if (rc) return rc;
+    const int tiles = prm.m_tiles * prm.n_tiles;
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    proj_gemm_kernel<EPI, HD><<<grid, kThreadsG, kSmemG, stream>>>(ma, mb, prm);
+    return launch_status();
+}
+
+int check_gemm_shape(const void *out, int64_t out_stride, const void *x, int64_t x_stride,
+                     const void *w, int64_t w_stride, int M, int N, int K) {
+    if (!out || !x || !w) return LC_ERR_INVALID_ARGUMENT;
+    if (M < 0 || N <= 0 || K <= 0 || (N & 31) || (K & 7)) return LC_ERR_UNSUPPORTED_SHAPE;
+    if (x_stride < K || w_stride < K || out_stride < N) return LC_ERR_INVALID_ARGUMENT;
+    if (!aligned16(out) || !aligned16(x) || !aligned16(w) || (x_stride & 7) || (w_stride & 7) ||
+        (out_stride & 7))
+        return LC_ERR_MISALIGNED;
+    if ((int64_t)M >= (int64_t(1) << 31) - kBM || (int64_t)N >= (int64_t(1) << 31) - kBN)
+        return LC_ERR_INVALID_ARGUMENT;
+    return LC_OK;
+}
+
+}  // namespace
+}  // namespace lc
+
+using namespace lc;
+
+extern "C" int lc_proj_gemm(void *out, int64_t out_stride, const void *x, int64_t x_stride,
+                            const void *w, int64_t w_stride, int M, int N, int K,
+                            const void *residual, int64_t res_stride, lc_stream_t stream) {
+    int rc = check_gemm_shape(out, out_stride, x, x_stride, w, w_stride, M, N, K);
+    if (rc) return rc;
+    if (residual && (!aligned16(residual) || (res_stride & 7))) return LC_ERR_MISALIGNED;
+    if (residual && res_stride < N) return LC_ERR_INVALID_ARGUMENT;
+    if (M == 0) return LC_OK;
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.m_tiles = (M + kBM - 1) / kBM;
+    p.n_tiles = (N + kBN - 1) / kBN;
+    p.out = (bf16 *)out;
+    p.out_stride = out_stride;
+    p.residual = (const bf16 *)residual;
+    p.res_stride = res_stride;
+    cudaStream_t s = as_stream(stream);
+    return residual ? launch_gemm<kResidual, 64>(p, x, x_stride, w, w_stride, s)
+                    : launch_gemm<kPlain, 64>(p, x, x_stride, w, w_stride, s);
+}
+
+extern "C" int lc_qkv_proj_rope_append(void *qkv, int64_t row_stride, const void *x,
+                                       int64_t x_stride, const void *w_qkv, int64_t w_stride,
+                                       int hidden, int num_seqs, int tokens_per_seq,
+                                       const int *positions, const void *q_bias,
+                                       const void *k_bias, const void *v_bias,
+                                       const float *cos_cache, const float *sin_cache,
+                                       int rope_rows, void *k_pool, void *v_pool,
+                                       int64_t num_blocks, int num_layers, int layer,
+                                       int num_q_heads, int num_kv_heads, int head_dim,
+                                       const int *block_tables, int table_stride,
+                                       int *dev_status, lc_stream_t stream) {
+    if (!positions || !q_bias || !k_bias || !v_bias || !cos_cache || !sin_cache || !k_pool ||
+        !v_pool || !block_tables)
+        return LC_ERR_INVALID_ARGUMENT;
+    if (head_dim != 64 && head_dim != 128) return LC_ERR_UNSUPPORTED_HEAD_DIM;
+    if (num_seqs < 0 || tokens_per_seq <= 0 || num_layers <= 0 || layer < 0 ||
+        layer >= num_layers || num_q_heads <= 0 || num_kv_heads <= 0 || num_blocks <= 0 ||
+        table_stride <= 0 || rope_rows <= 0)
+        return LC_ERR_INVALID_ARGUMENT;
+    if (num_q_heads % num_kv_heads) return LC_ERR_UNSUPPORTED_SHAPE;
+    if ((int64_t)num_seqs * tokens_per_seq >= (int64_t(1) << 31) - kBM)
+        return LC_ERR_INVALID_ARGUMENT;
+    const int M = num_seqs * tokens_per_seq;
+    const int N = (num_q_heads + 2 * num_kv_heads) * head_dim;
+    int rc = check_gemm_shape(qkv, row_stride, x, x_stride, w_qkv, w_stride, M, N, hidden);
+    if (rc) return rc;
+    if (!aligned16(q_bias) || !aligned16(k_bias) || !aligned16(v_bias) || !aligned16(cos_cache) ||
+        !aligned16(sin_cache) || !aligned16(k_pool) || !aligned16(v_pool))
+        return LC_ERR_MISALIGNED;
+    if (M == 0) return LC_OK;
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = hidden;
+    p.m_tiles = (M + kBM - 1) / kBM;
+    p.n_tiles = (N + kBN - 1) / kBN;
+    p.out = (bf16 *)qkv;
+    p.out_stride = row_stride;
+    p.tokens_per_seq = tokens_per_seq;
+    p.positions = positions;
+    p.q_bias = (const bf16 *)q_bias;
+    p.k_bias = (const bf16 *)k_bias;
+    p.v_bias = (const bf16 *)v_bias;
+    p.cos_t = cos_cache;
+    p.sin_t = sin_cache;
+    p.rope_rows = rope_rows;
+    p.k_pool = (bf16 *)k_pool;
+    p.v_pool = (bf16 *)v_pool;
+    p.num_blocks = num_blocks;
+    p.num_layers = num_layers;
+    p.layer = layer;
+    p.num_q_heads = num_q_heads;
+    p.num_kv_heads = num_kv_heads;
+    p.head_dim = head_dim;
+    p.tables = block_tables;
+    p.table_stride = table_stride;
+    p.status = dev_status;
+    cudaStream_t s = as_stream(stream);
+    return head_dim == 64 ? launch_gemm<kQkvRope, 64>(p, x, x_stride, w_qkv, w_stride, s)
+                          : launch_gemm<kQkvRope, 128>(p, x, x_stride, w_qkv, w_stride, s);
+}

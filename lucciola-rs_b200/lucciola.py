@@ -68,6 +68,10 @@ SIGNATURES = {
     "lc_kv_cache_num_allocated_blocks": (_i32, [_vp]),
     "lc_kv_cache_free": (None, [_vp]),
     "lc_apply_flash_decoding": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _vp, _i32]),
+    "lc_proj_gemm": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp, _i64, _vp]),
+    "lc_qkv_proj_rope_append": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp,
+                                       _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _i64, _i32, _i32,
+                                       _i32, _i32, _i32, _vp, _i32, _vp, _vp]),
     "lc_block_alloc_new": (_i32, [_i64, _i32, _i32, C.POINTER(_vp)]),
     "lc_block_alloc_add_seq": (_i32, [_vp, _pi32]),
     "lc_block_alloc_release_seq": (_i32, [_vp, _i32]),
@@ -430,6 +434,29 @@ class BlockAlloc:
             self.close()
         except Exception:
             pass
+
+
+def proj_gemm(out, x, w, residual=None, stream=None):
+    """out = x . w^T (+ residual): bf16 [M, K] x [N, K] -> [M, N], fp32 accumulation."""
+    M, K = x.shape
+    N = w.shape[0]
+    check(lib.lc_proj_gemm(_p(out), out.stride(0), _p(x), x.stride(0), _p(w), w.stride(0), M, N,
+                           K, _p(residual), residual.stride(0) if residual is not None else 0,
+                           _stream(stream)), "lc_proj_gemm")
+
+
+def qkv_proj_rope_append(qkv, x, w_qkv, positions, q_bias, k_bias, v_bias, cos, sin, k_pool,
+                         v_pool, num_blocks, num_layers, layer, num_q_heads, num_kv_heads,
+                         head_dim, block_tables, tokens_per_seq=1, dev_status=None, stream=None):
+    """qkv = x . w_qkv^T with lc_rope_append fused into the epilogue."""
+    rows, hidden = x.shape
+    assert rows % tokens_per_seq == 0
+    check(lib.lc_qkv_proj_rope_append(
+        _p(qkv), qkv.stride(0), _p(x), x.stride(0), _p(w_qkv), w_qkv.stride(0), hidden,
+        rows // tokens_per_seq, tokens_per_seq, _p(positions), _p(q_bias), _p(k_bias),
+        _p(v_bias), _p(cos), _p(sin), cos.shape[0], _p(k_pool), _p(v_pool), num_blocks,
+        num_layers, layer, num_q_heads, num_kv_heads, head_dim, _p(block_tables),
+        block_tables.stride(0), _p(dev_status), _stream(stream)), "lc_qkv_proj_rope_append")
 
 
 def pool_blocks_for_budget(num_layers, num_kv_heads, head_dim, free_bytes, total_bytes,
