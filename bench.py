@@ -1,7 +1,7 @@
 """Benchmark of the paged decode-attention path on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c3|c5]
+                    [--config c2|c1|c3|c4|c4p|c5] [--driver]
 
 Default workload: BASELINE config 2 (Qwen2.5-0.5B shape batched ragged decode:
 64 sequences per GPU, 14 q heads / 2 KV heads, head_dim 64, context lengths
@@ -978,13 +978,109 @@ def run_prefill_bench(args, rank, world, local):
     del graph
 
 
+PROJ = {"c4p": ("qwen2.5-1.5b QKV projection of a 4 x 4096-token prompt with bias + RoPE + "
+                 "paged KV append fused into the GEMM epilogue (BASELINE config 4 shape)",
+                 4, 12, 2, 128, 1536, 4096)}
+
+
+def run_proj_bench(args, rank, world, local):
+    """lc_qkv_proj_rope_append: qkv = x . w_qkv^T on the tensor cores (CTA pairs)
+    with bias + RoPE + the paged K/V append in its epilogue, one launch per layer.
+    Beside it, the same work as the reference runs it: cublasGemmEx (through
+    torch.matmul, bf16 in, fp32 compute, bf16 out) then lc_rope_append."""
+    import lucciola as L
+    label, B, hq, hkv, hd, hidden, T = PROJ[args.config]
+    layers = 4  # distinct x / w per layer: 4 x 56 MB > 126 MB L2, no flush needed
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(777)
+    M, N, K = B * T, (hq + 2 * hkv) * hd, hidden
+    xs = [torch.randn(M, K, generator=gen, device=device).to(torch.bfloat16) for _ in range(layers)]
+    ws = [(torch.randn(N, K, generator=gen, device=device) * K ** -0.5).to(torch.bfloat16)
+          for _ in range(layers)]
+    qkv = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+    pages = (T + 15) // 16
+    nb = B * pages + 1
+    perm = torch.randperm(nb, generator=gen, device=device).to(torch.int32)
+    tables = perm[:B * pages].reshape(B, pages).contiguous()
+    k_pool = torch.zeros((nb, layers, hkv, 16, hd), dtype=torch.bfloat16, device=device)
+    v_pool = torch.zeros_like(k_pool)
+    bias = (torch.randn((layers, N), generator=gen, device=device) * 0.01).to(torch.bfloat16)
+    qb, kb, vb = (bias[:, :hq * hd].contiguous(), bias[:, hq * hd:(hq + hkv) * hd].contiguous(),
+                  bias[:, (hq + hkv) * hd:].contiguous())
+    cos, sin = (torch.from_numpy(x).to(device) for x in L.rope_table_host(T + 16, hd, 1e6))
+    positions = torch.arange(T, dtype=torch.int32, device=device).repeat(B)
+
+    def fused(l):
+        L.qkv_proj_rope_append(qkv, xs[l], ws[l], positions, qb[l], kb[l], vb[l], cos, sin,
+                               k_pool, v_pool, nb, layers, l, hq, hkv, hd, tables,
+                               tokens_per_seq=T)
+
+    def library(l):
+        torch.matmul(xs[l], ws[l].t(), out=qkv)
+        L.rope_append(qkv, positions, qb[l], kb[l], vb[l], cos, sin, k_pool, v_pool, nb, layers,
+                      l, hq, hkv, hd, tables, tokens_per_seq=T)
+
+    if args.mode == "kernel":  # eager launches only, for profilers
+        for i in range(args.warmup + args.steps):
+            fused(i % layers)
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": "kernel", "config": args.config, "launches":
+                          args.warmup + args.steps}))
+        return
+
+    def timed(fn):
+        for i in range(args.warmup):
+            fn(i % layers)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            fn(i % layers)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    sampler = ClockSampler(local)
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        fused(0)
+    torch.cuda.synchronize()
+    ms = timed(fused)
+    ms_lib = timed(library)
+    clocks = sampler.stop()
+    flops = 2.0 * M * N * K
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops_sustained") \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1400.0
+    value = flops / (ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "prefill QKV projection TFLOP/s (bias + RoPE + paged KV append fused)",
+        "value": round(value, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded bf16 ~N(0,1) x, w ~N(0,1/hidden))",
+        "config": {"workload": label, "tokens": M, "n": N, "k": K, "layers_rotated": layers,
+                   "l2": "no flush: 4 distinct x/w of 56 MB each > 126 MB L2"},
+        "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(value / peak, 4), "traffic": None,
+                     "kernel": "proj_gemm2_kernel<qkv rope>",
+                     "peak_kind": "measured (sustained cuBLAS bf16)"},
+        "library_path": {"ms": round(ms_lib, 5),
+                         "tflops": round(flops / (ms_lib * 1e-3) / 1e12, 1),
+                         "how": "torch.matmul (cublasGemmEx, bf16, fp32 compute) then "
+                                "lc_rope_append, as the reference sequences them"},
+        "gpu_launches": args.steps, "clocks": clocks}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(HEAD_SHARDED),
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(HEAD_SHARDED) +
+                    sorted(PROJ),
                     default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
@@ -1017,6 +1113,15 @@ def main():
                                   "single-GPU; its arm is run on the decode headline (config 2)"}))
             return 0
         run_head_sharded(args, rank, world, local)
+        return 0
+    if args.config in PROJ:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is run on "
+                              "the decode headline (config 2); its projection is cuBLAS, timed "
+                              "beside ours in this config's library_path"}))
+            return 0
+        if rank == 0:
+            run_proj_bench(args, rank, world, local)
         return 0
     if args.config in PREFILL:
         if args.impl == "reference":

@@ -179,6 +179,16 @@ namespace lc {
 // box_rows}, 128-byte swizzle, zero fill out of bounds. Not cached.
 int tensor_map_2d_sw128(const void *base, int64_t inner, int64_t rows, int64_t row_bytes,
                         int box_inner, int box_rows, CUtensorMap *out) {
+    return tensor_map_2d(base, inner, rows, row_bytes, box_inner, box_rows, 128, out);
+}
+
+// The same with a chosen swizzle span: 0 (none), 32, 64 or 128 bytes.
+int tensor_map_2d(const void *base, int64_t inner, int64_t rows, int64_t row_bytes, int box_inner,
+                  int box_rows, int swizzle_bytes, CUtensorMap *out) {
+    const CUtensorMapSwizzle swz = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                   : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                         : CU_TENSOR_MAP_SWIZZLE_NONE;
     if (!aligned16(base) || (row_bytes & 15)) return LC_ERR_MISALIGNED;
     if (inner <= 0 || rows <= 0 || rows >= (int64_t(1) << 31)) return LC_ERR_INVALID_ARGUMENT;
     auto fn = encode_fn();
@@ -188,7 +198,7 @@ int tensor_map_2d_sw128(const void *base, int64_t inner, int64_t rows, int64_t r
     cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? LC_OK : LC_ERR_CUDA;
 }

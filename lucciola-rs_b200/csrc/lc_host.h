@@ -33,6 +33,10 @@ int pool_tensor_map_nocache(const void *pool, int64_t rows, int head_dim, CUtens
 int tensor_map_2d_sw128(const void *base, int64_t inner, int64_t rows, int64_t row_bytes,
                         int box_inner, int box_rows, CUtensorMap *out);
 
+// The same with a swizzle span of 0 (none), 32, 64 or 128 bytes.
+int tensor_map_2d(const void *base, int64_t inner, int64_t rows, int64_t row_bytes, int box_inner,
+                  int box_rows, int swizzle_bytes, CUtensorMap *out);
+
 // Applies cudaFuncAttributeMaxDynamicSharedMemorySize once per (function, device).
 int ensure_smem_attr(const void *func, int bytes);
 

@@ -118,11 +118,77 @@ __device__ __forceinline__ int64_t pool_base(const GemmParams &p, int row, int p
            (int64_t)(pos % kBlockSize) * p.head_dim;
 }
 
+// Output of the epilogue warps. Direct: each thread stores its row's 32
+// values (the 1-SM kernel). Staged (CTA pairs): the warp's 32 rows x 32
+// columns go to shared memory (64-byte rows, 64-byte swizzle as the output
+// tensor map has it) and lane 0 writes them with one TMA store per box; two
+// buffers of two boxes per warp, so a step's stores overlap the next step.
+struct OutDirect {
+    bf16 *out;
+    int64_t stride;
+    __device__ __forceinline__ void begin() {}
+    __device__ __forceinline__ void put(int row, bool live, int col, int box, const float (&f)[32]) {
+        (void)box;
+        if (live) store32(out + (int64_t)row * stride + col, f);
+    }
+    __device__ __forceinline__ void issue(int, int, int, int, bool) {}
+    __device__ __forceinline__ void drain() {}
+};
+
+struct OutStaged {
+    uint8_t *base;  // this warp's 8 KiB, 2 KiB aligned
+    const CUtensorMap *map;
+    int step, lane;
+    __device__ __forceinline__ uint8_t *buf(int box) const {
+        return base + (step & 1) * 4096 + box * 2048;
+    }
+    // The buffer about to be written was last stored two steps ago.
+    __device__ __forceinline__ void begin() {
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
+    }
+    __device__ __forceinline__ void put(int, bool, int, int box, const float (&f)[32]) {
+        uint8_t *b = buf(box) + lane * 64;
+        const int sw = (lane >> 1) & 3;  // 64-byte swizzle: 16-byte chunk ^ address bits 7-8
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            uint4 o;
+            o.x = pack_bf16(f[8 * v + 0], f[8 * v + 1]);
+            o.y = pack_bf16(f[8 * v + 2], f[8 * v + 3]);
+            o.z = pack_bf16(f[8 * v + 4], f[8 * v + 5]);
+            o.w = pack_bf16(f[8 * v + 6], f[8 * v + 7]);
+            *reinterpret_cast<uint4 *>(b + ((v ^ sw) << 4)) = o;
+        }
+    }
+    // Boxes 0 .. nbox-1 of this step go to columns x0 / x1 of rows y .. y + 31.
+    __device__ __forceinline__ void issue(int nbox, int x0, int x1, int y, bool any_row) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0 && any_row) {
+            for (int b = 0; b < nbox; ++b)
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                        reinterpret_cast<uint64_t>(map)),
+                    "r"(b ? x1 : x0), "r"(y), "r"(smem_u32(buf(b)))
+                    : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        ++step;
+    }
+    // Before the CTA exits: every store has been written out.
+    __device__ __forceinline__ void drain() {
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        __syncwarp();
+    }
+};
+
 // Epilogue of one 256-column tile for the thread owning output row `row`
-// (TMEM lane quadrant base `tacc`): plain / residual; chunks half, half + 2, ...
-template <int EPI>
-__device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc, int row, int col0,
-                                              int half) {
+// (TMEM lane quadrant base `tacc`; the warp's rows start at `y`): plain /
+// residual; chunks half, half + 2, ...
+template <int EPI, class Out>
+__device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc, int row, int y,
+                                              int col0, int half, Out &o) {
+    const bool live = row < p.M;
 #pragma unroll 1
     for (int c = half; c < kBN / 32; c += 2) {
         const int col = col0 + 32 * c;
@@ -130,18 +196,24 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams &p, uint32_t tacc
         uint32_t r[32];
         tmem_ld32(tacc + 32 * c, r);
         tmem_wait_ld_regs(r);
-        if (row >= p.M) continue;
         float f[32];
         if constexpr (EPI == kResidual) {
             float res[32];
-            load32(p.residual + (int64_t)row * p.res_stride + col, res);
+            if (live) {
+                load32(p.residual + (int64_t)row * p.res_stride + col, res);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) res[i] = 0.f;
+            }
 #pragma unroll
             for (int i = 0; i < 32; ++i) f[i] = __fadd_rn(u2f(r[i]), res[i]);
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) f[i] = u2f(r[i]);
         }
-        store32(p.out + (int64_t)row * p.out_stride + col, f);
+        o.begin();
+        o.put(row, live, col, 0, f);
+        o.issue(1, col, 0, y, y < p.M);
     }
 }
 
@@ -181,16 +253,16 @@ struct QkvRow {
 
 // QKV epilogue: head by head over the tile's columns (a warp pair splits them:
 // 32-dim chunks half, half + 2, ... of the tile's half-heads). Per element the
-// arithmetic is that of rope_append_vec_kernel on the bf16-rounded GEMM result.
-template <int HD>
-__device__ __forceinline__ void epilogue_qkv(const GemmParams &p, uint32_t tacc, int row, int col0,
-                                             int half, const QkvRow<HD> &w) {
+// arithmetic is that of rope_append_vec_kernel on the bf16-rounded GEMM result;
+// the row keeps the projection where rope_append leaves it (v, a negative
+// position, a position past the RoPE table).
+template <int HD, class Out>
+__device__ __forceinline__ void epilogue_qkv(const GemmParams &p, uint32_t tacc, int row, int y,
+                                             int col0, int half, const QkvRow<HD> &w, Out &o) {
     constexpr int kHalf = HD / 2;
     const int hq = p.num_q_heads, hkv = p.num_kv_heads;
-    const bool live = w.live, rope_ok = w.rope_ok;
-    const int pos = w.pos;
+    const bool live = w.live;
     const int64_t base = w.base;
-    bf16 *orow = p.out + (int64_t)row * p.out_stride;
     const int64_t stride_blk = (int64_t)kBlockSize * HD;
     constexpr int kChunks = kHalf / 32;  // 32-dim chunks per half head
 #pragma unroll 1
@@ -200,50 +272,20 @@ __device__ __forceinline__ void epilogue_qkv(const GemmParams &p, uint32_t tacc,
         if (hc >= p.N) break;
         const int g = hc / HD;  // head index over [q | k | v]
         const int kind = g < hq ? 0 : (g < hq + hkv ? 1 : 2);
-        {
-            const int d0 = 32 * c;  // dims [d0, d0 + 32) of the first half, their partners
-            uint32_t r1[32], r2[32];
-            tmem_ld32(tacc + h * HD + d0, r1);
-            tmem_ld32(tacc + h * HD + kHalf + d0, r2);
-            tmem_wait_ld_regs(r1);
-            tmem_wait_ld_regs(r2);
-            if (!live) continue;
-            float x1[32], x2[32];
+        const int d0 = 32 * c;  // dims [d0, d0 + 32) of the first half, their partners
+        uint32_t r1[32], r2[32];
+        tmem_ld32(tacc + h * HD + d0, r1);
+        tmem_ld32(tacc + h * HD + kHalf + d0, r2);
+        tmem_wait_ld_regs(r1);
+        tmem_wait_ld_regs(r2);
+        float x1[32], x2[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                x1[i] = round_bf16(u2f(r1[i]));
-                x2[i] = round_bf16(u2f(r2[i]));
-            }
-            if (pos < 0) {  // the row is left as the projection wrote it
-                store32(orow + hc + d0, x1);
-                store32(orow + hc + kHalf + d0, x2);
-                continue;
-            }
-            if (kind == 2) {
-                // v: the row keeps the projection; the pool gets v + bias.
-                store32(orow + hc + d0, x1);
-                store32(orow + hc + kHalf + d0, x2);
-                if (base < 0) continue;
-                const int vh = g - hq - hkv;
-                const bf16 *vb = p.v_bias + vh * HD;
-                float b1[32], b2[32];
-                load32(vb + d0, b1);
-                load32(vb + kHalf + d0, b2);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    x1[i] = __fadd_rn(x1[i], b1[i]);
-                    x2[i] = __fadd_rn(x2[i], b2[i]);
-                }
-                bf16 *dst = p.v_pool + base + vh * stride_blk;
-                store32(dst + d0, x1);
-                store32(dst + kHalf + d0, x2);
-                continue;
-            }
-            if (!rope_ok) {  // past the RoPE table: q and k stay unrotated, k is not appended
-                store32(orow + hc + d0, x1);
-                store32(orow + hc + kHalf + d0, x2);
-                continue;
-            }
+        for (int i = 0; i < 32; ++i) {
+            x1[i] = round_bf16(u2f(r1[i]));
+            x2[i] = round_bf16(u2f(r2[i]));
+        }
+        const bool appendable = live && w.pos >= 0 && base >= 0;
+        if (live && w.pos >= 0 && kind != 2 && w.rope_ok) {
             const int hh = kind == 0 ? g : g - hq;
             const bf16 *bias = (kind == 0 ? p.q_bias : p.k_bias) + hh * HD;
             // rotated in place: element i reads x1[i], x2[i] before writing them
@@ -271,16 +313,39 @@ __device__ __forceinline__ void epilogue_qkv(const GemmParams &p, uint32_t tacc,
                     x2[i] = rot_add(v1, w.sn[i], v2, w.cs[i]);
                 }
             }
-            store32(orow + hc + d0, x1);
-            store32(orow + hc + kHalf + d0, x2);
-            if (kind == 1) {
-                if (base >= 0) {
-                    bf16 *dst = p.k_pool + base + hh * stride_blk;
-                    store32(dst + d0, x1);
-                    store32(dst + kHalf + d0, x2);
+        }
+        // The row: q / k rotated, v (and rows rope_append skips) as projected.
+        o.begin();
+        o.put(row, live, hc + d0, 0, x1);
+        o.put(row, live, hc + kHalf + d0, 1, x2);
+        if (appendable) {
+            if (kind == 1 && w.rope_ok) {
+                bf16 *dst = p.k_pool + base + (g - hq) * stride_blk;
+                store32(dst + d0, x1);
+                store32(dst + kHalf + d0, x2);
+            } else if (kind == 2) {  // past the RoPE table k is not appended, v still is
+                const int vh = g - hq - hkv;
+                const bf16 *vb = p.v_bias + vh * HD;
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                    const uint4 u1 = reinterpret_cast<const uint4 *>(vb + d0)[v];
+                    const uint4 u2 = reinterpret_cast<const uint4 *>(vb + kHalf + d0)[v];
+                    const __nv_bfloat162 *h1 = reinterpret_cast<const __nv_bfloat162 *>(&u1);
+                    const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&u2);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        x1[8 * v + 2 * i] = __fadd_rn(x1[8 * v + 2 * i], __low2float(h1[i]));
+                        x1[8 * v + 2 * i + 1] = __fadd_rn(x1[8 * v + 2 * i + 1], __high2float(h1[i]));
+                        x2[8 * v + 2 * i] = __fadd_rn(x2[8 * v + 2 * i], __low2float(h2[i]));
+                        x2[8 * v + 2 * i + 1] = __fadd_rn(x2[8 * v + 2 * i + 1], __high2float(h2[i]));
+                    }
                 }
+                bf16 *dst = p.v_pool + base + vh * stride_blk;
+                store32(dst + d0, x1);
+                store32(dst + kHalf + d0, x2);
             }
         }
+        o.issue(2, hc + d0, hc + kHalf + d0, y, y < p.M);
     }
 }
 
@@ -393,16 +458,18 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             const int mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
             const int row = mt * kBM + r, col0 = nt * kBN;
             const uint32_t tacc = tmem + ((uint32_t)(quad * 32) << 16) + buf * kBN;
+            OutDirect o{p.out, p.out_stride};
+            const int y = mt * kBM + quad * 32;
             if constexpr (EPI == kQkvRope) {
                 QkvRow<HD> w;
                 w.load(p, row, col0, half);  // overlaps the tile's MMAs
                 if (!mbar_wait_bounded(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status)) break;
                 tc_fence_after();
-                epilogue_qkv<HD>(p, tacc, row, col0, half, w);
+                epilogue_qkv<HD>(p, tacc, row, y, col0, half, w, o);
             } else {
                 if (!mbar_wait_bounded(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status)) break;
                 tc_fence_after();
-                epilogue_rows<EPI>(p, tacc, row, col0, half);
+                epilogue_rows<EPI>(p, tacc, row, y, col0, half, o);
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[buf]);
@@ -413,6 +480,165 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemColsG);
+    }
+}
+
+
+// ------------------------------------------------------------ CTA pairs --
+// The same GEMM over 256 x 256 tiles shared by a cluster of two CTAs
+// (tcgen05.mma.cta_group::2): CTA r loads rows [128 r, 128 r + 128) of the
+// tile's x rows and of its w rows, so a K block costs each CTA 32 KiB of
+// loads instead of 48 KiB. Rank 0 issues the MMAs; the pair's loads complete
+// on its stage barriers, its commits arrive on both CTAs' barriers, and both
+// CTAs' epilogue warps release the accumulator to it. The epilogue writes its
+// rows through shared memory with TMA stores (OutStaged).
+constexpr int kStages2 = 5;
+constexpr uint32_t kHalfTile = 128 * kBK * 2;  // 16 KiB: 128 rows of one operand
+constexpr uint32_t kStageBytes2 = 2 * kHalfTile;
+constexpr uint32_t kStageOut = 8192;  // per epilogue warp: 2 buffers x 2 boxes of 32 x 32
+constexpr int kSmem2 = kStages2 * kStageBytes2 + kEpiWarps * kStageOut + 1024;
+constexpr uint32_t kIdesc2 = idesc_bf16_f32(256, kBN, 0);
+constexpr int kBM2 = 256;
+
+template <int EPI, int HD>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
+    proj_gemm2_kernel(const __grid_constant__ CUtensorMap tm_a,
+                      const __grid_constant__ CUtensorMap tm_b,
+                      const __grid_constant__ CUtensorMap tm_out, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *gen = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[kStages2];
+    __shared__ __align__(8) uint64_t empty[kStages2];
+    __shared__ __align__(8) uint64_t acc_full[2];
+    __shared__ __align__(8) uint64_t acc_empty[2];
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int s_abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages2; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * kEpiWarps);
+        }
+        s_abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_2sm(&tmem_base_sh, kTmemColsG);
+        tmem_relinquish_2sm();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers exist and the pair's TMEM is allocated
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+    const int pairs = (int)(gridDim.x >> 1), pair = (int)(blockIdx.x >> 1);
+    const int tiles = p.m_tiles * p.n_tiles;
+    const int kblocks = (p.K + kBK - 1) / kBK;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA --
+        if (lane == 0) {
+            prefetch_tensormap(&tm_a);
+            prefetch_tensormap(&tm_b);
+            int it = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += pairs) {
+                const int mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages2;
+                    if (it >= kStages2 &&
+                        !mbar_wait_bounded_cluster(&empty[s], ((it / kStages2) - 1) & 1, &s_abort,
+                                                   p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * kStageBytes2);
+                    const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+                    uint8_t *st = gen + s * kStageBytes2;
+                    tma_load_2d_2sm(st, &tm_a, kb * kBK, mt * kBM2 + (int)rank * 128, fb);
+                    tma_load_2d_2sm(st + kHalfTile, &tm_b, kb * kBK, nt * kBN + (int)rank * 128, fb);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------- MMA (rank 0 only) --
+        if (leader && lane == 0) {
+            int it = 0, tl = 0;
+            bool ok = true;
+            for (int tile = pair; tile < tiles && ok; tile += pairs, ++tl) {
+                const int buf = tl & 1;
+                if (tl >= 2 && !mbar_wait_bounded_cluster(&acc_empty[buf], ((tl >> 1) - 1) & 1,
+                                                          &s_abort, p.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + buf * kBN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages2;
+                    if (!mbar_wait_bounded_cluster(&full[s], (it / kStages2) & 1, &s_abort,
+                                                   p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(gen + s * kStageBytes2), b = a + kHalfTile;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_bf16_2sm(d, sw128_desc(a + kk * 32, 16, 1024),
+                                      sw128_desc(b + kk * 32, 16, 1024), kIdesc2,
+                                      (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit_2sm(&empty[s], 0x3);  // frees the stage in both CTAs
+                }
+                if (ok) umma_commit_2sm(&acc_full[buf], 0x3);
+            }
+        }
+    } else {
+        // ----------------------------------------------------------- epilogue --
+        const int quad = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int r = quad * 32 + lane;
+        const uint32_t release = mapa_shared(smem_u32(&acc_empty[0]), 0);
+        OutStaged o{gen + kStages2 * kStageBytes2 + (warp - 2) * kStageOut, &tm_out, 0, lane};
+        if (lane == 0) prefetch_tensormap(&tm_out);
+        int tl = 0;
+        for (int tile = pair; tile < tiles; tile += pairs, ++tl) {
+            const int buf = tl & 1;
+            const int mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
+            const int row = mt * kBM2 + (int)rank * 128 + r, col0 = nt * kBN;
+            const uint32_t tacc = tmem + ((uint32_t)(quad * 32) << 16) + buf * kBN;
+            const int y = mt * kBM2 + (int)rank * 128 + quad * 32;
+            if constexpr (EPI == kQkvRope) {
+                QkvRow<HD> w;
+                w.load(p, row, col0, half);  // overlaps the tile's MMAs
+                if (!mbar_wait_bounded_cluster(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status))
+                    break;
+                tc_fence_after();
+                epilogue_qkv<HD>(p, tacc, row, y, col0, half, w, o);
+            } else {
+                if (!mbar_wait_bounded_cluster(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status))
+                    break;
+                tc_fence_after();
+                epilogue_rows<EPI>(p, tacc, row, y, col0, half, o);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(release + buf * 8);  // acc_empty[buf] of rank 0
+        }
+        o.drain();
+    }
+    tc_fence_before();
+    cluster_sync();  // the pair's MMAs, copies and arrivals are over before TMEM is freed
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_2sm(tmem, kTmemColsG);
     }
 }
 
@@ -430,6 +656,59 @@ int launch_gemm(const GemmParams &prm, const void *x, int64_t x_stride, const vo
     const int grid = tiles < sm_count() ? tiles : sm_count();
     proj_gemm_kernel<EPI, HD><<<grid, kThreadsG, kSmemG, stream>>>(ma, mb, prm);
     return launch_status();
+}
+
+// Clusters of two that fit on the current device at once (cached per device).
+template <int EPI, int HD>
+int pair_slots() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return sm_count() / 2;
+    }
+    if (!cached[dev]) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(kThreadsG);
+        cfg.dynamicSmemBytes = kSmem2;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, proj_gemm2_kernel<EPI, HD>, &cfg) != cudaSuccess ||
+            n < 1) {
+            cudaGetLastError();
+            n = sm_count() / 2;
+        }
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+// M > 128: tiles of 256 rows on CTA pairs; the pair count is what fits at once.
+template <int EPI, int HD>
+int launch_gemm2(GemmParams prm, const void *x, int64_t x_stride, const void *w,
+                 int64_t w_stride, cudaStream_t stream) {
+    prm.m_tiles = (prm.M + kBM2 - 1) / kBM2;
+    CUtensorMap ma, mb, mo;
+    int rc = tensor_map_2d_sw128(x, prm.K, prm.M, x_stride * 2, kBK, 128, &ma);
+    if (rc) return rc;
+    rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kBK, 128, &mb);
+    if (rc) return rc;
+    rc = tensor_map_2d(prm.out, prm.N, prm.M, prm.out_stride * 2, 32, 32, 64, &mo);
+    if (rc) return rc;
+    rc = ensure_smem_attr((const void *)proj_gemm2_kernel<EPI, HD>, kSmem2);
+    if (rc) return rc;
+    const int tiles = prm.m_tiles * prm.n_tiles;
+    const int slots = pair_slots<EPI, HD>();
+    const int pairs = tiles < slots ? tiles : slots;
+    proj_gemm2_kernel<EPI, HD><<<2 * pairs, kThreadsG, kSmem2, stream>>>(ma, mb, mo, prm);
+    return launch_status();
+}
+
+template <int EPI, int HD>
+int launch_any(const GemmParams &prm, const void *x, int64_t x_stride, const void *w,
+               int64_t w_stride, cudaStream_t stream) {
+    return prm.M > kBM ? launch_gemm2<EPI, HD>(prm, x, x_stride, w, w_stride, stream)
+                       : launch_gemm<EPI, HD>(prm, x, x_stride, w, w_stride, stream);
 }
 
 int check_gemm_shape(const void *out, int64_t out_stride, const void *x, int64_t x_stride,
@@ -469,8 +748,8 @@ extern "C" int lc_proj_gemm(void *out, int64_t out_stride, const void *x, int64_
     p.residual = (const bf16 *)residual;
     p.res_stride = res_stride;
     cudaStream_t s = as_stream(stream);
-    return residual ? launch_gemm<kResidual, 64>(p, x, x_stride, w, w_stride, s)
-                    : launch_gemm<kPlain, 64>(p, x, x_stride, w, w_stride, s);
+    return residual ? launch_any<kResidual, 64>(p, x, x_stride, w, w_stride, s)
+                    : launch_any<kPlain, 64>(p, x, x_stride, w, w_stride, s);
 }
 
 extern "C" int lc_qkv_proj_rope_append(void *qkv, int64_t row_stride, const void *x,
@@ -531,6 +810,6 @@ extern "C" int lc_qkv_proj_rope_append(void *qkv, int64_t row_stride, const void
     p.table_stride = table_stride;
     p.status = dev_status;
     cudaStream_t s = as_stream(stream);
-    return head_dim == 64 ? launch_gemm<kQkvRope, 64>(p, x, x_stride, w_qkv, w_stride, s)
-                          : launch_gemm<kQkvRope, 128>(p, x, x_stride, w_qkv, w_stride, s);
+    return head_dim == 64 ? launch_any<kQkvRope, 64>(p, x, x_stride, w_qkv, w_stride, s)
+                          : launch_any<kQkvRope, 128>(p, x, x_stride, w_qkv, w_stride, s);
 }
