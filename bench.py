@@ -1,7 +1,7 @@
 """Benchmark of the paged decode-attention path on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c3|c4|c4p|c5] [--driver]
+                    [--config c2|c1|c3|c4|c4p|c5|s2] [--driver]
 
 Default workload: BASELINE config 2 (Qwen2.5-0.5B shape batched ragged decode:
 64 sequences per GPU, 14 q heads / 2 KV heads, head_dim 64, context lengths
@@ -1073,6 +1073,86 @@ def run_proj_bench(args, rank, world, local):
         "gpu_launches": args.steps, "clocks": clocks}), flush=True)
 
 
+SAMPLING = {"s2": ("top-k / top-p token sampling over the Qwen2 vocabulary for config 2's batch "
+                   "(64 rows x 151936 logits, top_k 64, top_p 0.9)", 64, 151936, 64, 0.9)}
+
+
+def run_sampling_bench(args, rank, world, local):
+    """lc_sample_top_p on a batch of logits rows (one launch of the 32-partition
+    top-k filter for all rows, one of the sort-and-draw). --impl reference runs
+    the reference's kernels (oracle/_ref) one row at a time, as
+    CudaFunctions::apply_sort_and_sample launches them."""
+    label, B, V, top_k, top_p = SAMPLING[args.config]
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99)
+    nbuf = 8  # 8 x 19.4 MB of logits > 126 MB L2: no flush needed
+    logits = [(torch.randn(B, V, generator=gen, device=device) * 3).to(torch.bfloat16)
+              for _ in range(nbuf)]
+    rand = torch.rand(B, generator=gen, device=device)
+    tp = torch.full((B,), top_p, dtype=torch.float32, device=device)
+    out = torch.zeros(B, dtype=torch.int32, device=device)
+    if args.impl == "reference":
+        import ctypes as C
+        import oracle.oracle as O
+        R = O.ref_lib()
+        cand = torch.zeros(2 * 32 * (top_k // 32), dtype=torch.int32, device=device)
+        stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        rv = rand.cpu().tolist()
+
+        def step(i):
+            x = logits[i % nbuf]
+            for r in range(B):
+                R.ref_sample_top_p(C.c_void_p(x[r].data_ptr()), V, top_k, top_p, rv[r],
+                                   C.c_void_p(cand.data_ptr()), C.c_void_p(out[r:].data_ptr()),
+                                   stream)
+        launches = 2 * B
+    else:
+        import lucciola as L
+        ws = L.alloc_sample_workspace(B, top_k, device=device)
+
+        def step(i):
+            L.sample_top_p(out, logits[i % nbuf], top_k, tp, rand, ws)
+        launches = 2
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    peak, peak_kind = measured_peak()
+    gbs = B * V * 2 / (ms * 1e-3) / 1e9
+    line = {"metric": "token sampling rows/s (top-k 64, top-p 0.9, Qwen2 vocabulary)",
+            "value": round(B / (ms * 1e-3), 1), "unit": "rows/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded bf16 logits ~N(0, 9), uniform draws)",
+            "config": {"workload": label, "rows": B, "vocab": V, "top_k": top_k,
+                       "top_p": top_p, "l2": "8 rotating logits batches of 19.4 MB > L2"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None,
+                         "kernel": "topk_filter_kernel + sort_sample_kernel",
+                         "peak_kind": f"{peak_kind} (burst copy)",
+                         "algorithmic_bytes": B * V * 2},
+            "gpu_launches": launches * args.steps, "clocks": clocks}
+    if args.impl == "reference":
+        line["impl"] = "reference"
+        line["cpu_baseline"] = {"value": line["value"], "unit": "rows/s", "cores": 0,
+                                "kind": "reference",
+                                "sample": "the reference's CUDA kernels (oracle/_ref), one row "
+                                          "per launch pair; its path has no CPU implementation"}
+        line["e2e"] = {"value": line["value"], "unit": "rows/s", "h2d_bytes_per_step": 0,
+                       "d2h_bytes_per_step": 0}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1080,7 +1160,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(HEAD_SHARDED) +
-                    sorted(PROJ),
+                    sorted(PROJ) + sorted(SAMPLING),
                     default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
@@ -1113,6 +1193,10 @@ def main():
                                   "single-GPU; its arm is run on the decode headline (config 2)"}))
             return 0
         run_head_sharded(args, rank, world, local)
+        return 0
+    if args.config in SAMPLING:
+        if rank == 0:
+            run_sampling_bench(args, rank, world, local)
         return 0
     if args.config in PROJ:
         if args.impl == "reference":

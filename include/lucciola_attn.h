@@ -336,6 +336,40 @@ int lc_qkv_proj_rope_append(void *qkv, int64_t row_stride, const void *x, int64_
                             int table_stride, int *dev_status, lc_stream_t stream);
 
 /* ------------------------------------------------------------------------- */
+/* Token selection from the logits of a batch of sequences.                   */
+/* ------------------------------------------------------------------------- */
+/* Greedy: out_idx[b] = index of the largest logit of row b (rows of `vocab`
+ * bf16, row_stride elements apart), as CudaFunctions::apply_argmax /
+ * argmax_kernel (src/kernels.rs:322-344, src/kernels/sampling.cu) chooses it,
+ * ties included (lower i % 1024, then lower i); 0xffffffff when no logit
+ * exceeds -1e30. One launch for the whole batch. */
+int lc_argmax(const void *logits, int64_t row_stride, int vocab, int batch, unsigned *out_idx,
+              lc_stream_t stream);
+
+/* Bytes of candidates lc_sample_top_p keeps per call: batch * n * 8, with
+ * n = 32 * (top_k / 32); 0 for an unsupported top_k. Layout: int32 keys
+ * [batch][n], then float values [batch][n], each row partition-major as the
+ * reference's top_k_filter writes its candidates. */
+size_t lc_sample_workspace_size(int batch, int top_k);
+
+/* Top-k / top-p sampling, as CudaFunctions::apply_sort_and_sample
+ * (src/kernels.rs:346-490, src/kernels/sampling_optimized.cu) for each row b:
+ * the top_k / 32 largest logits of each of 32 vocabulary partitions, sorted
+ * (descending, the reference's bitonic network), softmax over them, the
+ * smallest prefix whose probability reaches top_p[b], and the candidate whose
+ * cumulative interval holds rand_vals[b] * that prefix's probability (device
+ * arrays of `batch` floats; the reference draws rand_val on the host per
+ * step). n = 32 * (top_k / 32) must be a power of two from 32 to 1024
+ * (LC_ERR_UNSUPPORTED_SHAPE otherwise, as the reference bails), vocab >= 32.
+ * The candidate set is exact; the draw equals the reference's except where
+ * rand * cutoff falls within fp32 rounding of a cumulative boundary. When no
+ * candidate wins (rounding at the top) out_idx[b] is left as it was, as in the
+ * reference. Two launches for the whole batch. */
+int lc_sample_top_p(const void *logits, int64_t row_stride, int vocab, int batch, int top_k,
+                    const float *top_p, const float *rand_vals, unsigned *out_idx,
+                    void *workspace, size_t workspace_bytes, lc_stream_t stream);
+
+/* ------------------------------------------------------------------------- */
 /* Batched token-step driver: many sequences in one paged pool.               */
 /* ------------------------------------------------------------------------- */
 /* The reference's KVCache holds one sequence (one block table,

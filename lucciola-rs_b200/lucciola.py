@@ -72,6 +72,9 @@ SIGNATURES = {
     "lc_qkv_proj_rope_append": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _vp,
                                        _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp, _i64, _i32, _i32,
                                        _i32, _i32, _i32, _vp, _i32, _vp, _vp]),
+    "lc_argmax": (_i32, [_vp, _i64, _i32, _i32, _vp, _vp]),
+    "lc_sample_workspace_size": (_sz, [_i32, _i32]),
+    "lc_sample_top_p": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
     "lc_block_alloc_new": (_i32, [_i64, _i32, _i32, C.POINTER(_vp)]),
     "lc_block_alloc_add_seq": (_i32, [_vp, _pi32]),
     "lc_block_alloc_release_seq": (_i32, [_vp, _i32]),
@@ -457,6 +460,29 @@ def qkv_proj_rope_append(qkv, x, w_qkv, positions, q_bias, k_bias, v_bias, cos, 
         _p(v_bias), _p(cos), _p(sin), cos.shape[0], _p(k_pool), _p(v_pool), num_blocks,
         num_layers, layer, num_q_heads, num_kv_heads, head_dim, _p(block_tables),
         block_tables.stride(0), _p(dev_status), _stream(stream)), "lc_qkv_proj_rope_append")
+
+
+def argmax(out_idx, logits, stream=None):
+    """out_idx[b] = index of the largest logit of row b (int32 tensor, bits of uint32)."""
+    batch, vocab = logits.shape
+    check(lib.lc_argmax(_p(logits), logits.stride(0), vocab, batch, _p(out_idx), _stream(stream)),
+          "lc_argmax")
+
+
+def alloc_sample_workspace(batch, top_k, device="cuda"):
+    import torch
+    n = lib.lc_sample_workspace_size(batch, top_k)
+    if n == 0:
+        raise LucciolaError(3, "lc_sample_workspace_size")
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def sample_top_p(out_idx, logits, top_k, top_p, rand_vals, workspace, stream=None):
+    """Top-k / top-p draw per row; top_p and rand_vals are float32 device tensors [batch]."""
+    batch, vocab = logits.shape
+    check(lib.lc_sample_top_p(_p(logits), logits.stride(0), vocab, batch, top_k, _p(top_p),
+                              _p(rand_vals), _p(out_idx), _p(workspace), workspace.numel(),
+                              _stream(stream)), "lc_sample_top_p")
 
 
 def pool_blocks_for_budget(num_layers, num_kv_heads, head_dim, free_bytes, total_bytes,

@@ -364,3 +364,128 @@ int lco_gather_kv(uint16_t *k_out, uint16_t *v_out, const uint16_t *k_pool,
     }
     return err;
 }
+
+/* ------------------------------------------------------------- sampling --
+ * Restatement of the reference's token selection (src/kernels/sampling.cu,
+ * src/kernels/sampling_optimized.cu; launched by src/kernels.rs:322-490).
+ * Ties are resolved as the reference's reductions resolve them: argmax_kernel
+ * (1024 threads, cub block reduction, left operand kept on ties) prefers the
+ * lowest thread i % 1024, then the first i of that thread; top_k_filter (256
+ * threads, shfl_down tree over offsets 16..1 keeping its own value on ties,
+ * for lanes and then for warps) prefers warps and lanes in bit-reversed order,
+ * then the first index of the thread. */
+
+static int bitrev5(int x) {
+    int r = 0;
+    for (int b = 0; b < 5; ++b) r |= ((x >> b) & 1) << (4 - b);
+    return r;
+}
+
+/* argmax_kernel: index of the largest logit above -1e30 (-1 if none). */
+int lco_argmax(const uint16_t *logits, int vocab) {
+    int best = -1;
+    float bv = -1e30f;
+    for (int i = 0; i < vocab; ++i) {
+        const float v = lco_bf16_to_f32(logits[i]);
+        if (v > bv) {
+            best = i, bv = v;
+        } else if (v == bv && best >= 0 && (i % 1024) < (best % 1024)) {
+            best = i;  /* an earlier thread holds an equal maximum */
+        }
+    }
+    return best;
+}
+
+/* top_k_filter over 32 partitions [p*V/32, (p+1)*V/32): each yields its kpb
+ * largest logits in order, by repeated block argmax with removal (a removed
+ * or exhausted entry reads as -1e30 and is never chosen again). keys/values:
+ * [32 * kpb], partition-major; an exhausted partition gives key start - 1 and
+ * value -1e30. */
+void lco_top_k_filter(const uint16_t *logits, int vocab, int kpb, int *keys, float *values) {
+    for (int p = 0; p < 32; ++p) {
+        const int start = (int)((long long)p * vocab / 32);
+        const int end = (int)((long long)(p + 1) * vocab / 32);
+        const int n = end - start;
+        float *v = (float *)malloc(sizeof(float) * (n > 0 ? n : 1));
+        for (int i = 0; i < n; ++i) v[i] = lco_bf16_to_f32(logits[start + i]);
+        for (int k = 0; k < kpb; ++k) {
+            int best = -1;
+            float bv = -1e30f;
+            for (int i = 0; i < n; ++i) {
+                if (v[i] > bv) {
+                    best = i, bv = v[i];
+                } else if (v[i] == bv && best >= 0) {
+                    const int t = i % 256, tb = best % 256;
+                    const int pr = bitrev5(t / 32) * 32 + bitrev5(t % 32);
+                    const int pb = bitrev5(tb / 32) * 32 + bitrev5(tb % 32);
+                    if (pr < pb) best = i;  /* same value, preferred thread */
+                }
+            }
+            if (n <= 0) continue;  /* the reference writes nothing for an empty partition */
+            keys[p * kpb + k] = start + best;
+            values[p * kpb + k] = bv;
+            if (best >= 0) v[best] = -1e30f;
+        }
+        free(v);
+    }
+}
+
+/* fused_top_p_sample_impl<n>: bitonic sort of the n candidates (descending,
+ * the reference's compare-exchange network, so equal values keep its order),
+ * softmax over them, the top-p cutoff and the draw. Sums here are in double;
+ * *margin returns how far (in probability) the draw and the cutoff were from
+ * a boundary, so that a caller comparing with fp32 arithmetic can skip draws
+ * that rounding could move. Returns the chosen key, or -1 when no candidate
+ * wins (the reference then leaves its output untouched). */
+int lco_top_p_sample(const int *keys_in, const float *values_in, int n, float top_p,
+                     float rand_val, double *margin) {
+    int *keys = (int *)malloc(sizeof(int) * n);
+    float *vals = (float *)malloc(sizeof(float) * n);
+    memcpy(keys, keys_in, sizeof(int) * n);
+    memcpy(vals, values_in, sizeof(float) * n);
+    for (int k = 2; k <= n; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1)
+            for (int t = 0; t < n; ++t) {
+                const int o = t ^ j;
+                if (o <= t) continue;
+                const int sw = (t & k) == 0 ? vals[t] < vals[o] : vals[t] > vals[o];
+                if (sw) {
+                    const float tv = vals[t];
+                    const int tk = keys[t];
+                    vals[t] = vals[o], keys[t] = keys[o];
+                    vals[o] = tv, keys[o] = tk;
+                }
+            }
+    double *e = (double *)malloc(sizeof(double) * n);
+    double total = 0.0;
+    for (int t = 0; t < n; ++t) {
+        e[t] = exp((double)vals[t] - (double)vals[0]);
+        total += e[t];
+    }
+    double cdf = 0.0, cutoff = 1.0, m = 1.0;
+    for (int t = 0; t < n; ++t) {
+        const double prev = cdf;
+        cdf += e[t] / total;
+        if (prev < top_p && cdf >= top_p) cutoff = cdf;
+        /* a cumulative value next to top_p can move the cutoff to the next
+         * candidate's; past the last one the alternative is 1.0, which the
+         * last cumulative value equals up to rounding */
+        const double d = fabs(cdf - top_p);
+        if (t < n - 1 && d < m) m = d;
+    }
+    const double target = (double)rand_val * cutoff;
+    int chosen = -1;
+    cdf = 0.0;
+    for (int t = 0; t < n; ++t) {
+        const double prev = cdf;
+        cdf += e[t] / total;
+        if (cdf >= target && prev < target) chosen = keys[t];
+        const double d = fabs(cdf - target);
+        if (d < m) m = d;
+    }
+    if (margin) *margin = m;
+    free(e);
+    free(keys);
+    free(vals);
+    return chosen;
+}

@@ -95,6 +95,12 @@ int lco_gather_kv(uint16_t *k_out, uint16_t *v_out, const uint16_t *k_pool,
                   const int *context_lens, int len_offset, int batch,
                   int max_context_len);
 
+/* Token selection (src/kernels/sampling.cu, sampling_optimized.cu). */
+int lco_argmax(const uint16_t *logits, int vocab);
+void lco_top_k_filter(const uint16_t *logits, int vocab, int kpb, int *keys, float *values);
+int lco_top_p_sample(const int *keys, const float *values, int n, float top_p, float rand_val,
+                     double *margin);
+
 #ifdef __cplusplus
 }
 #endif

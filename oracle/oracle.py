@@ -59,6 +59,11 @@ def lib():
         L.lco_paged_prefill.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                         _i32, _i32, _vp, _i32, _vp, _i32, _i32, _f32, _i32]
         L.lco_paged_prefill.restype = _i32
+        L.lco_argmax.argtypes = [_vp, _i32]
+        L.lco_argmax.restype = _i32
+        L.lco_top_k_filter.argtypes = [_vp, _i32, _i32, _vp, _vp]
+        L.lco_top_p_sample.argtypes = [_vp, _vp, _i32, _f32, _f32, C.POINTER(C.c_double)]
+        L.lco_top_p_sample.restype = _i32
         L.lco_gather_kv.argtypes = [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32,
                                     _vp, _i32, _i32, _i32]
         L.lco_gather_kv.restype = _i32
@@ -209,6 +214,8 @@ def ref_lib():
                                        _i32, _vp, _i32, _vp, _vp, _i32, _i32, _vp]
         R.ref_rope_append.argtypes = [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp]
+        R.ref_argmax.argtypes = [_vp, _i32, _vp, _vp]
+        R.ref_sample_top_p.argtypes = [_vp, _i32, _i32, _f32, _f32, _vp, _vp, _vp]
         R.ref_prefill.argtypes = [_vp, _i64, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
                                   _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _i32,
                                   _i32, _vp]
@@ -217,3 +224,34 @@ def ref_lib():
             getattr(R, f).restype = _i32
         _ref = R
     return _ref
+
+
+# ----------------------------------------------------------------- sampling --
+
+def argmax(logits):
+    """argmax_kernel (src/kernels/sampling.cu): per row, with its tie order."""
+    logits = np.ascontiguousarray(logits, dtype=np.uint16)
+    rows = logits.reshape(-1, logits.shape[-1])
+    return np.array([lib().lco_argmax(_ptr(np.ascontiguousarray(r)), r.shape[0]) for r in rows],
+                    np.int64)
+
+
+def top_k_filter(logits, top_k):
+    """top_k_filter (src/kernels/sampling_optimized.cu): 32 partitions x top_k/32
+    candidates of one row, partition-major: (keys int32, values float32)."""
+    row = np.ascontiguousarray(logits, dtype=np.uint16)
+    kpb = top_k // 32
+    keys = np.zeros(32 * kpb, np.int32)
+    vals = np.zeros(32 * kpb, np.float32)
+    lib().lco_top_k_filter(_ptr(row), row.shape[0], kpb, _ptr(keys), _ptr(vals))
+    return keys, vals
+
+
+def top_p_sample(keys, values, top_p, rand_val):
+    """fused_top_p_sample_impl: (chosen key or -1, margin to the nearest boundary)."""
+    keys = np.ascontiguousarray(keys, dtype=np.int32)
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    m = C.c_double()
+    k = lib().lco_top_p_sample(_ptr(keys), _ptr(values), keys.shape[0], float(top_p),
+                               float(rand_val), C.byref(m))
+    return k, m.value

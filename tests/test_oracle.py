@@ -182,3 +182,47 @@ def test_rope_append_oracle_semantics():
         assert np.array_equal(kp[blk, case.layer, :, p % 16, :].ravel(), qkv[b, hq * hd:nq])
         assert np.array_equal(vp[blk, case.layer, :, p % 16, :].ravel(),
                               O.f32_to_bf16(O.bf16_to_f32(before[b, nq:]) + O.bf16_to_f32(vb)))
+
+
+# ----------------------------------------------------------------- sampling --
+
+def _bf(values):
+    return O.f32_to_bf16(np.asarray(values, np.float32))
+
+
+def test_oracle_argmax_tie_order():
+    """argmax_kernel keeps, among equal maxima, the lowest thread i % 1024 and
+    then that thread's first index (src/kernels/sampling.cu)."""
+    x = np.full(5000, O.f32_to_bf16(np.float32(0.0)), np.uint16)
+    x[[10, 1029, 4000]] = O.f32_to_bf16(np.float32(3.0))   # threads 10, 5, 928
+    assert int(O.argmax(x)[0]) == 1029
+    x[[1029]] = O.f32_to_bf16(np.float32(1.0))
+    x[[2058, 10]] = O.f32_to_bf16(np.float32(3.0))           # thread 10 twice: first index
+    assert int(O.argmax(x)[0]) == 10
+    assert int(O.argmax(_bf([-2e30] * 64))[0]) == -1         # nothing above -1e30
+
+
+def test_oracle_top_k_filter_partitions_and_ties():
+    """Each of 32 partitions yields its own top k/32 (not the global top-k);
+    equal values go in the bit-reversed warp / lane order of thread i % 256."""
+    vocab = 32 * 600
+    x = np.zeros(vocab, np.float32)
+    x[:600] = np.arange(600, dtype=np.float32) / 100.0   # partition 0 holds the 600 largest
+    keys, vals = O.top_k_filter(O.f32_to_bf16(x), 128)   # 4 per partition
+    assert keys[0] == 599 and vals[0] == 6.0               # partition 0: its own top 4
+    # 5.97 and 5.98 round to the same bf16 as 5.96: indices 596-598 tie on
+    # threads 84-86 (warp 2, lanes 20-22; bit-reversed lane order 20, 22, 21)
+    assert list(keys[1:4]) == [596, 598, 597]
+    # partition 1 is all zeros: thread 0 (warp 0, lane 0) comes first with all
+    # of its elements (offsets 0, 256, 512), then lane 16 (bit-reversed 1)
+    assert list(keys[4:8]) == [600, 856, 1112, 616] and (vals[4:8] == 0).all()
+
+
+def test_oracle_top_p_sample_small_cases():
+    keys = np.arange(32, dtype=np.int32)
+    vals = np.full(32, -1e30, np.float32)
+    vals[0], vals[1] = 0.0, float(np.log(3.0))    # probabilities 1/4, 3/4 after sorting: 3/4 first
+    k, m = O.top_p_sample(keys, vals, 0.5, 0.5)   # cutoff at 3/4: always key 1
+    assert k == 1
+    k, m = O.top_p_sample(keys, vals, 0.9, 0.9)   # cutoff 1.0, target 0.9 > 0.75: key 0
+    assert k == 0
