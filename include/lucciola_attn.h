@@ -342,7 +342,7 @@ int lc_qkv_proj_rope_append(void *qkv, int64_t row_stride, const void *x, int64_
  * bf16, row_stride elements apart), as CudaFunctions::apply_argmax /
  * argmax_kernel (src/kernels.rs:322-344, src/kernels/sampling.cu) chooses it,
  * ties included (lower i % 1024, then lower i); 0xffffffff when no logit
- * exceeds -1e30. One launch for the whole batch. */
+ * exceeds -1e30. One launch for the whole batch; any row stride. */
 int lc_argmax(const void *logits, int64_t row_stride, int vocab, int batch, unsigned *out_idx,
               lc_stream_t stream);
 

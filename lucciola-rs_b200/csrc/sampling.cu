@@ -7,10 +7,10 @@
 //
 // The reference runs one sequence per launch; here one launch covers the batch
 // (a block per row, or per (row, vocabulary partition)), reads the bf16 logits
-// with 16-byte loads and keeps the candidates in a caller workspace. Results
-// equal the reference's: the candidate set is that of its 32-partition top-k
-// filter, and ties are broken in the order its reductions break them, stated
-// as explicit keys:
+// (argmax with 16-byte loads where rows are aligned) and keeps the candidates in
+// a caller workspace. Results equal the reference's: the candidate set is that
+// of its 32-partition top-k filter, and ties are broken in the order its
+// reductions break them, stated as explicit keys:
 //   argmax:      larger value, then lower i % 1024 (the reference thread), then
 //                lower i;
 //   top-k:       per partition of [p*V/32, (p+1)*V/32): larger value, then the
@@ -82,11 +82,11 @@ __device__ __forceinline__ Cand block_best(Cand c, Cand *red) {
 
 // ------------------------------------------------------------------ argmax --
 __global__ void __launch_bounds__(1024) argmax_kernel(const bf16 *logits, int64_t stride, int vocab,
-                                                      unsigned *out) {
+                                                      unsigned *out, int vec) {
     __shared__ Cand red[32];
     const bf16 *row = logits + (int64_t)blockIdx.x * stride;
     Cand best{kNone, -1};
-    const int n8 = vocab >> 3;
+    const int n8 = vec ? vocab >> 3 : 0;  // rows not 16-byte aligned: element by element
     for (int c = threadIdx.x; c < n8; c += blockDim.x) {
         const uint4 u = reinterpret_cast<const uint4 *>(row)[c];
         const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
@@ -235,10 +235,10 @@ extern "C" int lc_argmax(const void *logits, int64_t row_stride, int vocab, int 
                          unsigned *out_idx, lc_stream_t stream) {
     if (!logits || !out_idx || vocab <= 0 || batch < 0 || row_stride < vocab)
         return LC_ERR_INVALID_ARGUMENT;
-    if (!aligned16(logits) || (row_stride & 7)) return LC_ERR_MISALIGNED;
     if (batch == 0) return LC_OK;
+    const int vec = aligned16(logits) && (row_stride & 7) == 0;
     argmax_kernel<<<batch, 1024, 0, as_stream(stream)>>>((const bf16 *)logits, row_stride, vocab,
-                                                          out_idx);
+                                                          out_idx, vec);
     return launch_status();
 }
 

@@ -62,10 +62,10 @@ class Mirror:
             t[i, :len(pg)] = pg
         return t
 
-    def prefill(self, slot, tokens):
-        self.pool.prepare_prefill(slot, 0, tokens)
+    def prefill(self, slot, tokens, start=0):
+        self.pool.prepare_prefill(slot, start, tokens)
         tab = self.tables([slot])
-        pos = np.arange(tokens, dtype=np.int32)
+        pos = np.arange(start, start + tokens, dtype=np.int32)
         for layer in range(LAYERS):
             qkv = rows(self.rng, (tokens, ROW))
             dqkv = to_device(qkv)
@@ -75,7 +75,7 @@ class Mirror:
             O.rope_append(qkv, pos, qb, kb, vb, self.cos, self.sin, self.k, self.v, LAYERS,
                           layer, HQ, HKV, HD, tab, tokens_per_seq=tokens)
             ref = O.paged_prefill(np.ascontiguousarray(qkv[:, :HQ * HD]), self.k, self.v, layer,
-                                  HQ, HKV, HD, tab, np.zeros(1, np.int32), tokens, LAYERS,
+                                  HQ, HKV, HD, tab, np.full(1, start, np.int32), tokens, LAYERS,
                                   threads=8)
             torch.cuda.synchronize()
             check_attention(out, ref)
@@ -195,3 +195,31 @@ def test_pool_decode_graph_replay_matches_eager():
     del graph
     for p in pools:
         p.close()
+
+
+def test_pool_chunked_prefill_then_decode():
+    """A prompt in three chunks (prepare_prefill with a start position): each
+    chunk attends over the pages the earlier chunks filled; then decode steps."""
+    pool = L.KVPool(LAYERS, HQ, HKV, HD, 2, MAX_LEN, NB)
+    m = Mirror(pool, seed=9)
+    s = pool.add_sequence()
+    start = 0
+    for tokens in (100, 37, 130):  # chunk boundaries inside pages
+        m.prefill(s, tokens, start=start)
+        start += tokens
+    assert len(pool.pages(s)) == (start + 15) // 16
+    for _ in range(2):
+        pool.prepare_step([s], [start])
+        qkvs = m.decode_inputs(1)
+        outs = []
+        for layer in range(LAYERS):
+            out = torch.empty(1, HQ * HD, dtype=torch.bfloat16, device="cuda")
+            pool.decode_layer(layer, out, to_device(qkvs[layer]), *m.dbias[layer], m.dcos, m.dsin)
+            outs.append(out)
+        refs = m.decode_reference([s], [start], qkvs)
+        torch.cuda.synchronize()
+        for out, ref in zip(outs, refs):
+            check_attention(out, ref)
+        start += 1
+    m.check_pools()
+    pool.close()

@@ -60,13 +60,22 @@ def test_argmax_matches_oracle_and_reference_with_ties():
         ref.append(int(from_device(o).view(np.uint32)[0]))
     assert list(ours) == list(orc) == ref
     assert ours[1] == 1024 + 5 and ours[2] == 7 and ours[4] == 0xFFFFFFFF
+    # rows of odd length (unaligned rows: element by element), with ties
+    y = _logits(rng, 3, vocab=300001, quantum=0.5)
+    out3 = torch.zeros(3, dtype=torch.int32, device="cuda")
+    L.argmax(out3, to_device(y))
+    torch.cuda.synchronize()
+    assert list(from_device(out3).view(np.uint32).astype(np.int64)) == list(O.argmax(y))
 
 
-@pytest.mark.parametrize("top_k,quantum", [(64, None), (256, 0.25), (1024, None), (32, 0.5)])
-def test_top_k_candidates_match_oracle_and_reference(top_k, quantum):
+@pytest.mark.parametrize("top_k,quantum,vocab", [
+    (64, None, VOCAB), (256, 0.25, VOCAB), (1024, None, VOCAB), (32, 0.5, VOCAB),
+    (64, 0.5, 300001),  # odd row length: unaligned rows and partitions
+])
+def test_top_k_candidates_match_oracle_and_reference(top_k, quantum, vocab):
     rng = np.random.default_rng(top_k)
     rows = 3
-    x = _logits(rng, rows, quantum=quantum)
+    x = _logits(rng, rows, vocab=vocab, quantum=quantum)
     d = to_device(x)
     n = 32 * (top_k // 32)
     ws = L.alloc_sample_workspace(rows, top_k)
@@ -84,7 +93,7 @@ def test_top_k_candidates_match_oracle_and_reference(top_k, quantum):
         assert np.array_equal(keys[r], ok) and np.array_equal(vals[r], ov)
         cand = torch.zeros(n * 2, dtype=torch.int32, device="cuda")  # {int key, float value}
         o = torch.zeros(1, dtype=torch.int32, device="cuda")
-        assert R.ref_sample_top_p(_ptr(d[r]), VOCAB, top_k, 0.9, 0.5, _ptr(cand), _ptr(o),
+        assert R.ref_sample_top_p(_ptr(d[r]), vocab, top_k, 0.9, 0.5, _ptr(cand), _ptr(o),
                                   _stream()) == 0
         torch.cuda.synchronize()
         rc = from_device(cand).reshape(n, 2)
