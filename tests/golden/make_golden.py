@@ -1,11 +1,12 @@
 """Generates the golden fixtures that pin the CPU oracle to the reference.
 
-Runs the reference's own CUDA kernels (src/kernels/{rope,kv_cache,attention}.cu,
-compiled unchanged into oracle/_ref/libref_kernels.so) on seeded inputs on a
+Runs the reference's own CUDA kernels (src/kernels/{rope,kv_cache,attention,
+sampling,sampling_optimized}.cu, compiled unchanged into oracle/_ref/libref_kernels.so)
+on seeded inputs on a
 GPU and stores inputs and outputs as small .npz files next to this script.
 tests/test_golden.py then checks the CPU oracle against them on any machine.
 
-    python tests/golden/make_golden.py [--out DIR]   # needs a GPU and oracle/_ref
+    python tests/golden/make_golden.py [--out DIR] [--only NAME ...]   # needs a GPU and oracle/_ref
 """
 from __future__ import annotations
 
@@ -94,21 +95,63 @@ def attention_fixture(R, hq, hkv, hd, pos, seed):
                 out=from_device(out))
 
 
+def sampling_fixture(R, vocab, rows, seed):
+    """argmax_kernel, top_k_filter (top_k 64 and 256) and fused_top_p_sample on
+    quantised logits (many ties), with a few (top_p, rand) draws per row."""
+    rng = np.random.default_rng(seed)
+    x = np.round(rng.standard_normal((rows, vocab)).astype(np.float32) * 6.0) / 2.0
+    logits = O.f32_to_bf16(x)
+    d = to_device(logits)
+    draws = np.array([(0.3, 0.25), (0.9, 0.5), (0.9, 0.97), (1.0, 0.61)], np.float32)
+    out = dict(vocab=vocab, logits=logits, draws=draws)
+    am = []
+    for r in range(rows):
+        o = torch.zeros(1, dtype=torch.int32, device="cuda")
+        assert R.ref_argmax(p(d[r]), vocab, p(o), s()) == 0
+        torch.cuda.synchronize()
+        am.append(int(from_device(o).view(np.uint32)[0]))
+    out["argmax"] = np.array(am, np.int64)
+    for top_k in (64, 256):
+        keys, vals, picks = [], [], []
+        for r in range(rows):
+            row_picks = []
+            for top_p, rand in draws:
+                cand = torch.zeros(2 * top_k, dtype=torch.int32, device="cuda")
+                o = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+                assert R.ref_sample_top_p(p(d[r]), vocab, top_k, float(top_p), float(rand),
+                                          p(cand), p(o), s()) == 0
+                torch.cuda.synchronize()
+                row_picks.append(int(from_device(o)[0]))
+            c = from_device(cand).reshape(top_k, 2)
+            keys.append(c[:, 0].copy())
+            vals.append(c[:, 1].view(np.float32).copy())
+            picks.append(row_picks)
+        out[f"keys_{top_k}"] = np.stack(keys)
+        out[f"values_{top_k}"] = np.stack(vals)
+        out[f"picks_{top_k}"] = np.array(picks, np.int64)
+    return out
+
+
 def main() -> int:
     import argparse
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default=str(HERE), help="directory for the .npz files")
-    out_dir = Path(ap.parse_args().out)
+    ap.add_argument("--only", nargs="*", default=None, help="fixture names to (re)generate")
+    args = ap.parse_args()
+    out_dir = Path(args.out)
     out_dir.mkdir(parents=True, exist_ok=True)
     R = O.ref_lib()
-    fx = {
-        "rope_hd64": rope_fixture(R, 64, 14, 2, 1),
-        "rope_hd128": rope_fixture(R, 128, 28, 4, 2),
-        "update_kv_cache": update_fixture(R, 3),
-        "attention_hd64": attention_fixture(R, 14, 2, 64, 150, 4),
-        "attention_hd128": attention_fixture(R, 12, 2, 128, 77, 5),
-        "attention_hd128_gqa8": attention_fixture(R, 16, 2, 128, 40, 6),
+    makers = {
+        "rope_hd64": lambda: rope_fixture(R, 64, 14, 2, 1),
+        "rope_hd128": lambda: rope_fixture(R, 128, 28, 4, 2),
+        "update_kv_cache": lambda: update_fixture(R, 3),
+        "attention_hd64": lambda: attention_fixture(R, 14, 2, 64, 150, 4),
+        "attention_hd128": lambda: attention_fixture(R, 12, 2, 128, 77, 5),
+        "attention_hd128_gqa8": lambda: attention_fixture(R, 16, 2, 128, 40, 6),
+        "sampling": lambda: sampling_fixture(R, 8192 + 37, 4, 7),
     }
+    names = args.only if args.only else list(makers)
+    fx = {name: makers[name]() for name in names}
     for name, d in fx.items():
         path = out_dir / f"{name}.npz"
         np.savez_compressed(path, **{k: np.asarray(v) for k, v in d.items()})

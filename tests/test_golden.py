@@ -1,9 +1,10 @@
 """Pins the CPU oracle to the reference: golden fixtures recorded from the
 reference's own CUDA kernels on a B200 (tests/golden/make_golden.py).
 
-RoPE and the KV append must match bit for bit; attention must match within
-4e-3 (the oracle follows attention.cu's warp structure and summation order;
-only the last bits of expf differ between glibc and CUDA). No GPU needed."""
+RoPE, the KV append, the greedy index and the sampling candidates must match
+bit for bit; attention must match within 4e-3 (the oracle follows
+attention.cu's warp structure and summation order; only the last bits of expf
+differ between glibc and CUDA). No GPU needed."""
 from pathlib import Path
 
 import numpy as np
@@ -13,7 +14,7 @@ import oracle.oracle as O
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 FIXTURES = ["rope_hd64", "rope_hd128", "update_kv_cache", "attention_hd64", "attention_hd128",
-            "attention_hd128_gqa8"]
+            "attention_hd128_gqa8", "sampling"]
 
 
 def load(name):
@@ -56,3 +57,26 @@ def test_attention_oracle_matches_reference_kernel(name):
     assert err <= 4e-3
     # most elements are bit-identical
     assert (out == f["out"]).mean() > 0.9
+
+
+def test_sampling_oracle_matches_reference_kernels():
+    """argmax_kernel, top_k_filter and fused_top_p_sample (run on a GPU by
+    tests/golden/make_golden.py) against the CPU oracle: the greedy index and the
+    candidate keys and values exactly, ties included (the logits are quantised);
+    the draws wherever they are not within rounding of a boundary."""
+    g = np.load(GOLDEN / "sampling.npz")
+    logits, draws = g["logits"], g["draws"]
+    assert list(O.argmax(logits)) == list(g["argmax"])
+    checked = 0
+    for top_k in (64, 256):
+        for r in range(logits.shape[0]):
+            keys, vals = O.top_k_filter(logits[r], top_k)
+            assert np.array_equal(keys, g[f"keys_{top_k}"][r])
+            assert np.array_equal(vals, g[f"values_{top_k}"][r])
+            for j, (top_p, rand) in enumerate(draws):
+                want, margin = O.top_p_sample(keys, vals, top_p, rand)
+                if margin < 1e-5:
+                    continue
+                assert want == g[f"picks_{top_k}"][r, j]
+                checked += 1
+    assert checked >= 24
