@@ -638,10 +638,13 @@ def run_driver(args, rank, world, local):
         dist.destroy_process_group()
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one fused decode launch of the
-# bench workload, from the ncu captures summarised in profiles/paged_decode_c2.md
-# and profiles/paged_decode_c3.md (same per-launch work as the bench's launches).
-TRAFFIC: dict = {"c2": 75958016, "c3": 543651840}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of each config's
+# dominant kernel, from the ncu captures summarised in profiles/ (same
+# per-launch work as the bench's launches): the fused decode (c2, c3), the
+# prefill (c4, reported in MB to one decimal there), the fused QKV projection
+# (c4p) and the top-k filter (s2).
+TRAFFIC: dict = {"c2": 75958016, "c3": 543651840, "c4": 77800000, "c4p": 101494272,
+                 "s2": 19465984}
 
 
 # ------------------------------------------------------------ reference arm --
@@ -967,7 +970,8 @@ def run_prefill_bench(args, rank, world, local):
                    "step": "per layer: lc_rope_append (prompt rows) + lc_paged_prefill; CUDA graph"},
         "ms_per_layer": round(ms_step / layers, 4),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_sust,
-                     "unit": "TFLOP/s", "frac": round(achieved / peak_sust, 4), "traffic": None,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_sust, 4),
+                     "traffic": TRAFFIC.get(args.config),
                      "kernel": f"paged_prefill_kernel<{hd}>",
                      "peak_kind": f"{kind} (sustained bf16 GEMM; burst {peak_burst})",
                      "launch_ms": round(launch_ms, 4)},
@@ -1063,7 +1067,8 @@ def run_proj_bench(args, rank, world, local):
         "config": {"workload": label, "tokens": M, "n": N, "k": K, "layers_rotated": layers,
                    "l2": "no flush: 4 distinct x/w of 56 MB each > 126 MB L2"},
         "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(value / peak, 4), "traffic": None,
+                     "unit": "TFLOP/s", "frac": round(value / peak, 4),
+                     "traffic": TRAFFIC.get(args.config),
                      "kernel": "proj_gemm2_kernel<qkv rope>",
                      "peak_kind": "measured (sustained cuBLAS bf16)"},
         "library_path": {"ms": round(ms_lib, 5),
@@ -1137,7 +1142,7 @@ def run_sampling_bench(args, rank, world, local):
             "config": {"workload": label, "rows": B, "vocab": V, "top_k": top_k,
                        "top_p": top_p, "l2": "8 rotating logits batches of 19.4 MB > L2"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "traffic": None,
+                         "frac": round(gbs / peak, 4), "traffic": TRAFFIC.get(args.config),
                          "kernel": "topk_filter_kernel + sort_sample_kernel",
                          "peak_kind": f"{peak_kind} (burst copy)",
                          "algorithmic_bytes": B * V * 2},
