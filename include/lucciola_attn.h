@@ -435,7 +435,9 @@ int lc_kv_pool_release_sequence(lc_kv_pool *p, int slot);
  * order) and positions are copied to the pool's device buffers on `stream`.
  * Those buffers keep their addresses, so the per-layer launches of a step may
  * be captured once in a CUDA graph and replayed after each prepare_step with
- * the same batch size. */
+ * the same batch size. On LC_ERR_OUT_OF_BLOCKS the sequences before the one
+ * that failed keep the pages they were given (they need them next step as
+ * well) and nothing is uploaded. */
 int lc_kv_pool_prepare_step(lc_kv_pool *p, lc_stream_t stream, int batch,
                             const int *slots, const int *positions);
 /* Layer `layer` of the prepared step: bias + RoPE + append of each row's new
