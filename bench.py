@@ -211,8 +211,9 @@ class OursStep:
         self.fused = fused
         self.ws = L.alloc_decode_workspace(w.batch, w.hq, w.hkv, w.hd, device=w.device)
 
-    def layer(self, l, decode_events=None):
+    def layer(self, l, decode_events=None, out=None, gate=None):
         w, L = self.w, self.L
+        out = w.out[l] if out is None else out
         if not self.fused:
             L.rope_append(w.qkv[l], w.positions, w.q_bias[l], w.k_bias[l], w.v_bias[l], w.cos,
                           w.sin, w.k_pool, w.v_pool, w.num_blocks, w.layers, l, w.hq, w.hkv,
@@ -220,12 +221,12 @@ class OursStep:
         if decode_events is not None:
             decode_events[0].record()
         if self.fused:
-            L.rope_append_decode(w.out[l], w.qkv[l], w.positions, w.q_bias[l], w.k_bias[l],
+            L.rope_append_decode(out, w.qkv[l], w.positions, w.q_bias[l], w.k_bias[l],
                                  w.v_bias[l], w.cos, w.sin, w.k_pool, w.v_pool, w.num_blocks,
                                  w.layers, l, w.hq, w.hkv, w.hd, w.tables, w.max_ctx,
-                                 partition_tokens=w.ptok, workspace=self.ws)
+                                 partition_tokens=w.ptok, workspace=self.ws, gate=gate)
         else:
-            L.paged_decode(w.out[l], w.qkv[l], w.k_pool, w.v_pool, w.num_blocks, w.layers, l,
+            L.paged_decode(out, w.qkv[l], w.k_pool, w.v_pool, w.num_blocks, w.layers, l,
                            w.hq, w.hkv, w.hd, w.tables, w.positions, w.max_ctx, len_offset=1,
                            partition_tokens=w.ptok, workspace=self.ws)
         if decode_events is not None:
@@ -371,49 +372,86 @@ def run_ours(args, rank, world, local):
     ms_step = ms_total / args.steps
 
     # e2e: the step's inputs come from pinned host memory and its outputs go
-    # back, through the same C-ABI calls. A copy stream carries the transfers
-    # next to the compute stream. Inputs go in groups of 1, 2, 4, 8, ... layers
-    # (the first layer starts after one layer's copy; a cross-stream wait in
-    # front of a launch costs its programmatic overlap with the launch before,
-    # so waits are few); outputs go back in the mirrored groups (..., 4, 2, 1
-    # layers), each as soon as its last layer is done, so the last copy is short.
-    # The whole step, transfers included, is one CUDA graph.
+    # back, through the same C-ABI calls, inside the timed region. The whole
+    # step, transfers included, is one CUDA graph. Inputs go in groups of 1, 2,
+    # 4, 8, ... layers (the first layer starts after one layer's copy).
     qkv_host = w.qkv.cpu().pin_memory()
     pos_host = w.positions.cpu().pin_memory()
-    out_host = torch.empty(w.out.shape, dtype=w.out.dtype).pin_memory()
     comp_s, copy_s = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
     groups, g0, size = [], 0, 1
     while g0 < w.layers:
         groups.append((g0, min(g0 + size, w.layers)))
         g0, size = g0 + size, size * 2
-    out_groups, g1 = [], w.layers
-    for a, b in groups:  # mirrored sizes, from the last layer backwards
-        out_groups.append((g1 - (b - a), g1))
-        g1 -= b - a
-    out_end = {b - 1: (a, b) for a, b in out_groups}
+    host_out = None
     g_e2e = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_e2e, stream=comp_s):
-        copy_s.wait_stream(comp_s)
-        ev_in = {}
-        with torch.cuda.stream(copy_s):
-            w.positions.copy_(pos_host, non_blocking=True)
-            for a, b in groups:
-                w.qkv[a:b].copy_(qkv_host[a:b], non_blocking=True)
-                ev = torch.cuda.Event()
-                ev.record(copy_s)
-                ev_in[a] = ev
-        for l in range(w.layers):
-            if l in ev_in:
-                comp_s.wait_event(ev_in[l])
-            runner.layer(l)
-            if l in out_end:
-                a, b = out_end[l]
-                ev = torch.cuda.Event()
-                ev.record(comp_s)
-                copy_s.wait_event(ev)
-                with torch.cuda.stream(copy_s):
-                    out_host[a:b].copy_(w.out[a:b], non_blocking=True)
-        comp_s.wait_stream(copy_s)
+    if runner.fused:
+        # Fused step: each group's copy is followed on the copy stream by a
+        # 4-byte copy that sets the group's gate; each layer's launch waits for
+        # its gate on the device before it reads its rows, so the compute stream
+        # holds decode launches only and keeps their programmatic overlap. The
+        # launches write their outputs straight into mapped pinned host memory.
+        from cuda.bindings import runtime as cudart
+        nbytes = w.out.numel() * 2
+        err, hptr = cudart.cudaHostAlloc(nbytes, cudart.cudaHostAllocMapped)
+        assert int(err) == 0, err
+        err, dptr = cudart.cudaHostGetDevicePointer(hptr, 0)
+        assert int(err) == 0 and int(dptr) == int(hptr), (err, dptr, hptr)
+        import ctypes
+        host_out = hptr
+        out_host = torch.frombuffer((ctypes.c_uint8 * nbytes).from_address(int(hptr)),
+                                    dtype=torch.bfloat16).view(w.out.shape)
+        gates = torch.zeros(len(groups), dtype=torch.int32, device=device)
+        one_host = torch.ones(1, dtype=torch.int32).pin_memory()
+        group_of = {l: gi for gi, (a, b) in enumerate(groups) for l in range(a, b)}
+        with torch.cuda.graph(g_e2e, stream=comp_s):
+            copy_s.wait_stream(comp_s)
+            w.positions.copy_(pos_host, non_blocking=True)  # read by the launches' set-up
+            with torch.cuda.stream(copy_s):
+                for gi, (a, b) in enumerate(groups):
+                    w.qkv[a:b].copy_(qkv_host[a:b], non_blocking=True)
+                    gates[gi:gi + 1].copy_(one_host, non_blocking=True)
+            for l in range(w.layers):
+                runner.layer(l, out=out_host[l], gate=gates[group_of[l]:group_of[l] + 1])
+            comp_s.wait_stream(copy_s)
+            gates.zero_()  # closed again for the next step
+        e2e_how = ("pinned host qkv/positions in (qkv in groups of 1, 2, 4, ... layers on a copy "
+                   "stream, each group opening a device gate the layer's launch waits on); the "
+                   "launches write their outputs into mapped pinned host memory; one CUDA graph")
+    else:
+        # Two-launch step: cross-stream waits on the copies; outputs go back in
+        # the mirrored groups (..., 4, 2, 1 layers), each as soon as its last
+        # layer is done.
+        out_host = torch.empty(w.out.shape, dtype=w.out.dtype).pin_memory()
+        out_groups, g1 = [], w.layers
+        for a, b in groups:
+            out_groups.append((g1 - (b - a), g1))
+            g1 -= b - a
+        out_end = {b - 1: (a, b) for a, b in out_groups}
+        with torch.cuda.graph(g_e2e, stream=comp_s):
+            copy_s.wait_stream(comp_s)
+            ev_in = {}
+            with torch.cuda.stream(copy_s):
+                w.positions.copy_(pos_host, non_blocking=True)
+                for a, b in groups:
+                    w.qkv[a:b].copy_(qkv_host[a:b], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(copy_s)
+                    ev_in[a] = ev
+            for l in range(w.layers):
+                if l in ev_in:
+                    comp_s.wait_event(ev_in[l])
+                runner.layer(l)
+                if l in out_end:
+                    a, b = out_end[l]
+                    ev = torch.cuda.Event()
+                    ev.record(comp_s)
+                    copy_s.wait_event(ev)
+                    with torch.cuda.stream(copy_s):
+                        out_host[a:b].copy_(w.out[a:b], non_blocking=True)
+            comp_s.wait_stream(copy_s)
+        e2e_how = ("pinned host qkv/positions in (groups of 1, 2, 4, ... layers), outputs out "
+                   "(mirrored groups), on a copy stream overlapped with the compute stream; one "
+                   "CUDA graph")
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -490,9 +528,7 @@ def run_ours(args, rank, world, local):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(w.h2d_bytes), "d2h_bytes_per_step": int(w.d2h_bytes),
                     "ms_per_step": round(e2e_ms_step, 5),
-                    "how": "pinned host qkv/positions in (groups of 1, 2, 4, ... layers), "
-                           "outputs out (mirrored groups), on a copy stream overlapped with the "
-                           "compute stream; one CUDA graph"},
+                    "how": e2e_how},
             "gpu_launches": runner.launches_per_step * args.steps,
             "clocks": clocks,
         }
@@ -502,6 +538,10 @@ def run_ours(args, rank, world, local):
             line["cpu_baseline"] = None
         print(json.dumps(line), flush=True)
     del graph, g_e2e
+    if host_out is not None:
+        torch.cuda.synchronize()
+        from cuda.bindings import runtime as cudart
+        cudart.cudaFreeHost(host_out)
     if dist:
         dist.barrier()
         dist.destroy_process_group()

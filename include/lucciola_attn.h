@@ -154,7 +154,9 @@ int lc_rope_append(void *qkv, int64_t row_stride, int num_seqs,
 size_t lc_paged_decode_workspace_size(int batch, int num_q_heads,
                                       int num_kv_heads, int head_dim);
 /* Zeroes the workspace (once, after allocation). Every lc_paged_decode call
- * leaves its arrival counters at zero again. */
+ * leaves its arrival counters at zero again, except one whose status word
+ * reports LC_DEV_TIMEOUT: a launch that gave up may leave counters set, so
+ * zero the workspace again before the next call. */
 int lc_paged_decode_workspace_init(void *workspace, size_t workspace_bytes,
                                    lc_stream_t stream);
 
@@ -204,6 +206,26 @@ int lc_rope_append_decode(void *out, int64_t out_stride, const void *qkv,
                           int partition_tokens, float sm_scale, void *workspace,
                           size_t workspace_bytes, int *dev_status,
                           lc_stream_t stream);
+
+/* lc_rope_append_decode with an input gate: the launch reads its qkv rows only
+ * once the int at `gate` (device-visible memory) is non-zero, waiting for it
+ * on the device (2 s at most, then LC_DEV_TIMEOUT in the status word). For a
+ * step whose rows arrive by a host-to-device copy on another stream that then
+ * sets the gate (a 4-byte copy after the rows' copy, in the same stream): the
+ * decode launches need no cross-stream dependency, which would cost each one
+ * its programmatic overlap with the launch before. The caller clears the gate
+ * before the next use. out may be mapped pinned host memory (the outputs then
+ * cross PCIe as they are written). */
+int lc_rope_append_decode_gated(void *out, int64_t out_stride, const void *qkv,
+                                int64_t row_stride, const int *positions, const void *q_bias,
+                                const void *k_bias, const void *v_bias, const float *cos_cache,
+                                const float *sin_cache, int rope_rows, void *k_pool,
+                                void *v_pool, int64_t num_blocks, int num_layers, int layer,
+                                int num_q_heads, int num_kv_heads, int head_dim,
+                                const int *block_tables, int table_stride, int batch,
+                                int max_context_len, int partition_tokens, float sm_scale,
+                                void *workspace, size_t workspace_bytes, int *dev_status,
+                                const int *gate, lc_stream_t stream);
 
 /* Allocation-free variant of lc_paged_decode. No counterpart in the reference.
  * For callers that cannot allocate device memory while they decode (a serving
@@ -467,6 +489,9 @@ int lc_kv_pool_table_stride(const lc_kv_pool *p);
 int64_t lc_kv_pool_num_blocks(const lc_kv_pool *p);
 int64_t lc_kv_pool_num_free_blocks(const lc_kv_pool *p);
 int lc_kv_pool_sequence_pages(const lc_kv_pool *p, int slot, int *dst, int capacity);
+/* After a decode layer whose status word reported LC_DEV_TIMEOUT: zeroes the
+ * pool's split-K workspace on `stream` (see lc_paged_decode_workspace_init). */
+int lc_kv_pool_recover(lc_kv_pool *p, lc_stream_t stream);
 /* lc_block_alloc_fingerprint of the pool's page bookkeeping. */
 uint64_t lc_kv_pool_fingerprint(const lc_kv_pool *p);
 void lc_kv_pool_free(lc_kv_pool *p);

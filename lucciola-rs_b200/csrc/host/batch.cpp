@@ -412,6 +412,11 @@ extern "C" int lc_kv_pool_prefill_layer(lc_kv_pool *p, lc_stream_t stream, int l
                             p->pf_start, 1.0f / std::sqrt((float)p->head_dim), dev_status, stream);
 }
 
+extern "C" int lc_kv_pool_recover(lc_kv_pool *p, lc_stream_t stream) {
+    if (!p) return LC_ERR_INVALID_ARGUMENT;
+    return lc_paged_decode_workspace_init(p->workspace, p->workspace_bytes, stream);
+}
+
 extern "C" uint64_t lc_kv_pool_fingerprint(const lc_kv_pool *p) {
     return p ? lc_block_alloc_fingerprint(p->alloc) : 0;
 }

@@ -110,6 +110,9 @@ struct DecodeParams {
     // qkv rows [q | k | v]; context_lens holds the new token's position.
     const bf16 *qkv;
     const bf16 *q_bias, *k_bias, *v_bias;
+    // Optional input gate: the qkv rows are read only once *gate != 0 (a flag
+    // a copy stream sets after the rows' host-to-device copy).
+    const int *gate;
     const float *cos_t, *sin_t;
     int rope_rows;
     bf16 *k_pool_w, *v_pool_w;
@@ -204,6 +207,30 @@ struct ChunkCursor {
         return false;
     }
 };
+
+// Fused mode, epilogue warp: waits (bounded) until *gate is non-zero before
+// the first qkv row is read. Lane 0 polls with acquire loads; a timeout sets
+// LC_DEV_TIMEOUT and the abort flag (the rows are then not trusted).
+__device__ __forceinline__ void gate_wait(const int *gate, volatile int *abort_flag, int *status,
+                                          int lane) {
+    if (lane == 0) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(gate) : "memory");
+        if (v == 0) {
+            const uint64_t t0 = global_timer_ns();
+            for (uint32_t it = 1;; ++it) {
+                asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(gate) : "memory");
+                if (v != 0) break;
+                if ((it & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+                    *abort_flag = 1;
+                    set_status(status, LC_DEV_TIMEOUT);
+                    break;
+                }
+            }
+        }
+    }
+    __syncwarp();
+}
 
 // Fused mode, epilogue warp: everything a chunk needs from the qkv rows, made
 // ahead of the consumer warps (signalled on `ready`):
@@ -823,6 +850,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         // last read by chunk k - 1, which has finished. The dependency wait
         // sits inside the first chunk's preparation.
         bool waited = !(FUSED && p.pdl_mode == 2);
+        bool gated = !FUSED || p.gate == nullptr;
         if (p.pdl_mode == 2 && !FUSED) griddep_wait();
         ChunkCursor pcur;
         int prepared = 0;
@@ -840,6 +868,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                     if (!waited) {
                         griddep_wait();
                         waited = true;
+                    }
+                    if (!gated) {
+                        gate_wait(p.gate, &s_abort, p.status, lane);
+                        gated = true;
                     }
                     cp.finish(p, c, q_prep + qb * kHeadsPerCta * HD, nk_rows + qb * 2 * HD,
                               &q_full[qb], lane);
@@ -1269,6 +1301,18 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
                           : launch_decode<128>(prm, grid, k_pool, v_pool, s);
 }
 
+static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qkv,
+                                   int64_t row_stride, const int *positions,
+                                   const void *q_bias, const void *k_bias, const void *v_bias,
+                                   const float *cos_cache, const float *sin_cache,
+                                   int rope_rows, void *k_pool, void *v_pool,
+                                   int64_t num_blocks, int num_layers, int layer,
+                                   int num_q_heads, int num_kv_heads, int head_dim,
+                                   const int *block_tables, int table_stride, int batch,
+                                   int max_context_len, int partition_tokens, float sm_scale,
+                                   void *workspace, size_t workspace_bytes, int *dev_status,
+                                   lc_stream_t stream, const int *gate);
+
 extern "C" int lc_rope_append_decode(void *out, int64_t out_stride, const void *qkv,
                                      int64_t row_stride, const int *positions,
                                      const void *q_bias, const void *k_bias, const void *v_bias,
@@ -1280,6 +1324,42 @@ extern "C" int lc_rope_append_decode(void *out, int64_t out_stride, const void *
                                      int max_context_len, int partition_tokens, float sm_scale,
                                      void *workspace, size_t workspace_bytes, int *dev_status,
                                      lc_stream_t stream) {
+    return rope_append_decode_impl(out, out_stride, qkv, row_stride, positions, q_bias, k_bias,
+                                   v_bias, cos_cache, sin_cache, rope_rows, k_pool, v_pool,
+                                   num_blocks, num_layers, layer, num_q_heads, num_kv_heads,
+                                   head_dim, block_tables, table_stride, batch, max_context_len,
+                                   partition_tokens, sm_scale, workspace, workspace_bytes,
+                                   dev_status, stream, nullptr);
+}
+
+extern "C" int lc_rope_append_decode_gated(
+    void *out, int64_t out_stride, const void *qkv, int64_t row_stride, const int *positions,
+    const void *q_bias, const void *k_bias, const void *v_bias, const float *cos_cache,
+    const float *sin_cache, int rope_rows, void *k_pool, void *v_pool, int64_t num_blocks,
+    int num_layers, int layer, int num_q_heads, int num_kv_heads, int head_dim,
+    const int *block_tables, int table_stride, int batch, int max_context_len,
+    int partition_tokens, float sm_scale, void *workspace, size_t workspace_bytes,
+    int *dev_status, const int *gate, lc_stream_t stream) {
+    if (!gate) return LC_ERR_INVALID_ARGUMENT;
+    return rope_append_decode_impl(out, out_stride, qkv, row_stride, positions, q_bias, k_bias,
+                                   v_bias, cos_cache, sin_cache, rope_rows, k_pool, v_pool,
+                                   num_blocks, num_layers, layer, num_q_heads, num_kv_heads,
+                                   head_dim, block_tables, table_stride, batch, max_context_len,
+                                   partition_tokens, sm_scale, workspace, workspace_bytes,
+                                   dev_status, stream, gate);
+}
+
+static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qkv,
+                                     int64_t row_stride, const int *positions,
+                                     const void *q_bias, const void *k_bias, const void *v_bias,
+                                     const float *cos_cache, const float *sin_cache,
+                                     int rope_rows, void *k_pool, void *v_pool,
+                                     int64_t num_blocks, int num_layers, int layer,
+                                     int num_q_heads, int num_kv_heads, int head_dim,
+                                     const int *block_tables, int table_stride, int batch,
+                                     int max_context_len, int partition_tokens, float sm_scale,
+                                     void *workspace, size_t workspace_bytes, int *dev_status,
+                                     lc_stream_t stream, const int *gate) {
     if (!out || !qkv || !positions || !q_bias || !k_bias || !v_bias || !cos_cache ||
         !sin_cache || !k_pool || !v_pool || !block_tables)
         return LC_ERR_INVALID_ARGUMENT;
@@ -1346,6 +1426,7 @@ extern "C" int lc_rope_append_decode(void *out, int64_t out_stride, const void *
     prm.rope_rows = rope_rows;
     prm.k_pool_w = (bf16 *)k_pool;
     prm.v_pool_w = (bf16 *)v_pool;
+    prm.gate = gate;
     cudaStream_t s = as_stream(stream);
     return head_dim == 64 ? launch_decode<64, true>(prm, grid, k_pool, v_pool, s)
                           : launch_decode<128, true>(prm, grid, k_pool, v_pool, s);

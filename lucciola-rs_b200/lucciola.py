@@ -45,6 +45,10 @@ SIGNATURES = {
     "lc_rope_append_decode": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _i32,
                                      _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _i32,
                                      _i32, _i32, _i32, _f32, _vp, _sz, _vp, _vp]),
+    "lc_rope_append_decode_gated": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                                           _i32, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32,
+                                           _vp, _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp, _vp,
+                                           _vp]),
     "lc_paged_decode_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                       _i32, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32,
                                       _vp, _vp]),
@@ -103,6 +107,7 @@ SIGNATURES = {
     "lc_kv_pool_num_free_blocks": (_i64, [_vp]),
     "lc_kv_pool_sequence_pages": (_i32, [_vp, _i32, _pi32, _i32]),
     "lc_kv_pool_fingerprint": (C.c_uint64, [_vp]),
+    "lc_kv_pool_recover": (_i32, [_vp, _vp]),
     "lc_kv_pool_free": (None, [_vp]),
     "lc_shard_sequences": (_i32, [_pi32, _i32, _i32, _pi32]),
     "lc_shard_kv_heads": (_i32, [_i32, _i32, _i32, _i32, _pi32, _pi32]),
@@ -231,19 +236,24 @@ def paged_decode(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_he
 def rope_append_decode(out, qkv, positions, q_bias, k_bias, v_bias, cos, sin, k_pool, v_pool,
                        num_blocks, num_layers, layer, num_q_heads, num_kv_heads, head_dim,
                        block_tables, max_context_len=0, sm_scale=None, partition_tokens=0,
-                       workspace=None, dev_status=None, stream=None):
-    """One launch: bias + RoPE + append of each sequence's new token, then decode."""
+                       workspace=None, dev_status=None, stream=None, gate=None):
+    """One launch: bias + RoPE + append of each sequence's new token, then decode.
+    With `gate` (int32 device tensor) the qkv rows are read once it is non-zero."""
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(head_dim)
     batch = positions.shape[0]
-    check(lib.lc_rope_append_decode(_p(out), out.stride(0), _p(qkv), qkv.stride(0),
-                                    _p(positions), _p(q_bias), _p(k_bias), _p(v_bias), _p(cos),
-                                    _p(sin), cos.shape[0], _p(k_pool), _p(v_pool), num_blocks,
-                                    num_layers, layer, num_q_heads, num_kv_heads, head_dim,
-                                    _p(block_tables), block_tables.stride(0), batch,
-                                    max_context_len, partition_tokens, sm_scale, _p(workspace),
-                                    0 if workspace is None else workspace.numel() * workspace.element_size(),
-                                    _p(dev_status), _stream(stream)), "lc_rope_append_decode")
+    args = [_p(out), out.stride(0), _p(qkv), qkv.stride(0), _p(positions), _p(q_bias), _p(k_bias),
+            _p(v_bias), _p(cos), _p(sin), cos.shape[0], _p(k_pool), _p(v_pool), num_blocks,
+            num_layers, layer, num_q_heads, num_kv_heads, head_dim, _p(block_tables),
+            block_tables.stride(0), batch, max_context_len, partition_tokens, sm_scale,
+            _p(workspace),
+            0 if workspace is None else workspace.numel() * workspace.element_size(),
+            _p(dev_status)]
+    if gate is None:
+        check(lib.lc_rope_append_decode(*args, _stream(stream)), "lc_rope_append_decode")
+    else:
+        check(lib.lc_rope_append_decode_gated(*args, _p(gate), _stream(stream)),
+              "lc_rope_append_decode_gated")
 
 
 def paged_decode_static(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_heads,
@@ -574,6 +584,10 @@ class KVPool:
 
     def fingerprint(self):
         return lib.lc_kv_pool_fingerprint(self._h)
+
+    def recover(self, stream=None):
+        """Zero the split-K workspace after a step that reported LC_DEV_TIMEOUT."""
+        check(lib.lc_kv_pool_recover(self._h, _stream(stream)), "lc_kv_pool_recover")
 
     def close(self):
         if self._h:

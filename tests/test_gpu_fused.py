@@ -123,3 +123,98 @@ def test_dependent_launch_modes_give_identical_results(mode):
         got = run(mode, graph)
         for x, y in zip(base, got):
             assert torch.equal(x.view(torch.int16), y.view(torch.int16))
+
+
+def _gated_case(seed):
+    hq, hkv, hd, B = 14, 2, 64, 12
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(1, 2000, B).astype(np.int32)
+    case = make_case(B, hq, hkv, hd, ctx + 1, seed=seed)
+    row = (hq + 2 * hkv) * hd
+    d = dict(qkv=to_device(randn_bf16(rng, (B, row))), pos=to_device(ctx),
+             tables=to_device(case.tables), ws=L.alloc_decode_workspace(B, hq, hkv, hd))
+    d["qb"], d["kb"], d["vb"] = (to_device(randn_bf16(rng, (n * hd,))) for n in (hq, hkv, hkv))
+    d["cos"], d["sin"] = (to_device(x) for x in O.rope_table(4096, hd, 1e6))
+    return case, d, (hq, hkv, hd, B, int(ctx.max()) + 1)
+
+
+def _decode(case, d, shape, out, gate=None, status=None):
+    hq, hkv, hd, B, max_ctx = shape
+    kp, vp = to_device(case.k_pool), to_device(case.v_pool)
+    L.rope_append_decode(out, d["qkv"], d["pos"], d["qb"], d["kb"], d["vb"], d["cos"], d["sin"],
+                         kp, vp, case.num_blocks, case.num_layers, case.layer, hq, hkv, hd,
+                         d["tables"], max_ctx, workspace=d["ws"], dev_status=status, gate=gate)
+    return kp, vp
+
+
+def test_gated_decode_to_host_memory_equals_plain():
+    """lc_rope_append_decode_gated: an open gate and outputs written into mapped
+    pinned host memory give the plain launch's outputs and pools bit for bit."""
+    import ctypes
+    from cuda.bindings import runtime as cudart
+    case, d, shape = _gated_case(1)
+    hq, hkv, hd, B, _ = shape
+    out_a = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    ka, va = _decode(case, d, shape, out_a)
+    nbytes = B * hq * hd * 2
+    err, hptr = cudart.cudaHostAlloc(nbytes, cudart.cudaHostAllocMapped)
+    assert int(err) == 0
+    try:
+        out_h = torch.frombuffer((ctypes.c_uint8 * nbytes).from_address(int(hptr)),
+                                 dtype=torch.bfloat16).view(B, hq * hd)
+        gate = torch.ones(1, dtype=torch.int32, device="cuda")
+        st = torch.zeros(1, dtype=torch.int32, device="cuda")
+        kb_, vb_ = _decode(case, d, shape, out_h, gate=gate, status=st)
+        torch.cuda.synchronize()
+        assert int(st.item()) == 0
+        assert torch.equal(out_a.cpu().view(torch.int16), out_h.view(torch.int16))
+        assert torch.equal(ka.view(torch.int16), kb_.view(torch.int16))
+        assert torch.equal(va.view(torch.int16), vb_.view(torch.int16))
+    finally:
+        torch.cuda.synchronize()
+        cudart.cudaFreeHost(hptr)
+
+
+def test_gate_opened_late_by_a_copy():
+    """The launch waits on the device for a gate that a copy on another stream
+    opens later (issued by the host after a pause); same result as plain."""
+    import time
+    case, d, shape = _gated_case(2)
+    hq, hkv, hd, B, _ = shape
+    out_a = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    _decode(case, d, shape, out_a)
+    torch.cuda.synchronize()
+    gate = torch.zeros(1, dtype=torch.int32, device="cuda")
+    one = torch.ones(1, dtype=torch.int32).pin_memory()
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out_b = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    _decode(case, d, shape, out_b, gate=gate, status=st)
+    time.sleep(0.05)  # the launch is waiting on the device by now
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        gate.copy_(one, non_blocking=True)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert torch.equal(out_a.view(torch.int16), out_b.view(torch.int16))
+
+
+def test_gate_never_opened_times_out_with_status():
+    """A gate nothing opens: the bounded wait gives up (2 s), the launch
+    returns with LC_DEV_TIMEOUT in the status word, and the context stays
+    usable: after the workspace is zeroed again (the aborted launch may leave
+    arrival counters set) the next launches are exact."""
+    case, d, shape = _gated_case(3)
+    hq, hkv, hd, B, _ = shape
+    gate = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    _decode(case, d, shape, out, gate=gate, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) & L.LC_DEV_TIMEOUT
+    d["ws"].zero_()
+    out_a = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    out_c = torch.empty(B, hq * hd, dtype=torch.bfloat16, device="cuda")
+    _decode(case, d, shape, out_a)
+    _decode(case, d, shape, out_c, gate=torch.ones(1, dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    assert torch.equal(out_a.view(torch.int16), out_c.view(torch.int16))
