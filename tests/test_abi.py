@@ -100,6 +100,83 @@ def test_prefill_rejects_bad_arguments():
     assert rc in (2, 11)
 
 
+def test_proj_gemm_rejects_bad_arguments():
+    def call(**kw):
+        a = dict(out=FAKE, out_stride=1152, x=FAKE, x_stride=896, w=FAKE, w_stride=896, M=300,
+                 N=1152, K=896, res=None, res_stride=0)
+        a.update(kw)
+        return L.lib.lc_proj_gemm(a["out"], a["out_stride"], a["x"], a["x_stride"], a["w"],
+                                  a["w_stride"], a["M"], a["N"], a["K"], a["res"],
+                                  a["res_stride"], None)
+    assert call(out=None) == 1
+    assert call(N=40, out_stride=40) == 3        # N a multiple of the 32-column store box
+    assert call(K=900, x_stride=904, w_stride=904) == 3  # K a multiple of 8
+    assert call(M=-1) == 3
+    assert call(x_stride=800) == 1               # row shorter than K
+    assert call(out_stride=1000) == 1
+    assert call(x=FAKE + 8) == 5                 # TMA sources 16-byte aligned
+    assert call(w_stride=900) == 5
+    assert call(res=FAKE + 2, res_stride=1152) == 5
+    assert call(res=FAKE, res_stride=1000) == 1
+    assert call(M=0) == 0                        # nothing to do
+    assert call(M=0, res=FAKE, res_stride=1152) == 0
+
+
+def test_qkv_proj_rope_append_rejects_bad_arguments():
+    def call(**kw):
+        a = dict(qkv=FAKE, hd=64, hq=14, hkv=2, hidden=896, seqs=2, tps=8, layer=0, layers=2,
+                 q_bias=FAKE, rope_rows=4096)
+        a.update(kw)
+        n = (a["hq"] + 2 * a["hkv"]) * a["hd"]
+        return L.lib.lc_qkv_proj_rope_append(
+            a["qkv"], n, FAKE, a["hidden"], FAKE, a["hidden"], a["hidden"], a["seqs"], a["tps"],
+            FAKE, a["q_bias"], FAKE, FAKE, FAKE, FAKE, a["rope_rows"], FAKE, FAKE, 64,
+            a["layers"], a["layer"], a["hq"], a["hkv"], a["hd"], FAKE, 64, None, None)
+    assert call(hd=96) == 2
+    assert call(hkv=3) == 3
+    assert call(layer=2) == 1
+    assert call(tps=0) == 1
+    assert call(rope_rows=0) == 1
+    assert call(q_bias=None) == 1
+    assert call(q_bias=FAKE + 4) == 5
+    assert call(qkv=None) == 1
+    assert call(hidden=900) == 3
+    assert call(seqs=0) == 0
+
+
+def test_token_selection_rejects_bad_arguments():
+    V = 151936
+    assert L.lib.lc_argmax(None, V, V, 1, FAKE, None) == 1
+    assert L.lib.lc_argmax(FAKE, V - 1, V, 1, FAKE, None) == 1  # row shorter than vocab
+    assert L.lib.lc_argmax(FAKE, V, V, -1, FAKE, None) == 1
+    assert L.lib.lc_argmax(FAKE, V, V, 0, FAKE, None) == 0
+
+    # candidate counts: 32 * (top_k / 32), a power of two in 32 .. 1024
+    assert L.lib.lc_sample_workspace_size(4, 64) == 4 * 64 * 8
+    assert L.lib.lc_sample_workspace_size(4, 70) == 4 * 64 * 8
+    assert L.lib.lc_sample_workspace_size(2, 1024) == 2 * 1024 * 8
+    for bad in (0, 31, 96, 100, 2048):
+        assert L.lib.lc_sample_workspace_size(4, bad) == 0
+    assert L.lib.lc_sample_workspace_size(0, 64) == 0
+
+    def sample(vocab=V, batch=2, top_k=64, ws=FAKE, ws_bytes=2 * 64 * 8, top_p=FAKE):
+        return L.lib.lc_sample_top_p(FAKE, vocab, vocab, batch, top_k, top_p, FAKE, FAKE, ws,
+                                     ws_bytes, None)
+    assert sample(top_p=None) == 1
+    assert sample(top_k=96) == 3                 # no reference kernel for 96 candidates
+    assert sample(vocab=31) == 3
+    assert sample(ws_bytes=2 * 64 * 8 - 1) == 4
+    assert sample(ws=None) == 4
+    assert sample(batch=0, ws=None, ws_bytes=0) == 0
+
+
+def test_gated_decode_needs_a_gate():
+    rc = L.lib.lc_rope_append_decode_gated(
+        FAKE, 14 * 64, FAKE, 18 * 64, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 4096, FAKE, FAKE, 64, 2,
+        0, 14, 2, 64, FAKE, 64, 1, 1024, 0, 0.125, None, 0, None, None, None)
+    assert rc == 1
+
+
 def test_workspace_sizes():
     # host-only sizing assumes a 148-SM B200: 3 CTAs/SM at hd 64, 2 at hd 128
     segs = 64 * 2                      # batch x (kv heads x 8-head slices)
