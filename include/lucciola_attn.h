@@ -510,6 +510,74 @@ int lc_shard_sequences(const int *context_lens, int batch, int num_ranks,
 int lc_shard_kv_heads(int num_q_heads, int num_kv_heads, int num_ranks,
                       int rank, int *first_kv_head, int *num_local_kv_heads);
 
+/* ------------------------------------------------------------------------- */
+/* Peer exchange: KV-head-sharded decode that writes every rank's output.    */
+/* No counterpart in the reference (one GPU, src/models.rs:486-550).         */
+/* ------------------------------------------------------------------------- */
+
+/* Under KV-head sharding each rank computes the attention rows of its own q
+ * heads; the next operator (o_proj) wants all heads of every sequence. In
+ * place of an all-gather after the decode, lc_rope_append_decode_peer stores
+ * each finished output row into the same place of every rank's output buffer
+ * (NVLink peer stores from the decode's epilogue), and lc_peer_wait, on each
+ * rank, waits on the device until every peer's decode of the same layer has
+ * landed.
+ *
+ * Every rank allocates one exchange region of the same size
+ * (lc_peer_region_alloc): its first LC_PEER_SIGNAL_BYTES hold the signal
+ * words; output buffers are carved from the rest at the same offsets on every
+ * rank. The regions' IPC handles are exchanged by the caller (any host
+ * collective) and opened by lc_peer_group_open. One process per GPU; a group
+ * holds at most LC_PEER_MAX_RANKS ranks. */
+#define LC_PEER_MAX_RANKS 8
+#define LC_PEER_SIGNAL_BYTES 256
+#define LC_PEER_HANDLE_BYTES 64 /* sizeof(cudaIpcMemHandle_t) */
+
+typedef struct lc_peer_group lc_peer_group;
+
+/* Allocates and zeroes `bytes` (> LC_PEER_SIGNAL_BYTES) of device memory on the
+ * current device and writes its IPC handle (LC_PEER_HANDLE_BYTES) to
+ * handle_out. */
+int lc_peer_region_alloc(size_t bytes, void **region, void *handle_out);
+int lc_peer_region_free(void *region);
+
+/* Group of `world` ranks; `region` is this rank's, handles[r *
+ * LC_PEER_HANDLE_BYTES] rank r's (this rank's entry is not read). Opens every
+ * peer's region in this process (peer access over NVLink). */
+int lc_peer_group_open(int rank, int world, void *region, size_t region_bytes,
+                       const void *handles, lc_peer_group **out);
+/* The same over regions this process already addresses (regions[r] for rank r;
+ * several ranks driven from one process, e.g. on one GPU). */
+int lc_peer_group_local(int rank, int world, void *const *regions, size_t region_bytes,
+                        lc_peer_group **out);
+/* Closes the opened peer mappings; the regions stay allocated. */
+void lc_peer_group_destroy(lc_peer_group *g);
+
+/* lc_rope_append_decode whose output rows also land in every peer's region:
+ * `out` must lie in this rank's region past the signal words (rows up to
+ * batch-1 included), and is written at the same offset in each peer's region.
+ * After its last store the launch raises this rank's signal word in every
+ * peer's region (system-scope release); a batch of 0 still launches, so that it
+ * still signals. Launches and lc_peer_wait calls pair up in order: the k-th
+ * wait on a rank waits for the k-th peer decode launch of every other rank of
+ * the group. */
+int lc_rope_append_decode_peer(void *out, int64_t out_stride, const void *qkv,
+                               int64_t row_stride, const int *positions, const void *q_bias,
+                               const void *k_bias, const void *v_bias, const float *cos_cache,
+                               const float *sin_cache, int rope_rows, void *k_pool,
+                               void *v_pool, int64_t num_blocks, int num_layers, int layer,
+                               int num_q_heads, int num_kv_heads, int head_dim,
+                               const int *block_tables, int table_stride, int batch,
+                               int max_context_len, int partition_tokens, float sm_scale,
+                               void *workspace, size_t workspace_bytes, int *dev_status,
+                               const lc_peer_group *group, lc_stream_t stream);
+
+/* Waits on the device, in stream order after this rank's peer decode launch,
+ * until every other rank of the group has signalled the same launch count;
+ * launches after it on `stream` see all ranks' rows. A wait that exceeds 2 s
+ * sets LC_DEV_TIMEOUT in *dev_status (if given) and returns. */
+int lc_peer_wait(const lc_peer_group *group, int *dev_status, lc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,3 +47,21 @@ int sm_count();
 int dependent_launch_mode();
 
 }  // namespace lc
+
+// Peer exchange group (lc_peer_group_*): the ranks' exchange regions as this
+// process addresses them. Signal words at the head of every region (int32):
+// [0, 8) rank r's launch count, written by rank r into every peer's region;
+// kPeerDoneWord: CTAs of the running peer decode that have finished (local);
+// kPeerSeqWord: peer decode launches so far (local); kPeerWaitWord: waits so
+// far (local).
+struct lc_peer_group {
+    int rank, world;
+    size_t bytes;
+    uint8_t *region[LC_PEER_MAX_RANKS];
+    bool opened[LC_PEER_MAX_RANKS];  // mapped by lc_peer_group_open (closed on destroy)
+};
+
+namespace lc {
+constexpr int kPeerDoneWord = 16, kPeerSeqWord = 17, kPeerWaitWord = 18;
+static_assert((kPeerWaitWord + 1) * 4 <= LC_PEER_SIGNAL_BYTES, "signal words fit");
+}  // namespace lc

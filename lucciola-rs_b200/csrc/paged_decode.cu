@@ -47,6 +47,7 @@ constexpr int kEpilogueWarp = kConsumerWarps + 1;  // warp 5
 constexpr int kThreads = (kConsumerWarps + 2) * 32;
 constexpr int kHeadsPerCta = 8;
 constexpr int kPagesPerStage = kConsumerWarps;  // one page per consumer warp per stage
+constexpr int kMaxPeers = LC_PEER_MAX_RANKS - 1;
 constexpr int kMinPagesPerCta = 8;               // auto split: two stages per CTA at least
 
 // kFinal marks the last stage of the CTA's whole range.
@@ -116,6 +117,15 @@ struct DecodeParams {
     const float *cos_t, *sin_t;
     int rope_rows;
     bf16 *k_pool_w, *v_pool_w;
+    // Peer exchange (PEER kernels only): every output row is also stored at
+    // its address + peer_delta[r], r < n_peer (the same row of a peer's output
+    // buffer, mapped into this process). After its last store each CTA counts
+    // itself on peer_done; the grid's last CTA resets it, advances peer_seq and
+    // stores the new count into every peer_flag[r] (system-scope release).
+    int n_peer;
+    long long peer_delta[kMaxPeers];
+    int *peer_flag[kMaxPeers];
+    int *peer_done, *peer_seq;
 };
 
 // Shared-memory byte address of 16-byte chunk `kc` (of hd/8) of token row `r` in a
@@ -132,6 +142,41 @@ __device__ __forceinline__ float fast_exp2(float x) {
 
 __device__ __forceinline__ void fence_acq_rel_gpu() {
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+// An output element; PEER kernels store it into every peer's buffer as well.
+template <bool PEER>
+__device__ __forceinline__ void put_out(const DecodeParams &p, bf16 *a, bf16 v) {
+    *a = v;
+    if constexpr (PEER) {
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r)
+            if (r < p.n_peer)
+                *reinterpret_cast<bf16 *>(reinterpret_cast<char *>(a) + p.peer_delta[r]) = v;
+    }
+}
+
+// PEER kernels: one thread per CTA, once every output store of the CTA has
+// been fenced at system scope by the thread that made it and a barrier has
+// joined them. The wait for the preceding grid comes first, so that a CTA of
+// a launch that started early (programmatic dependent launch) never counts
+// while the previous launch's CTAs still do. The grid's last CTA publishes.
+__device__ __forceinline__ void peer_arrive(const DecodeParams &p) {
+    griddep_wait();
+    if (atomicAdd(p.peer_done, 1) != (int)gridDim.x - 1) return;
+    fence_acq_rel_sys();  // acquire side of the other CTAs' fence + count
+    *p.peer_done = 0;     // ready for the next launch
+    const int seq = *p.peer_seq + 1;
+    *p.peer_seq = seq;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+        if (r < p.n_peer)
+            asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p.peer_flag[r]), "r"(seq)
+                         : "memory");
 }
 
 __device__ __forceinline__ int atom_add_acquire_gpu(int *addr, int v) {
@@ -372,13 +417,13 @@ __device__ __forceinline__ void patch_new_row(const bf16 *nk, uint8_t *smem_gen,
 
 // Sequences without cached tokens own no pages: their output rows are zero.
 // CTA `first` of `count` zeroes sequences first, first + count, ...
-template <int HD>
+template <int HD, bool PEER>
 __device__ __forceinline__ void zero_empty_outputs(const DecodeParams &p, int first, int count,
                                                    int t, int nthreads) {
     for (int b = first; b < p.batch; b += count)
         if (seq_tokens(p, b, false) == 0)
             for (int i = t; i < p.num_q_heads * HD; i += nthreads)
-                p.out[(int64_t)b * p.out_stride + i] = __float2bfloat16(0.f);
+                put_out<PEER>(p, p.out + (int64_t)b * p.out_stride + i, __float2bfloat16(0.f));
 }
 
 // Owner CTA of global page x under the balanced split start(c) = c*T/C.
@@ -506,8 +551,9 @@ __host__ __device__ constexpr int kMergeRingSlots() {
 // sum runs from shared memory. Lane l owns float4 f = l + 32q (q < HD/16) of
 // the [8][HD] slot: head f / (HD/4), dims 4 * (f % (HD/4)) .. +3. Returns false
 // when a wait gave up (abort flag set; the copies in flight have landed).
-template <int HD>
-__device__ __forceinline__ bool merge_from_ring(bf16 *orow, int nh, const float *ws_o,
+template <int HD, bool PEER>
+__device__ __forceinline__ bool merge_from_ring(const DecodeParams &p, bf16 *orow, int nh,
+                                             const float *ws_o,
                                              const float *ws_lse, long long slot0, int nch,
                                              uint8_t *ring, uint64_t *bar, uint32_t phase,
                                              volatile int *abort_flag, int *status, int lane) {
@@ -592,12 +638,13 @@ __device__ __forceinline__ bool merge_from_ring(bf16 *orow, int nh, const float 
         if (h >= nh) continue;
         const float inv = 1.f / head_of_f4<HD>(S, q, lane);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) orow[h * HD + d + k] = __float2bfloat16(O[q][k] * inv);
+        for (int k = 0; k < 4; ++k)
+            put_out<PEER>(p, orow + h * HD + d + k, __float2bfloat16(O[q][k] * inv));
     }
     return true;
 }
 
-template <int HD, bool FUSED>
+template <int HD, bool FUSED, bool PEER = false>
 __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
@@ -672,7 +719,12 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     const long long T = s_total * G;
     if (T == 0) {  // every sequence is empty: zero outputs, nothing else
         if (p.pdl_mode == 2) griddep_wait();
-        zero_empty_outputs<HD>(p, blockIdx.x, gridDim.x, tid, kThreads);
+        zero_empty_outputs<HD, PEER>(p, blockIdx.x, gridDim.x, tid, kThreads);
+        if constexpr (PEER) {
+            fence_acq_rel_sys();
+            __syncthreads();
+            if (tid == 0) peer_arrive(p);
+        }
         return;
     }
     int C = gridDim.x;
@@ -686,10 +738,13 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         if (T < C) C = (int)T;
     }
     const int cta = blockIdx.x;
-    if (cta >= C) return;
     const long long start = (long long)cta * T / C;
     const long long end = (long long)(cta + 1) * T / C;
-    if (start >= end) return;
+    if (cta >= C || start >= end) {  // no pages: no outputs either
+        if constexpr (PEER)
+            if (tid == 0) peer_arrive(p);
+        return;
+    }
     // ---- 2. locate the sequence holding `start` -------------------------------
     {
         const long long lo = s_part[tid] * G;
@@ -882,7 +937,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                     waited = true;
                 }
             }
-            if (k == 0) zero_empty_outputs<HD>(p, cta, C, lane, 32);
+            if (k == 0) zero_empty_outputs<HD, PEER>(p, cta, C, lane, 32);
             if (!mbar_wait_bounded(&epi_full, k & 1, &s_abort, p.status)) break;
             const EpiInfo e = epi;
             if (e.done) break;
@@ -912,7 +967,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                     const float il = 1.f / Lh[h];
 #pragma unroll
                     for (int kk = 0; kk < KD; ++kk)
-                        orow[h * HD + kk * 32 + lane] = __float2bfloat16(O[h][kk] * il);
+                        put_out<PEER>(p, orow + h * HD + kk * 32 + lane,
+                                      __float2bfloat16(O[h][kk] * il));
                 }
                 if (e.final) break;  // the consumers' end-of-range message is not needed
                 continue;
@@ -954,13 +1010,19 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         for (int i = 0; i < 2; ++i) {
             if (i >= npend || s_abort) break;
             const PendingMerge &m = pend[i];
-            const bool ok = merge_from_ring<HD>(
-                p.out + (int64_t)m.b * p.out_stride + (int64_t)m.head0 * HD, m.nh, p.ws_o, p.ws_lse,
+            const bool ok = merge_from_ring<HD, PEER>(
+                p, p.out + (int64_t)m.b * p.out_stride + (int64_t)m.head0 * HD, m.nh, p.ws_o,
+                p.ws_lse,
                 (long long)m.seg + m.c_first, m.nch, smem_gen, &merge_bar, merge_phase, &s_abort,
                 p.status, lane);
             merge_phase += (m.nch + kMergeRingSlots<HD>() - 1) / kMergeRingSlots<HD>();
             if (!ok) break;
             if (lane == 0) p.ws_cnt[m.seg] = 0;  // ready for the next call
+        }
+        if constexpr (PEER) {
+            fence_acq_rel_sys();
+            __syncwarp();
+            if (lane == 0) peer_arrive(p);
         }
         return;
     }
@@ -1176,7 +1238,7 @@ int max_ctas_for_device() {
 
 int max_ctas(int hd) { return hd == 64 ? max_ctas_for_device<64>() : max_ctas_for_device<128>(); }
 
-template <int HD, bool FUSED = false>
+template <int HD, bool FUSED = false, bool PEER = false>
 int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const void *v_pool,
                   cudaStream_t stream) {
     CUtensorMap mk, mv;
@@ -1185,7 +1247,7 @@ int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const v
     rc = pool_tensor_map(v_pool, prm.pool_rows, HD, &mv);
     if (rc) return rc;
     const int smem = DecodeCfg<HD>::kSmemBytes;
-    rc = ensure_smem_attr((const void *)paged_decode_kernel<HD, FUSED>, smem);
+    rc = ensure_smem_attr((const void *)paged_decode_kernel<HD, FUSED, PEER>, smem);
     if (rc) return rc;
     const int mode = dependent_launch_mode();
     DecodeParams prm2 = prm;
@@ -1200,7 +1262,8 @@ int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const v
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = mode > 0 ? 1 : 0;
-    if (cudaLaunchKernelEx(&cfg, paged_decode_kernel<HD, FUSED>, mk, mv, prm2) != cudaSuccess) {
+    if (cudaLaunchKernelEx(&cfg, paged_decode_kernel<HD, FUSED, PEER>, mk, mv, prm2) !=
+        cudaSuccess) {
         cudaGetLastError();
         return LC_ERR_CUDA;
     }
@@ -1311,7 +1374,8 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
                                    const int *block_tables, int table_stride, int batch,
                                    int max_context_len, int partition_tokens, float sm_scale,
                                    void *workspace, size_t workspace_bytes, int *dev_status,
-                                   lc_stream_t stream, const int *gate);
+                                   lc_stream_t stream, const int *gate,
+                                   const lc_peer_group *group);
 
 extern "C" int lc_rope_append_decode(void *out, int64_t out_stride, const void *qkv,
                                      int64_t row_stride, const int *positions,
@@ -1329,7 +1393,7 @@ extern "C" int lc_rope_append_decode(void *out, int64_t out_stride, const void *
                                    num_blocks, num_layers, layer, num_q_heads, num_kv_heads,
                                    head_dim, block_tables, table_stride, batch, max_context_len,
                                    partition_tokens, sm_scale, workspace, workspace_bytes,
-                                   dev_status, stream, nullptr);
+                                   dev_status, stream, nullptr, nullptr);
 }
 
 extern "C" int lc_rope_append_decode_gated(
@@ -1346,7 +1410,24 @@ extern "C" int lc_rope_append_decode_gated(
                                    num_blocks, num_layers, layer, num_q_heads, num_kv_heads,
                                    head_dim, block_tables, table_stride, batch, max_context_len,
                                    partition_tokens, sm_scale, workspace, workspace_bytes,
-                                   dev_status, stream, gate);
+                                   dev_status, stream, gate, nullptr);
+}
+
+extern "C" int lc_rope_append_decode_peer(
+    void *out, int64_t out_stride, const void *qkv, int64_t row_stride, const int *positions,
+    const void *q_bias, const void *k_bias, const void *v_bias, const float *cos_cache,
+    const float *sin_cache, int rope_rows, void *k_pool, void *v_pool, int64_t num_blocks,
+    int num_layers, int layer, int num_q_heads, int num_kv_heads, int head_dim,
+    const int *block_tables, int table_stride, int batch, int max_context_len,
+    int partition_tokens, float sm_scale, void *workspace, size_t workspace_bytes,
+    int *dev_status, const lc_peer_group *group, lc_stream_t stream) {
+    if (!group) return LC_ERR_INVALID_ARGUMENT;
+    return rope_append_decode_impl(out, out_stride, qkv, row_stride, positions, q_bias, k_bias,
+                                   v_bias, cos_cache, sin_cache, rope_rows, k_pool, v_pool,
+                                   num_blocks, num_layers, layer, num_q_heads, num_kv_heads,
+                                   head_dim, block_tables, table_stride, batch, max_context_len,
+                                   partition_tokens, sm_scale, workspace, workspace_bytes,
+                                   dev_status, stream, nullptr, group);
 }
 
 static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qkv,
@@ -1359,7 +1440,8 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
                                      const int *block_tables, int table_stride, int batch,
                                      int max_context_len, int partition_tokens, float sm_scale,
                                      void *workspace, size_t workspace_bytes, int *dev_status,
-                                     lc_stream_t stream, const int *gate) {
+                                     lc_stream_t stream, const int *gate,
+                                     const lc_peer_group *group) {
     if (!out || !qkv || !positions || !q_bias || !k_bias || !v_bias || !cos_cache ||
         !sin_cache || !k_pool || !v_pool || !block_tables)
         return LC_ERR_INVALID_ARGUMENT;
@@ -1369,7 +1451,7 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
         partition_tokens < 0)
         return LC_ERR_INVALID_ARGUMENT;
     if (num_q_heads % num_kv_heads) return LC_ERR_UNSUPPORTED_SHAPE;
-    if (batch == 0) return LC_OK;
+    if (batch == 0 && !group) return LC_OK;  // a peer launch still signals its peers
     if (!aligned16(k_pool) || !aligned16(v_pool) || !aligned16(qkv) || (row_stride & 7) ||
         ((uintptr_t)out & 1))
         return LC_ERR_MISALIGNED;
@@ -1428,6 +1510,28 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
     prm.v_pool_w = (bf16 *)v_pool;
     prm.gate = gate;
     cudaStream_t s = as_stream(stream);
+    if (group) {
+        // out's rows must lie in this rank's region past the signal words; the
+        // same offsets address them in every peer's region.
+        const uint8_t *base = group->region[group->rank];
+        const uint8_t *lo = (const uint8_t *)out;
+        const int64_t rows = batch > 0 ? batch : 1;
+        const uint8_t *hi =
+            lo + ((rows - 1) * out_stride + (int64_t)num_q_heads * head_dim) * 2;
+        if (lo < base + LC_PEER_SIGNAL_BYTES || hi > base + group->bytes)
+            return LC_ERR_INVALID_ARGUMENT;
+        int *words = (int *)group->region[group->rank];
+        prm.peer_done = words + kPeerDoneWord;
+        prm.peer_seq = words + kPeerSeqWord;
+        for (int r = 0; r < group->world; ++r) {
+            if (r == group->rank) continue;
+            prm.peer_delta[prm.n_peer] = (long long)(group->region[r] - base);
+            prm.peer_flag[prm.n_peer] = (int *)group->region[r] + group->rank;
+            ++prm.n_peer;
+        }
+        return head_dim == 64 ? launch_decode<64, true, true>(prm, grid, k_pool, v_pool, s)
+                              : launch_decode<128, true, true>(prm, grid, k_pool, v_pool, s);
+    }
     return head_dim == 64 ? launch_decode<64, true>(prm, grid, k_pool, v_pool, s)
                           : launch_decode<128, true>(prm, grid, k_pool, v_pool, s);
 }

@@ -111,6 +111,16 @@ SIGNATURES = {
     "lc_kv_pool_free": (None, [_vp]),
     "lc_shard_sequences": (_i32, [_pi32, _i32, _i32, _pi32]),
     "lc_shard_kv_heads": (_i32, [_i32, _i32, _i32, _i32, _pi32, _pi32]),
+    "lc_peer_region_alloc": (_i32, [_sz, C.POINTER(_vp), _vp]),
+    "lc_peer_region_free": (_i32, [_vp]),
+    "lc_peer_group_open": (_i32, [_i32, _i32, _vp, _sz, _vp, C.POINTER(_vp)]),
+    "lc_peer_group_local": (_i32, [_i32, _i32, C.POINTER(_vp), _sz, C.POINTER(_vp)]),
+    "lc_peer_group_destroy": (None, [_vp]),
+    "lc_rope_append_decode_peer": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                                          _i32, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32,
+                                          _vp, _i32, _i32, _i32, _i32, _f32, _vp, _sz, _vp, _vp,
+                                          _vp]),
+    "lc_peer_wait": (_i32, [_vp, _vp, _vp]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():
@@ -236,9 +246,13 @@ def paged_decode(out, q, k_pool, v_pool, num_blocks, num_layers, layer, num_q_he
 def rope_append_decode(out, qkv, positions, q_bias, k_bias, v_bias, cos, sin, k_pool, v_pool,
                        num_blocks, num_layers, layer, num_q_heads, num_kv_heads, head_dim,
                        block_tables, max_context_len=0, sm_scale=None, partition_tokens=0,
-                       workspace=None, dev_status=None, stream=None, gate=None):
+                       workspace=None, dev_status=None, stream=None, gate=None,
+                       peer_group=None):
     """One launch: bias + RoPE + append of each sequence's new token, then decode.
-    With `gate` (int32 device tensor) the qkv rows are read once it is non-zero."""
+    With `gate` (int32 device tensor) the qkv rows are read once it is non-zero.
+    With `peer_group` (PeerGroup) the output rows also land in every peer's
+    region (out must be a view of this rank's region); pair it with
+    peer_group.wait()."""
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(head_dim)
     batch = positions.shape[0]
@@ -249,7 +263,12 @@ def rope_append_decode(out, qkv, positions, q_bias, k_bias, v_bias, cos, sin, k_
             _p(workspace),
             0 if workspace is None else workspace.numel() * workspace.element_size(),
             _p(dev_status)]
-    if gate is None:
+    if peer_group is not None:
+        if gate is not None:
+            raise ValueError("a peer decode takes no gate")
+        check(lib.lc_rope_append_decode_peer(*args, peer_group.handle, _stream(stream)),
+              "lc_rope_append_decode_peer")
+    elif gate is None:
         check(lib.lc_rope_append_decode(*args, _stream(stream)), "lc_rope_append_decode")
     else:
         check(lib.lc_rope_append_decode_gated(*args, _p(gate), _stream(stream)),
@@ -322,6 +341,90 @@ def shard_kv_heads(num_q_heads, num_kv_heads, num_ranks, rank):
     check(lib.lc_shard_kv_heads(num_q_heads, num_kv_heads, num_ranks, rank, C.byref(first),
                                 C.byref(count)), "lc_shard_kv_heads")
     return first.value, count.value
+
+
+PEER_MAX_RANKS = 8
+PEER_SIGNAL_BYTES = 256
+PEER_HANDLE_BYTES = 64
+
+
+class _DeviceSpan:
+    """__cuda_array_interface__ over library-owned device memory (keeps its
+    owner alive while a torch view exists)."""
+
+    def __init__(self, owner, ptr, shape, typestr):
+        self.owner = owner
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class PeerRegion:
+    """One rank's exchange region (lc_peer_region_alloc): LC_PEER_SIGNAL_BYTES
+    of signal words, then output buffers at offsets shared by every rank."""
+
+    def __init__(self, nbytes):
+        ptr = C.c_void_p()
+        h = (C.c_uint8 * PEER_HANDLE_BYTES)()
+        check(lib.lc_peer_region_alloc(nbytes, C.byref(ptr), h), "lc_peer_region_alloc")
+        self.ptr = ptr.value
+        self.nbytes = nbytes
+        self.handle = bytes(h)
+
+    def view(self, offset, shape, dtype):
+        """A torch tensor over [offset, offset + size) of the region (bf16,
+        int32 or uint8)."""
+        import torch
+        codes = {torch.bfloat16: ("<i2", 2), torch.int32: ("<i4", 4), torch.uint8: ("|u1", 1)}
+        typestr, size = codes[dtype]
+        n = math.prod(shape) * size
+        if offset < 0 or offset % size or offset + n > self.nbytes:
+            raise ValueError("view outside the region")
+        t = torch.as_tensor(_DeviceSpan(self, self.ptr + offset, shape, typestr), device="cuda")
+        return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
+
+    def signal_words(self):
+        import torch
+        return self.view(0, (PEER_SIGNAL_BYTES // 4,), torch.int32)
+
+    def close(self):
+        if self.ptr:
+            check(lib.lc_peer_region_free(self.ptr), "lc_peer_region_free")
+            self.ptr = None
+
+
+class PeerGroup:
+    """lc_peer_group: the group's regions as this process addresses them."""
+
+    def __init__(self, handle, rank, world):
+        self.handle, self.rank, self.world = handle, rank, world
+
+    @classmethod
+    def open(cls, rank, world, region, handles):
+        """`handles`: the ranks' PeerRegion.handle values, in rank order."""
+        buf = b"".join(handles)
+        if len(handles) != world or len(buf) != world * PEER_HANDLE_BYTES:
+            raise ValueError("one handle per rank")
+        g = C.c_void_p()
+        check(lib.lc_peer_group_open(rank, world, region.ptr, region.nbytes, buf, C.byref(g)),
+              "lc_peer_group_open")
+        return cls(g, rank, world)
+
+    @classmethod
+    def local(cls, rank, world, regions):
+        """Regions that this process already addresses (one process, several ranks)."""
+        arr = (C.c_void_p * world)(*[r.ptr for r in regions])
+        g = C.c_void_p()
+        check(lib.lc_peer_group_local(rank, world, arr, regions[0].nbytes, C.byref(g)),
+              "lc_peer_group_local")
+        return cls(g, rank, world)
+
+    def wait(self, dev_status=None, stream=None):
+        check(lib.lc_peer_wait(self.handle, _p(dev_status), _stream(stream)), "lc_peer_wait")
+
+    def close(self):
+        if self.handle:
+            lib.lc_peer_group_destroy(self.handle)
+            self.handle = None
 
 
 def assemble_head_shards(gathered, num_ranks):

@@ -177,6 +177,31 @@ def test_gated_decode_needs_a_gate():
     assert rc == 1
 
 
+def test_peer_exchange_rejects_bad_arguments():
+    region = C.c_void_p()
+    handle = (C.c_uint8 * L.PEER_HANDLE_BYTES)()
+    assert L.lib.lc_peer_region_alloc(L.PEER_SIGNAL_BYTES, C.byref(region), handle) == 1
+    g = C.c_void_p()
+    regs = (C.c_void_p * 2)(FAKE, FAKE + 4096)
+    assert L.lib.lc_peer_group_local(2, 2, regs, 4096, C.byref(g)) == 1   # rank outside
+    assert L.lib.lc_peer_group_local(0, 9, regs, 4096, C.byref(g)) == 1   # > 8 ranks
+    assert L.lib.lc_peer_group_local(0, 2, regs, 256, C.byref(g)) == 1    # signal words only
+    assert L.lib.lc_peer_group_open(0, 2, None, 4096, bytes(128), C.byref(g)) == 1
+    assert L.lib.lc_peer_wait(None, None, None) == 1
+    # a group over addresses this process holds: host bookkeeping only
+    assert L.lib.lc_peer_group_local(0, 2, regs, 4096, C.byref(g)) == 0
+
+    def call(out, batch, group=g):
+        return L.lib.lc_rope_append_decode_peer(
+            out, 14 * 64, FAKE, 18 * 64, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 4096, FAKE, FAKE,
+            64, 2, 0, 14, 2, 64, FAKE, 64, batch, 1024, 0, 0.125, FAKE, 1 << 30, None, group,
+            None)
+    assert call(FAKE, 2) == 1             # rows over the signal words
+    assert call(FAKE + 256, 3) == 1       # row 2 ends past the region's 4096 bytes
+    assert call(FAKE + 256, 2, None) == 1  # no group
+    L.lib.lc_peer_group_destroy(g)
+
+
 def test_workspace_sizes():
     # host-only sizing assumes a 148-SM B200: 3 CTAs/SM at hd 64, 2 at hd 128
     segs = 64 * 2                      # batch x (kv heads x 8-head slices)
