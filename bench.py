@@ -795,8 +795,11 @@ HEAD_SHARDED = {"c5": ("qwen2.5-72b decode sharded by kv head (BASELINE config 5
 def run_head_sharded(args, rank, world, local):
     """KV-head sharding: rank r owns kv heads [r*8/N, (r+1)*8/N) of every layer
     (identical block tables everywhere), runs the fused decode on its heads, and
-    an NCCL all-gather assembles [B][Hq][hd]. Two physical layers alternate;
-    tokens/s is extrapolated to the model's 80 layers (attention only)."""
+    [B][Hq][hd] is assembled on every rank either by an NCCL all-gather plus a
+    permute (--gather nccl) or by the decode itself, which stores each row into
+    every rank's exchange region, followed by a device-side wait for the peers
+    (--gather peer). Two physical layers alternate; tokens/s is extrapolated to
+    the model's 80 layers (attention only)."""
     import lucciola as L
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -840,17 +843,42 @@ def run_head_sharded(args, rank, world, local):
     kb = bias[:, hq_loc * hd:(hq_loc + nloc) * hd].contiguous()
     vb = bias[:, (hq_loc + nloc) * hd:].contiguous()
     cos, sin = (torch.from_numpy(x).to(device) for x in L.rope_table_host(32768 + 16, hd, 1e6))
-    out_loc = torch.empty((layers, B, hq_loc * hd), dtype=torch.bfloat16, device=device)
-    gathered = torch.empty((layers, world * B, hq_loc * hd), dtype=torch.bfloat16, device=device)
-    full = torch.empty((layers, B, hq * hd), dtype=torch.bfloat16, device=device)
     ws = L.alloc_decode_workspace(B, hq_loc, nloc, hd, device=device)
     max_ctx = int(ctx.max()) + 1
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    peer = args.gather == "peer"
+    region = group = None
+    if peer:
+        # One exchange region per rank: signal words, then the layers' [B][Hq][hd]
+        # outputs at the same offsets everywhere; this rank's heads start at
+        # column first * (hq / hkv) * hd.
+        region = L.PeerRegion(L.PEER_SIGNAL_BYTES + layers * B * hq * hd * 2)
+        handles = [region.handle]
+        if dist:
+            handles = [None] * world
+            dist.all_gather_object(handles, region.handle)
+        group = L.PeerGroup.open(rank, world, region, handles) if world > 1 else \
+            L.PeerGroup.local(0, 1, [region])
+        full = region.view(L.PEER_SIGNAL_BYTES, (layers, B, hq * hd), torch.bfloat16)
+        col0 = first * (hq // hkv) * hd
+    else:
+        out_loc = torch.empty((layers, B, hq_loc * hd), dtype=torch.bfloat16, device=device)
+        gathered = torch.empty((layers, world * B, hq_loc * hd), dtype=torch.bfloat16,
+                               device=device)
+        full = torch.empty((layers, B, hq * hd), dtype=torch.bfloat16, device=device)
 
     def step():
         for l in range(layers):
+            if peer:
+                L.rope_append_decode(full[l][:, col0:col0 + hq_loc * hd], qkv[l], positions,
+                                     qb[l], kb[l], vb[l], cos, sin, k_pool, v_pool, nb, layers, l,
+                                     hq_loc, nloc, hd, tables, max_ctx, workspace=ws,
+                                     dev_status=status, peer_group=group)
+                group.wait(dev_status=status)
+                continue
             L.rope_append_decode(out_loc[l], qkv[l], positions, qb[l], kb[l], vb[l], cos, sin,
                                  k_pool, v_pool, nb, layers, l, hq_loc, nloc, hd, tables, max_ctx,
-                                 workspace=ws)
+                                 workspace=ws, dev_status=status)
             if dist:
                 dist.all_gather_into_tensor(gathered[l], out_loc[l])
                 full[l].copy_(L.assemble_head_shards(gathered[l], world))
@@ -888,6 +916,10 @@ def run_head_sharded(args, rank, world, local):
         dist.barrier()
     clocks = sampler.stop() if sampler else None
     kv_bytes_rank = float((ctx.astype(np.int64) + 1).sum()) * nloc * hd * 2 * 2 * layers
+    dev_word = torch.tensor([int(status.item())], dtype=torch.int32, device=device)
+    if dist:
+        dist.all_reduce(dev_word, op=dist.ReduceOp.MAX)
+    dev_word = int(dev_word.item())
     vals = torch.tensor([ms_step, kv_bytes_rank], dtype=torch.float64, device=device)
     if dist:
         mx = vals[:1].clone()
@@ -911,14 +943,27 @@ def run_head_sharded(args, rank, world, local):
             "config": {"workload": label, "batch": B, "q_heads": hq, "kv_heads": hkv,
                        "head_dim": hd, "kv_heads_per_gpu": nloc, "physical_layers": layers,
                        "kv_tokens": int(ctx.sum() + B),
-                       "parallelism": f"kv-head sharded x{world}, NCCL all-gather of outputs",
-                       "step": "per layer: lc_rope_append_decode on local heads, "
+                       "parallelism": f"kv-head sharded x{world}, " + (
+                           "outputs stored into every rank by the decode (NVLink peer stores)"
+                           if peer else "NCCL all-gather of outputs"),
+                       "step": "per layer: lc_rope_append_decode_peer on local heads writing "
+                               "[B][Hq][hd] on every rank, lc_peer_wait" if peer else
+                               "per layer: lc_rope_append_decode on local heads, "
                                "all_gather_into_tensor, permute to [B][Hq][hd]"},
             "ms_per_layer": round(t_layer, 4),
             "tokens_per_s_80_layers": round(B / (model_layers * t_layer * 1e-3), 1),
             "pct_hbm_per_gpu": round(100 * value / world / peak, 2),
+            "device_status": dev_word,
             "clocks": clocks,
         }), flush=True)
+    if group is not None:
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()  # every rank is done with the peers' regions
+        group.close()
+        if dist:
+            dist.barrier()
+        region.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -1232,6 +1277,10 @@ def main():
                          "driver (lc_kv_pool) with positions advancing every step")
     ap.add_argument("--partition", type=int, default=None,
                     help="override the split-K partition size in tokens (0 = auto)")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="nccl",
+                    help="config 5: assemble all heads by peer stores from the decode "
+                         "(lc_rope_append_decode_peer + lc_peer_wait) or by an NCCL "
+                         "all-gather after it")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

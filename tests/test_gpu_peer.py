@@ -1,0 +1,232 @@
+"""KV-head-sharded decode with the peer exchange (lc_rope_append_decode_peer +
+lc_peer_wait) against the same shards decoded by lc_rope_append_decode into one
+buffer: every rank's region must hold all heads' rows, bit for bit, and the
+pools the same appended rows.
+
+On one GPU two ranks are emulated by one process (lc_peer_group_local over two
+regions of this device): each launch's signal is complete before the wait
+that reads it is queued, so nothing waits on a kernel running beside it. With
+two GPUs two processes exchange IPC handles and run the real NVLink path.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import lucciola as L
+from workloads import from_device, make_case, randn_bf16, to_device
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+HQ, HKV, HD = 16, 4, 128
+CTX = np.array([0, 15, 300, 2000, 4095, 17, 1023], np.int32)
+
+
+def _inputs(world, seed=11):
+    """Full case plus each rank's slices (pools of its kv heads, qkv rows of
+    its q/k/v heads, biases)."""
+    rng = np.random.default_rng(seed)
+    B = len(CTX)
+    case = make_case(B, HQ, HKV, HD, CTX + 1, seed=seed)
+    qkv = randn_bf16(rng, (B, (HQ + 2 * HKV) * HD))
+    qb, kb, vb = (randn_bf16(rng, (n * HD,)) for n in (HQ, HKV, HKV))
+    cos, sin = L.rope_table_host(int(CTX.max()) + 8, HD, 1e6)
+    g = HQ // HKV
+    shards = []
+    for r in range(world):
+        f, n = L.shard_kv_heads(HQ, HKV, world, r)
+        q_cols = slice(f * g * HD, (f + n) * g * HD)
+        k_cols = slice((HQ + f) * HD, (HQ + f + n) * HD)
+        v_cols = slice((HQ + HKV + f) * HD, (HQ + HKV + f + n) * HD)
+        shards.append({
+            "first": f, "n": n, "q_cols": q_cols,
+            "qkv": np.ascontiguousarray(np.concatenate(
+                [qkv[:, q_cols], qkv[:, k_cols], qkv[:, v_cols]], axis=1)),
+            "k_pool": np.ascontiguousarray(case.k_pool[:, :, f:f + n]),
+            "v_pool": np.ascontiguousarray(case.v_pool[:, :, f:f + n]),
+            "bias": (qb[q_cols], kb[f * HD:(f + n) * HD], vb[f * HD:(f + n) * HD]),
+        })
+    return case, (cos, sin), shards
+
+
+class _Rank:
+    """Device copies of one rank's shard."""
+
+    def __init__(self, case, rope, sh):
+        self.sh = sh
+        self.n = sh["n"]
+        self.qkv = to_device(sh["qkv"])
+        self.k, self.v = to_device(sh["k_pool"]), to_device(sh["v_pool"])
+        self.bias = [to_device(b) for b in sh["bias"]]
+        self.rope = [to_device(x) for x in rope]
+        self.pos, self.tables = to_device(CTX), to_device(case.tables)
+        self.ws = L.alloc_decode_workspace(len(CTX), self.n * HQ // HKV, self.n, HD)
+        self.status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.case = case
+
+    def decode(self, out_full, layer, group=None):
+        out = out_full[:, self.sh["q_cols"]]
+        L.rope_append_decode(out, self.qkv, self.pos, *self.bias, *self.rope, self.k, self.v,
+                             self.case.num_blocks, self.case.num_layers, layer,
+                             self.n * HQ // HKV, self.n, HD, self.tables,
+                             int(CTX.max()) + 1, workspace=self.ws, dev_status=self.status,
+                             peer_group=group)
+
+
+def _region_bytes(slots):
+    return L.PEER_SIGNAL_BYTES + slots * len(CTX) * HQ * HD * 2
+
+
+def _slot(region, s):
+    off = L.PEER_SIGNAL_BYTES + s * len(CTX) * HQ * HD * 2
+    return region.view(off, (len(CTX), HQ * HD), torch.bfloat16)
+
+
+@pytest.mark.parametrize("pdl", [0, 2])
+def test_peer_decode_two_ranks_on_one_gpu(pdl):
+    world = 2
+    case, rope, shards = _inputs(world)
+    old = L.set_dependent_launch(pdl)
+    try:
+        ref_ranks = [_Rank(case, rope, sh) for sh in shards]
+        peer_ranks = [_Rank(case, rope, sh) for sh in shards]
+        regions = [L.PeerRegion(_region_bytes(2)) for _ in range(world)]
+        groups = [L.PeerGroup.local(r, world, regions) for r in range(world)]
+        try:
+            for it, layer in enumerate((1, 0, 1)):
+                ref = torch.full((len(CTX), HQ * HD), float("nan"), dtype=torch.bfloat16,
+                                 device="cuda")
+                for rk in ref_ranks:
+                    rk.decode(ref, layer)
+                for rk, g in zip(peer_ranks, groups):
+                    rk.decode(_slot(regions[g.rank], it % 2), layer, group=g)
+                for rk, g in zip(peer_ranks, groups):
+                    g.wait(dev_status=rk.status)
+                torch.cuda.synchronize()
+                for reg in regions:
+                    assert torch.equal(_slot(reg, it % 2).view(torch.int16),
+                                       ref.view(torch.int16)), f"iteration {it}"
+                for a, b in zip(ref_ranks, peer_ranks):
+                    assert torch.equal(a.k.view(torch.int16), b.k.view(torch.int16))
+                    assert torch.equal(a.v.view(torch.int16), b.v.view(torch.int16))
+                    assert int(a.status.item()) == 0 and int(b.status.item()) == 0
+                for r, reg in enumerate(regions):
+                    w = from_device(reg.signal_words())
+                    assert w[1 - r] == it + 1 and w[r] == 0      # the peer's launch count
+                    assert w[16] == 0 and w[17] == it + 1 and w[18] == it + 1
+        finally:
+            for g in groups:
+                g.close()
+            torch.cuda.synchronize()
+            for reg in regions:
+                reg.close()
+    finally:
+        L.set_dependent_launch(old)
+
+
+def test_peer_decode_batch_of_zero_still_signals():
+    case, rope, shards = _inputs(1)
+    rk = _Rank(case, rope, shards[0])
+    region = L.PeerRegion(_region_bytes(1))
+    group = L.PeerGroup.local(0, 1, [region])
+    try:
+        out = _slot(region, 0)
+        L.rope_append_decode(out, rk.qkv, rk.pos[:0], *rk.bias, *rk.rope, rk.k, rk.v,
+                             case.num_blocks, case.num_layers, 1, HQ, HKV, HD, rk.tables, 0,
+                             workspace=rk.ws, dev_status=rk.status, peer_group=group)
+        group.wait(dev_status=rk.status)
+        torch.cuda.synchronize()
+        w = from_device(region.signal_words())
+        assert w[16] == 0 and w[17] == 1 and w[18] == 1 and int(rk.status.item()) == 0
+    finally:
+        group.close()
+        torch.cuda.synchronize()
+        region.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _two_gpu_worker(rank, port, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / "lucciola-rs_b200"), str(root / "tests")]
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=60))
+    ok, msg = False, ""
+    try:
+        import lucciola as L
+        world = 2
+        case, rope, shards = _inputs(world)
+        ref_rank, peer_rank = _Rank(case, rope, shards[rank]), _Rank(case, rope, shards[rank])
+        region = L.PeerRegion(_region_bytes(2))
+        handles = [None] * world
+        dist.all_gather_object(handles, region.handle)
+        group = L.PeerGroup.open(rank, world, region, handles)
+        L.set_dependent_launch(2)
+        try:
+            for it, layer in enumerate((1, 0, 1, 0)):
+                ref = torch.zeros((len(CTX), HQ * HD), dtype=torch.bfloat16, device="cuda")
+                ref_rank.decode(ref, layer)
+                torch.cuda.synchronize()
+                dist.barrier()  # both ranks launch their peer decode together
+                peer_rank.decode(_slot(region, it % 2), layer, group=group)
+                group.wait(dev_status=peer_rank.status)
+                torch.cuda.synchronize()
+                # all ranks' reference shards, assembled on the host
+                mine = from_device(ref[:, shards[rank]["q_cols"]])
+                parts = [None] * world
+                dist.all_gather_object(parts, mine)
+                full = np.concatenate(parts, axis=1)
+                got = from_device(_slot(region, it % 2))
+                if not np.array_equal(got, full):
+                    msg = f"iteration {it}: {int((got != full).sum())} elements differ"
+                elif int(peer_rank.status.item()) != 0:
+                    msg = f"iteration {it}: status {int(peer_rank.status.item())}"
+                verdicts = [None] * world
+                dist.all_gather_object(verdicts, msg)  # every rank stops at the same point
+                if any(verdicts):
+                    msg = msg or "a peer failed"
+                    break
+            else:
+                ok = True
+        finally:
+            torch.cuda.synchronize()
+            dist.barrier()
+            group.close()
+            dist.barrier()
+            region.close()
+    finally:
+        dist.destroy_process_group()
+    q.put((rank, ok, msg))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_peer_decode_two_processes_over_nvlink():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_two_gpu_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    results = sorted(q.get() for _ in range(2))
+    assert all(ok for _, ok, _ in results), results
