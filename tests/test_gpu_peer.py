@@ -134,9 +134,14 @@ def test_peer_decode_batch_of_zero_still_signals():
     group = L.PeerGroup.local(0, 1, [region])
     try:
         out = _slot(region, 0)
-        L.rope_append_decode(out, rk.qkv, rk.pos[:0], *rk.bias, *rk.rope, rk.k, rk.v,
-                             case.num_blocks, case.num_layers, 1, HQ, HKV, HD, rk.tables, 0,
-                             workspace=rk.ws, dev_status=rk.status, peer_group=group)
+        p = lambda t: t.data_ptr()  # noqa: E731  (an empty torch slice has a null pointer)
+        rc = L.lib.lc_rope_append_decode_peer(
+            p(out), out.stride(0), p(rk.qkv), rk.qkv.stride(0), p(rk.pos), *map(p, rk.bias),
+            *map(p, rk.rope), rk.rope[0].shape[0], p(rk.k), p(rk.v), case.num_blocks,
+            case.num_layers, 1, HQ, HKV, HD, p(rk.tables), rk.tables.stride(0), 0, 0, 0,
+            1.0 / HD ** 0.5, p(rk.ws), rk.ws.numel() * rk.ws.element_size(), p(rk.status),
+            group.handle, torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
         group.wait(dev_status=rk.status)
         torch.cuda.synchronize()
         w = from_device(region.signal_words())
