@@ -7,10 +7,12 @@ Default workload: BASELINE config 2 (Qwen2.5-0.5B shape batched ragged decode:
 64 sequences per GPU, 14 q heads / 2 KV heads, head_dim 64, context lengths
 U[256, 4096], 16-token pages from a shuffled shared pool, 512-token split-K
 partitions, 24 layers). One step = one decode step of all 24 layers: per layer
-the fused bias+RoPE+KV append of the new token (lc_rope_append) and paged
-attention over the cache (lc_paged_decode). Multi-GPU: weak scaling, the
-global batch of 64*N sequences is sharded by sequence (longest-first bin
-packing, lc_shard_sequences); no collective on the data path.
+ONE launch, lc_rope_append_decode, which adds the biases to the new token's
+q/k/v, rotates q and k, appends k and v to the paged cache and runs the paged
+attention over the cache (the two-launch form, lc_rope_append then
+lc_paged_decode, is `--unfused`). Multi-GPU: weak scaling, the global batch of
+64*N sequences is sharded by sequence (longest-first bin packing,
+lc_shard_sequences); no collective on the data path.
 
 `value` is decode-attention KV GB/s summed over ranks (each unique KV byte
 counted once per layer), inputs resident in HBM, timed with CUDA events over K
@@ -21,7 +23,9 @@ outputs copied back inside the timed region. The 24 per-layer caches total
 
 `--impl reference` runs the reference's own kernels (compiled unchanged from
 its sources into oracle/_ref) the way the reference launches them: per
-sequence, rope -> update_kv_cache -> flash_decoding, one launch each.
+sequence, rope -> update_kv_cache -> flash_decoding, one launch each. It loads
+only oracle/_ref (its RoPE tables come from that library's host code) and, on
+N ranks, rank 0 runs the whole global batch on its GPU.
 """
 from __future__ import annotations
 
@@ -129,7 +133,11 @@ class Workload:
     """Synthetic paged decode batch for one rank, resident on the GPU."""
 
     def __init__(self, cfg_name: str, rank: int, world: int, device, seed: int = 1234,
-                 layers: int | None = None):
+                 layers: int | None = None, rope_table=None, shard: bool = True):
+        """`rope_table(max_pos, head_dim, base) -> (cos, sin)` builds the RoPE
+        tables (the product library's by default). With shard=False this
+        process takes the whole global batch of batch_per_rank * world
+        sequences (the reference arm, which runs on one GPU)."""
         (self.label, self.batch_per_rank, self.hq, self.hkv, self.hd, self.layers, ctx_spec,
          self.ptok) = CONFIGS[cfg_name]
         if layers:
@@ -141,11 +149,12 @@ class Workload:
             ctx_all = np.full(global_batch, ctx_spec[1], np.int32)
         else:
             ctx_all = rng.integers(ctx_spec[1], ctx_spec[2] + 1, global_batch).astype(np.int32)
-        if world > 1:
+        if world > 1 and shard:
             import lucciola as L
             owner = np.array(L.shard_sequences(ctx_all.tolist(), world))
         else:
             owner = np.zeros(global_batch, np.int64)
+            rank = 0
         self.global_batch = global_batch
         self.global_kv_tokens = int(ctx_all.sum() + global_batch)
         self.ctx = ctx_all[owner == rank].astype(np.int32)  # cached tokens before this step
@@ -186,8 +195,10 @@ class Workload:
         self.k_bias = bias[:, hq * hd:(hq + hkv) * hd].to(torch.bfloat16).contiguous()
         self.v_bias = bias[:, (hq + hkv) * hd:].to(torch.bfloat16).contiguous()
         self.out = torch.empty((L_, self.batch, hq * hd), dtype=torch.bfloat16, device=device)
-        import lucciola as L
-        cos, sin = L.rope_table_host(32768, hd, 1e6)
+        if rope_table is None:
+            import lucciola as L
+            rope_table = L.rope_table_host
+        cos, sin = rope_table(32768, hd, 1e6)
         self.cos = torch.from_numpy(cos).to(device)
         self.sin = torch.from_numpy(sin).to(device)
         # bytes: each unique KV byte of the attended context, once per layer
@@ -195,6 +206,19 @@ class Workload:
         self.kv_bytes_per_step = self.kv_bytes_per_layer * L_
         self.h2d_bytes = self.qkv.numel() * 2 + self.positions.numel() * 4
         self.d2h_bytes = self.out.numel() * 2
+
+
+def workload_config(w: Workload, world: int) -> dict:
+    """The `config` object of both arms' JSON lines (the workload, not the
+    implementation; each line's `step` key says how it was run)."""
+    return {"workload": w.label, "batch_per_gpu": w.batch_per_rank,
+            "global_batch": w.global_batch, "q_heads": w.hq, "kv_heads": w.hkv,
+            "head_dim": w.hd, "layers": w.layers, "page_tokens": 16,
+            "partition_tokens": w.ptok or "auto",
+            "kv_tokens_per_layer": w.global_kv_tokens,
+            "parallelism": f"sequence-sharded x{world}",
+            "l2": "no flush: %d per-layer caches, ~%.1f GB per GPU > 126 MB L2" %
+                  (w.layers, w.global_kv_tokens * w.hkv * w.hd * 4 * w.layers / world / 1e9)}
 
 
 # ------------------------------------------------------------------ our arm --
@@ -496,18 +520,11 @@ def run_ours(args, rank, world, local):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded bf16 ~N(0,1) K/V/Q, uniform context lengths)",
-            "config": {"workload": w.label, "batch_per_gpu": w.batch_per_rank,
-                       "global_batch": w.global_batch, "q_heads": w.hq, "kv_heads": w.hkv,
-                       "head_dim": w.hd, "layers": w.layers, "page_tokens": 16,
-                       "partition_tokens": w.ptok or "auto",
-                       "kv_tokens_per_layer": w.global_kv_tokens,
-                       "parallelism": f"sequence-sharded x{world}",
-                       "l2": "no flush: 24 per-layer caches, ~%.1f GB per GPU > 126 MB L2" %
-                             (w.kv_bytes_per_step / 1e9),
-                       "step": ("per layer: lc_rope_append + lc_paged_decode" if args.unfused else
-                                "per layer: lc_rope_append_decode (fused bias+RoPE+append+"
-                                "attention)") + "; CUDA graph" +
-                               (f"; programmatic dependent launch mode {args.pdl}" if args.pdl else "")},
+            "config": workload_config(w, world),
+            "step": ("per layer: lc_rope_append + lc_paged_decode" if args.unfused else
+                     "per layer: lc_rope_append_decode (fused bias+RoPE+append+attention)") +
+                    "; CUDA graph" +
+                    (f"; programmatic dependent launch mode {args.pdl}" if args.pdl else ""),
             "tokens_per_s": round(w.global_batch / (ms_step * 1e-3), 1),
             "pct_hbm": round(100 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -709,7 +726,12 @@ def run_reference(args, rank, world, local):
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    w = Workload(args.config, 0, 1, device)
+    # The reference has one GPU path: rank 0 runs the whole global batch (the
+    # same sequences the repo arm shards over `world` ranks). Its RoPE tables
+    # come from the reference library's host restatement of RopeCache::new, so
+    # this process loads nothing of the product.
+    w = Workload(args.config, 0, world, device, layers=args.layers, rope_table=O.ref_rope_table,
+                 shard=False)
     host_pos = (C.c_int * w.batch)(*w.positions_np.tolist())
     P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
 
@@ -756,24 +778,26 @@ def run_reference(args, rank, world, local):
     value = w.kv_bytes_per_step / (ms_step * 1e-3) / 1e9
     e2e_value = w.kv_bytes_per_step / (e2e_ms * 1e-3) / 1e9
     peak, _ = measured_peak()
+    cfg = workload_config(w, world)
+    if world > 1:
+        cfg["parallelism"] = (f"none: the reference has no multi-GPU path; one GPU ran the "
+                              f"global batch that the repo arm shards over {world}")
     line = {
         "impl": "reference",
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded bf16 ~N(0,1) K/V/Q, uniform context lengths)",
-        "config": {"workload": w.label, "batch_per_gpu": w.batch_per_rank,
-                   "global_batch": w.batch, "q_heads": w.hq, "kv_heads": w.hkv,
-                   "head_dim": w.hd, "layers": w.layers,
-                   "path": "reference kernels rope.cu/kv_cache.cu/attention.cu compiled "
-                           "unchanged for sm_100a, launched per sequence as src/kernels.rs and "
-                           "src/layers/kv_cache.rs do"},
+        "config": cfg,
+        "step": "per layer and sequence: the reference kernels rope -> update_kv_cache_kernel "
+                "-> flash_decoding_kernel (rope.cu/kv_cache.cu/attention.cu compiled unchanged "
+                "for sm_100a), launched as src/kernels.rs and src/layers/kv_cache.rs do",
         "tokens_per_s": round(w.batch / (ms_step * 1e-3), 1),
         "pct_hbm": round(100 * value / peak, 3),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": 1,
                          "kind": "reference",
                          "sample": "the reference's implementation of this path is CUDA only; "
-                                   "this arm runs its kernels on the B200 from one host thread, "
+                                   "this arm runs its kernels on one B200 from one host thread, "
                                    "full workload"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

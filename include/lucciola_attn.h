@@ -543,11 +543,15 @@ int lc_peer_region_free(void *region);
 
 /* Group of `world` ranks; `region` is this rank's, handles[r *
  * LC_PEER_HANDLE_BYTES] rank r's (this rank's entry is not read). Opens every
- * peer's region in this process (peer access over NVLink). */
+ * peer's region in this process (peer access over NVLink). Every region,
+ * this rank's and each opened peer's, must hold at least region_bytes from its
+ * start (checked against the allocation's extent); otherwise nothing stays
+ * open and LC_ERR_INVALID_ARGUMENT is returned. */
 int lc_peer_group_open(int rank, int world, void *region, size_t region_bytes,
                        const void *handles, lc_peer_group **out);
 /* The same over regions this process already addresses (regions[r] for rank r;
- * several ranks driven from one process, e.g. on one GPU). */
+ * several ranks driven from one process, e.g. on one GPU), each checked for
+ * region_bytes of room in the same way. */
 int lc_peer_group_local(int rank, int world, void *const *regions, size_t region_bytes,
                         lc_peer_group **out);
 /* Closes the opened peer mappings; the regions stay allocated. */

@@ -8,6 +8,7 @@
 // word in every peer's region; lc_peer_wait polls the peers' words in this
 // rank's region. Only plain loads and stores cross NVLink: no TMA and no
 // multicast object touch peer memory.
+#include <stdint.h>
 #include <string.h>
 
 #include <new>
@@ -71,6 +72,34 @@ int make_group(int rank, int world, uint8_t *const *regions, const bool *opened,
     return LC_OK;
 }
 
+// Bytes from `p` to the end of the device allocation that holds it
+// (cuMemGetAddressRange, through the runtime's driver entry point); 0 when the
+// driver knows no allocation there; SIZE_MAX when there is no driver to ask
+// (then no kernel can run either, so no store can overrun). Every region of a
+// group must have room for region_bytes: the decode writes the same offsets
+// into every peer's region.
+size_t room_after(const void *p) {
+    using RangeFn = CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr);
+    static RangeFn fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            f = nullptr;
+        }
+        return reinterpret_cast<RangeFn>(f);
+    }();
+    if (!p) return 0;
+    if (!fn) return SIZE_MAX;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (fn(&base, &size, (CUdeviceptr)(uintptr_t)p) != CUDA_SUCCESS) return 0;
+    const size_t off = (size_t)((uintptr_t)p - (uintptr_t)base);
+    return off < size ? size - off : 0;
+}
+
 bool group_args_ok(int rank, int world, size_t bytes, lc_peer_group **out) {
     return out && world >= 1 && world <= LC_PEER_MAX_RANKS && rank >= 0 && rank < world &&
            bytes > LC_PEER_SIGNAL_BYTES;
@@ -110,6 +139,7 @@ extern "C" int lc_peer_group_open(int rank, int world, void *region, size_t regi
     if (!group_args_ok(rank, world, region_bytes, out) || !region || !handles)
         return LC_ERR_INVALID_ARGUMENT;
     *out = nullptr;
+    if (room_after(region) < region_bytes) return LC_ERR_INVALID_ARGUMENT;
     uint8_t *regions[LC_PEER_MAX_RANKS] = {};
     bool opened[LC_PEER_MAX_RANKS] = {};
     int rc = LC_OK;
@@ -128,6 +158,10 @@ extern "C" int lc_peer_group_open(int rank, int world, void *region, size_t regi
         }
         regions[r] = (uint8_t *)p;
         opened[r] = true;
+        if (room_after(p) < region_bytes) {  // a peer allocated a smaller region
+            rc = LC_ERR_INVALID_ARGUMENT;
+            break;
+        }
     }
     if (rc == LC_OK) rc = make_group(rank, world, regions, opened, region_bytes, out);
     if (rc != LC_OK)
@@ -143,7 +177,7 @@ extern "C" int lc_peer_group_local(int rank, int world, void *const *regions,
     uint8_t *rs[LC_PEER_MAX_RANKS] = {};
     bool opened[LC_PEER_MAX_RANKS] = {};
     for (int r = 0; r < world; ++r) {
-        if (!regions[r]) return LC_ERR_INVALID_ARGUMENT;
+        if (!regions[r] || room_after(regions[r]) < region_bytes) return LC_ERR_INVALID_ARGUMENT;
         rs[r] = (uint8_t *)regions[r];
     }
     return make_group(rank, world, rs, opened, region_bytes, out);

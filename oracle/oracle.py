@@ -17,6 +17,9 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 ORACLE_LIB = HERE / "_build" / "liblc_oracle.so"
 REF_LIB = HERE / "_ref" / "libref_kernels.so"
+# Checkout of the reference (lucciola-rs): $REF_ROOT, else a directory named
+# `reference` beside this repository. Only the build of oracle/_ref reads it.
+REF_ROOT = Path(os.environ.get("REF_ROOT", HERE.parent.parent / "reference"))
 
 _vp, _i32, _i64, _f32 = C.c_void_p, C.c_int, C.c_int64, C.c_float
 
@@ -28,9 +31,9 @@ def build(ref: bool = False) -> None:
     """Builds the oracle (and, when asked and the reference sources exist, the
     reference kernels) with oracle/Makefile."""
     targets = ["oracle"]
-    if ref and Path(os.environ.get("REF_ROOT", "/root/reference"), "src/kernels").is_dir():
+    if ref and (REF_ROOT / "src" / "kernels").is_dir():
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE), f"REF_ROOT={REF_ROOT}", *targets], check=True)
 
 
 def lib():
@@ -214,6 +217,8 @@ def ref_lib():
                                        _i32, _vp, _i32, _vp, _vp, _i32, _i32, _vp]
         R.ref_rope_append.argtypes = [_vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _i32, _i32, _i32, _i32, _i32, _vp, _i32, _i32, _vp]
+        R.ref_rope_table.argtypes = [_i32, _i32, _f32, _f32, _vp, _vp]
+        R.ref_rope_table.restype = None
         R.ref_argmax.argtypes = [_vp, _i32, _vp, _vp]
         R.ref_sample_top_p.argtypes = [_vp, _i32, _i32, _f32, _f32, _vp, _vp, _vp]
         R.ref_prefill.argtypes = [_vp, _i64, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
@@ -224,6 +229,17 @@ def ref_lib():
             getattr(R, f).restype = _i32
         _ref = R
     return _ref
+
+
+def ref_rope_table(max_pos: int, head_dim: int, base: float, scale_factor: float = 0.0):
+    """RopeCache::new's tables (src/layers/rope.rs:20-31) computed by the
+    reference-kernel library's host code: the reference arm of bench.py uses
+    them so that it loads nothing but oracle/_ref."""
+    half = head_dim // 2
+    cos = np.empty((max_pos, half), np.float32)
+    sin = np.empty((max_pos, half), np.float32)
+    ref_lib().ref_rope_table(max_pos, head_dim, base, scale_factor, _ptr(cos), _ptr(sin))
+    return cos, sin
 
 
 # ----------------------------------------------------------------- sampling --

@@ -26,6 +26,22 @@ typedef __nv_bfloat16 bf16;
 
 static int ref_err(cudaError_t e) { return e == cudaSuccess ? 0 : 1000 + (int)e; }
 
+/* RopeCache::new (src/layers/rope.rs:20-31) on the host: t = pos / scale,
+ * theta = t / base^((2i)/hd), cos/sin tables f32 [max_pos][hd/2]. Lets the
+ * reference arm of bench.py build its tables without the product library. */
+extern "C" void ref_rope_table(int max_pos, int head_dim, float base, float scale_factor,
+                               float *cos_out, float *sin_out) {
+    const int half = head_dim / 2;
+    const float scale = scale_factor > 0.0f ? scale_factor : 1.0f;
+    for (int pos = 0; pos < max_pos; ++pos)
+        for (int i = 0; i < half; ++i) {
+            float t = (float)pos / scale;
+            float theta = t / powf(base, (float)(2 * i) / (float)head_dim);
+            cos_out[(int64_t)pos * half + i] = cosf(theta);
+            sin_out[(int64_t)pos * half + i] = sinf(theta);
+        }
+}
+
 extern "C" int ref_rope(void *q, const void *q_bias, void *k, const void *k_bias,
                         const float *cos_cache, const float *sin_cache,
                         const int *pos_ptr, int head_dim, int num_q_heads,

@@ -37,6 +37,20 @@ def test_rope_oracle_matches_reference_kernel(name):
         assert np.array_equal(k, f["k_out"][i]), f"k mismatch at pos {pos}"
 
 
+@pytest.mark.skipif(not O.REF_LIB.exists(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("hd", [64, 128])
+def test_reference_arm_rope_tables_match(hd):
+    """The tables bench.py's reference arm builds with the reference library's
+    host code equal the oracle's (and so the product's) bit for bit, and the
+    golden rows recorded from the reference."""
+    a_cos, a_sin = O.ref_rope_table(32768, hd, 1e6)
+    b_cos, b_sin = O.rope_table(32768, hd, 1e6)
+    assert np.array_equal(a_cos.view(np.uint32), b_cos.view(np.uint32))
+    assert np.array_equal(a_sin.view(np.uint32), b_sin.view(np.uint32))
+    f = load(f"rope_hd{hd}")
+    assert np.array_equal(a_cos[f["positions"]].view(np.uint32), f["cos_rows"].view(np.uint32))
+
+
 def test_update_oracle_matches_reference_kernel():
     f = load("update_kv_cache")
     kp, vp = f["k_pool"].copy(), f["v_pool"].copy()

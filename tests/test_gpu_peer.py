@@ -8,6 +8,7 @@ regions of this device): each launch's signal is complete before the wait
 that reads it is queued, so nothing waits on a kernel running beside it. With
 two GPUs two processes exchange IPC handles and run the real NVLink path.
 """
+import ctypes as C
 import os
 import socket
 
@@ -150,6 +151,60 @@ def test_peer_decode_batch_of_zero_still_signals():
         group.close()
         torch.cuda.synchronize()
         region.close()
+
+
+def test_peer_group_rejects_a_region_smaller_than_the_group_size():
+    """A region (this rank's or a peer's) with less room than region_bytes
+    would let the decode store past a peer's allocation: refused up front."""
+    region = L.PeerRegion(1 << 20)
+    try:
+        arr = (C.c_void_p * 1)(region.ptr)
+        g = C.c_void_p()
+        rc = L.lib.lc_peer_group_local(0, 1, arr, 64 << 20, C.byref(g))
+        assert rc == 1 and not g.value  # LC_ERR_INVALID_ARGUMENT, no group
+        # a region starting 4 KiB before the end of its allocation
+        arr2 = (C.c_void_p * 1)(region.ptr + (1 << 20) - 4096)
+        assert L.lib.lc_peer_group_local(0, 1, arr2, 8192, C.byref(g)) == 1
+        assert L.lib.lc_peer_group_local(0, 1, arr2, 4096, C.byref(g)) == 0
+        L.lib.lc_peer_group_destroy(g)
+        rc = L.lib.lc_peer_group_open(0, 1, region.ptr, 64 << 20, region.handle, C.byref(g))
+        assert rc == 1
+    finally:
+        region.close()
+
+
+def test_peer_wait_gives_up_and_the_context_stays_usable():
+    """Rank 0 of a two-rank group waits for a peer that never launches: the
+    wait stops after its 2 s limit with LC_DEV_TIMEOUT in the status word,
+    its wait count still advances (so later waits stay paired with later
+    launches), and the GPU keeps working."""
+    world = 2
+    case, rope, shards = _inputs(world)
+    rk = _Rank(case, rope, shards[0])
+    regions = [L.PeerRegion(_region_bytes(1)) for _ in range(world)]
+    group = L.PeerGroup.local(0, world, regions)
+    try:
+        out = torch.full((len(CTX), HQ * HD), float("nan"), dtype=torch.bfloat16, device="cuda")
+        rk.decode(_slot(regions[0], 0), 1, group=group)  # rank 1 never runs
+        group.wait(dev_status=rk.status)
+        torch.cuda.synchronize()
+        assert int(rk.status.item()) & L.LC_DEV_TIMEOUT
+        w = from_device(regions[0].signal_words())
+        assert w[1] == 0 and w[18] == 1  # nothing from rank 1; the wait counted itself
+        assert from_device(regions[1].signal_words())[0] == 1  # rank 0 did signal rank 1
+        # the context still runs kernels: the same shard without the exchange
+        ok = _Rank(case, rope, shards[0])
+        ok.decode(out, 1)
+        torch.cuda.synchronize()
+        assert int(ok.status.item()) == 0
+        mine = from_device(out[:, shards[0]["q_cols"]].contiguous())
+        assert np.array_equal(mine, from_device(_slot(regions[0], 0)[:, shards[0]["q_cols"]]
+                                                .contiguous()))
+    finally:
+        group.close()
+        torch.cuda.synchronize()
+        for reg in regions:
+            reg.close()
 
 
 def _free_port():
