@@ -63,7 +63,7 @@ struct StageMeta {
 
 // Finished chunk handed from the consumer warps to the epilogue warp.
 struct EpiInfo {
-    int b, seg, nh, head0, pages_b, whole, done, final;
+    int b, seg, nh, head0, pages_b, whole, done;
     long long seg_start;
 };
 
@@ -103,8 +103,10 @@ struct DecodeParams {
     // epilogue warp reads the first chunk's position, rope rows and biases
     // before it and only the qkv rows after.
     int pdl_mode;
-    float *ws_o;       // [slots][8][HD]
-    float *ws_lse;     // [slots][8]
+    // out and out_stride allow 16-byte row pieces (else element stores).
+    int out_vec;
+    uint64_t *ws_o;    // [slots][8][HD] tagged words (split-segment partials)
+    uint64_t *ws_lse;  // [slots][8] tagged words
     int *ws_cnt;       // [batch * seg_per_seq]
     int *status;
     // Fused bias + RoPE + append (FUSED kernels only). q/q_stride then address
@@ -502,144 +504,183 @@ __device__ __forceinline__ void state_combine(WarpState<HD> &st, const float *re
         }
 }
 
-// Value of per-head array `a` for the head of lane's float4 f = lane + 32q in a
-// [8][HD] slot, with register-only (static) indexing.
-template <int HD>
-__device__ __forceinline__ float head_of_f4(const float (&a)[kHeadsPerCta], int q, int lane) {
-    if constexpr (HD == 128) return a[q];      // 32 float4s per head
-    else return (lane & 16) ? a[2 * q + 1] : a[2 * q];  // 16 float4s per head
+// ---- split segments ---------------------------------------------------------
+// A segment whose pages span several CTAs ("pieces") is finished by the last
+// piece to arrive on the segment's counter. Every other piece leaves its
+// normalised result (O/l per head and dim, and log2-sum-exp per head) in its
+// workspace slot as 64-bit words: the value's bits low, a tag (1) high. A word
+// is written and read whole (single-copy atomic), so the merger sees either an
+// old cleared word (tag 0) or the new value, and needs no fence from the
+// writer: it re-reads a word until its tag is set (bounded). The merger clears
+// every word it consumed, so all tags are 0 again when the launch ends.
+constexpr uint64_t kPartTag = 1ull << 32;
+
+__device__ __forceinline__ uint64_t part_word(float v) { return kPartTag | __float_as_uint(v); }
+__device__ __forceinline__ bool part_ok(uint64_t w) { return (w >> 32) == 1u; }
+__device__ __forceinline__ float part_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
+
+__device__ __forceinline__ void st_part(uint64_t *a, uint64_t x) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(a), "l"(x) : "memory");
+}
+__device__ __forceinline__ void st_part2(uint64_t *a, uint64_t x, uint64_t y) {
+    asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(a), "l"(x), "l"(y)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t ld_part(const uint64_t *a) {
+    uint64_t x;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(x) : "l"(a) : "memory");
+    return x;
+}
+__device__ __forceinline__ void ld_part2(const uint64_t *a, uint64_t &x, uint64_t &y) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(a)
+                 : "memory");
 }
 
-// Log-sum-exp weights of a batch of up to 32 partials, lane j owning partial j:
-// lv[h] holds its log2-sum-exp on entry (-inf on lanes past the batch) and its
-// weight 2^(lse - M[h]) on exit. M and S (warp-uniform) are the running max and
-// weight sum per head; alpha[h] rescales the sums accumulated before the batch.
-__device__ __forceinline__ void merge_weights(float (&lv)[kHeadsPerCta], float (&M)[kHeadsPerCta],
-                                              float (&S)[kHeadsPerCta],
-                                              float (&alpha)[kHeadsPerCta]) {
+// Running log-sum-exp combination of normalised partials (base 2): the result
+// is acc / s; m is the largest log2-sum-exp combined so far.
+template <int ND>
+struct LseAcc {
+    float acc[ND];
+    float m, s;
+    __device__ __forceinline__ void reset() {
 #pragma unroll
-    for (int h = 0; h < kHeadsPerCta; ++h) {
-        float mb = lv[h];
+        for (int i = 0; i < ND; ++i) acc[i] = 0.f;
+        m = -INFINITY;
+        s = 0.f;
+    }
+    __device__ __forceinline__ void add(const float (&o)[ND], float lse) {
+        const float mn = fmaxf(m, lse);  // finite: a piece holds at least one token
+        const float a = fast_exp2(m - mn), b = fast_exp2(lse - mn);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-        const float mn = fmaxf(M[h], mb);  // finite: every partial has l > 0
-        alpha[h] = fast_exp2(M[h] - mn);
-        M[h] = mn;
-        lv[h] = fast_exp2(lv[h] - mn);
-        float sw = lv[h];
+        for (int i = 0; i < ND; ++i) acc[i] = acc[i] * a + o[i] * b;
+        s = s * a + b;
+        m = mn;
+    }
+};
+
+// ND output elements of one head as bf16 (8 or 16 bytes); PEER kernels store
+// them into every peer's buffer as well.
+template <int ND, bool PEER>
+__device__ __forceinline__ void put_out_vec(const DecodeParams &p, bf16 *a, const float (&v)[ND]) {
+    static_assert(ND == 4 || ND == 8, "4 or 8 elements");
+    uint32_t w[ND / 2];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sw += __shfl_xor_sync(0xffffffffu, sw, o);
-        S[h] = S[h] * alpha[h] + sw;
+    for (int i = 0; i < ND / 2; ++i) w[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
+    auto st = [&](char *dst) {
+        if constexpr (ND == 4)
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
+        else
+            *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    };
+    if (!p.out_vec) {  // rows not 16-byte aligned: element stores
+#pragma unroll
+        for (int i = 0; i < ND; ++i) put_out<PEER>(p, a + i, __float2bfloat16(v[i]));
+        return;
+    }
+    st(reinterpret_cast<char *>(a));
+    if constexpr (PEER) {
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r)
+            if (r < p.n_peer) st(reinterpret_cast<char *>(a) + p.peer_delta[r]);
     }
 }
 
-// Partial slots the stage ring holds at once for the merge: each a [8][HD] row
-// of O/l and 8 log2-sum-exps (at most 32: one per lane).
+// Consumer-thread share of a segment's [8][HD] result in the final-chunk path:
+// thread ct (0..127) owns head ct >> 4, dims (ct & 15) * ND .. + ND.
 template <int HD>
-__host__ __device__ constexpr int kMergeRingSlots() {
-    return DecodeCfg<HD>::kStages * DecodeCfg<HD>::kStageBytes /
-                       ((kHeadsPerCta * HD + kHeadsPerCta) * 4) < 32
-               ? DecodeCfg<HD>::kStages * DecodeCfg<HD>::kStageBytes /
-                     ((kHeadsPerCta * HD + kHeadsPerCta) * 4)
-               : 32;
-}
+struct ShareMap {
+    static constexpr int ND = HD / 16;
+    int h, d0;
+    __device__ __forceinline__ explicit ShareMap(int ct) : h(ct >> 4), d0((ct & 15) * ND) {}
+};
 
-// Merge of a split segment's partials by the epilogue warp of the last CTA to
-// finish it, when that chunk is the CTA's final one: the stage ring is idle, so
-// the nch partial rows (contiguous slots from slot0) and their log2-sum-exps
-// are bulk-copied into it (in batches that fit), and the log-sum-exp weighted
-// sum runs from shared memory. Lane l owns float4 f = l + 32q (q < HD/16) of
-// the [8][HD] slot: head f / (HD/4), dims 4 * (f % (HD/4)) .. +3. Returns false
-// when a wait gave up (abort flag set; the copies in flight have landed).
+// Merge of split segment `seg` by its last piece, run by the 128 consumer
+// threads: pieces j = 0..nch-1 sit in slots slot0 + j; piece `own` (or none,
+// -1) is this CTA's, whose normalised result and log2-sum-exp the caller holds
+// (`own_o`, `own_lse`) and whose words it wrote too. Combines the pieces in
+// slot order (the same order whichever piece merges, so the result does not
+// depend on arrival order), writes the head's ND outputs to `orow` (null: the
+// head is past the group), and clears every consumed word. Returns false when
+// a word stayed untagged past the wait limit (abort flag and status set).
 template <int HD, bool PEER>
-__device__ __forceinline__ bool merge_from_ring(const DecodeParams &p, bf16 *orow, int nh,
-                                             const float *ws_o,
-                                             const float *ws_lse, long long slot0, int nch,
-                                             uint8_t *ring, uint64_t *bar, uint32_t phase,
-                                             volatile int *abort_flag, int *status, int lane) {
-    constexpr int kSlotFloats = kHeadsPerCta * HD;
-    constexpr int kMaxSlots = kMergeRingSlots<HD>();
-    constexpr int kQ = HD / 16;   // float4s per lane per slot
-    constexpr int kF4 = HD / 4;   // float4s per head
-    const float *mo = reinterpret_cast<const float *>(ring);
-    float *ml = reinterpret_cast<float *>(ring) + kMaxSlots * kSlotFloats;
-    // Partials written by other CTAs (generic proxy, published through the
-    // arrival counter) are read here by the bulk-copy (async) proxy.
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    // Per head: running max M and weight sum S (warp-uniform); per lane: its
-    // kQ float4s of the weighted sum.
-    float M[kHeadsPerCta], S[kHeadsPerCta], O[kQ][4];
+__device__ __forceinline__ bool merge_split_segment(const DecodeParams &p, long long slot0, int nch,
+                                                    int own, const float (&own_o)[HD / 16],
+                                                    float own_lse, int h, int d0, bf16 *orow,
+                                                    volatile int *abort_flag) {
+    constexpr int ND = HD / 16;
+    constexpr int kB = 16 / ND;  // pieces loaded per round: 4 at hd 64, 2 at hd 128
+    LseAcc<ND> acc;
+    acc.reset();
+    bool ok = true;
+    for (int j0 = 0; j0 < nch && ok; j0 += kB) {
+        uint64_t lw[kB], ow[kB][ND];
 #pragma unroll
-    for (int h = 0; h < kHeadsPerCta; ++h) {
-        M[h] = -INFINITY;
-        S[h] = 0.f;
-    }
+        for (int jj = 0; jj < kB; ++jj) {
+            const int j = j0 + jj;
+            if (j >= nch || j == own) continue;
+            const long long slot = slot0 + j;
+            lw[jj] = ld_part(p.ws_lse + slot * kHeadsPerCta + h);
+            const uint64_t *src = p.ws_o + (slot * kHeadsPerCta + h) * HD + d0;
 #pragma unroll
-    for (int q = 0; q < kQ; ++q) O[q][0] = O[q][1] = O[q][2] = O[q][3] = 0.f;
-    for (int jb = 0; jb < nch; jb += kMaxSlots) {
-        const int cnt = min(kMaxSlots, nch - jb);
-        if (lane == 0) {
-            const uint32_t ob = (uint32_t)(cnt * kSlotFloats * 4), lb = (uint32_t)(cnt * kHeadsPerCta * 4);
-            mbar_arrive_expect_tx(bar, ob + lb);
-            bulk_load(ring, ws_o + (slot0 + jb) * kSlotFloats, ob, bar);
-            bulk_load(ml, ws_lse + (slot0 + jb) * kHeadsPerCta, lb, bar);
+            for (int i = 0; i < ND; i += 2) ld_part2(src + i, ow[jj][i], ow[jj][i + 1]);
         }
-        if (!mbar_wait_bounded(bar, phase & 1, abort_flag, status)) {
-            if (lane == 0) mbar_wait_drain(bar, phase & 1);
-            __syncwarp();
-            return false;
-        }
-        ++phase;
-        // Weights: lane j (< cnt) takes slot j's log2-sum-exps and leaves its
-        // weights in their place for every lane to read.
-        float lv[kHeadsPerCta], alpha[kHeadsPerCta];
-        if (lane < cnt) {
-            const float4 a = reinterpret_cast<const float4 *>(ml + lane * kHeadsPerCta)[0];
-            const float4 b = reinterpret_cast<const float4 *>(ml + lane * kHeadsPerCta)[1];
-            lv[0] = a.x, lv[1] = a.y, lv[2] = a.z, lv[3] = a.w;
-            lv[4] = b.x, lv[5] = b.y, lv[6] = b.z, lv[7] = b.w;
-        } else {
 #pragma unroll
-            for (int h = 0; h < kHeadsPerCta; ++h) lv[h] = -INFINITY;
+        for (int jj = 0; jj < kB; ++jj) {
+            const int j = j0 + jj;
+            if (j >= nch) break;
+            if (j == own) {
+                acc.add(own_o, own_lse);
+                continue;
+            }
+            const long long slot = slot0 + j;
+            const uint64_t *src = p.ws_o + (slot * kHeadsPerCta + h) * HD + d0;
+            auto ready = [&]() {
+                bool r = part_ok(lw[jj]);
+#pragma unroll
+                for (int i = 0; i < ND; ++i) r = r && part_ok(ow[jj][i]);
+                return r;
+            };
+            if (!ready()) {  // the piece's stores are still on their way
+                const uint64_t t0 = global_timer_ns();
+                for (uint32_t it = 1; !ready(); ++it) {
+                    if ((it & 63u) == 0 && (*abort_flag || global_timer_ns() - t0 > kWaitLimitNs)) {
+                        *abort_flag = 1;
+                        set_status(p.status, LC_DEV_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                    lw[jj] = ld_part(p.ws_lse + slot * kHeadsPerCta + h);
+#pragma unroll
+                    for (int i = 0; i < ND; i += 2) ld_part2(src + i, ow[jj][i], ow[jj][i + 1]);
+                }
+                if (!ok) break;
+            }
+            float v[ND];
+#pragma unroll
+            for (int i = 0; i < ND; ++i) v[i] = part_val(ow[jj][i]);
+            acc.add(v, part_val(lw[jj]));
         }
-        merge_weights(lv, M, S, alpha);
-        __syncwarp();  // every lane has read the log2-sum-exps
-        if (lane < cnt) {
-            reinterpret_cast<float4 *>(ml + lane * kHeadsPerCta)[0] = make_float4(lv[0], lv[1], lv[2], lv[3]);
-            reinterpret_cast<float4 *>(ml + lane * kHeadsPerCta)[1] = make_float4(lv[4], lv[5], lv[6], lv[7]);
-        }
+        // Clear what this round consumed (own words included). The 16 threads
+        // of a head read its log2-sum-exp word; they are one half-warp.
         __syncwarp();
 #pragma unroll
-        for (int q = 0; q < kQ; ++q) {
-            const float a = head_of_f4<HD>(alpha, q, lane);
-            O[q][0] *= a;
-            O[q][1] *= a;
-            O[q][2] *= a;
-            O[q][3] *= a;
-        }
-#pragma unroll 2
-        for (int j = 0; j < cnt; ++j) {
+        for (int jj = 0; jj < kB; ++jj) {
+            const int j = j0 + jj;
+            if (j >= nch || !ok) break;
+            const long long slot = slot0 + j;
+            uint64_t *dst = p.ws_o + (slot * kHeadsPerCta + h) * HD + d0;
 #pragma unroll
-            for (int q = 0; q < kQ; ++q) {
-                const int f = lane + 32 * q;
-                const float w = ml[j * kHeadsPerCta + f / kF4];
-                const float4 v = reinterpret_cast<const float4 *>(mo + j * kSlotFloats)[f];
-                O[q][0] += w * v.x;
-                O[q][1] += w * v.y;
-                O[q][2] += w * v.z;
-                O[q][3] += w * v.w;
-            }
+            for (int i = 0; i < ND; i += 2) st_part2(dst + i, 0ull, 0ull);
+            if (d0 == 0) st_part(p.ws_lse + slot * kHeadsPerCta + h, 0ull);
         }
-        __syncwarp();  // every lane is done with the batch before the next copy
     }
+    if (!ok) return false;
+    if (orow) {
+        const float inv = 1.f / acc.s;
+        float v[ND];
 #pragma unroll
-    for (int q = 0; q < kQ; ++q) {
-        const int f = lane + 32 * q, h = f / kF4, d = 4 * (f % kF4);
-        if (h >= nh) continue;
-        const float inv = 1.f / head_of_f4<HD>(S, q, lane);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-            put_out<PEER>(p, orow + h * HD + d + k, __float2bfloat16(O[q][k] * inv));
+        for (int i = 0; i < ND; ++i) v[i] = acc.acc[i] * inv;
+        put_out_vec<ND, PEER>(p, orow + h * HD + d0, v);
     }
     return true;
 }
@@ -656,7 +697,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     __shared__ __align__(8) uint64_t fin_bar;    // consumer-warp sync (bounded)
     __shared__ __align__(8) uint64_t epi_full;   // consumers -> epilogue: slots hold a chunk
     __shared__ __align__(8) uint64_t epi_empty;  // epilogue -> consumers: slots free again
-    __shared__ __align__(8) uint64_t merge_bar;  // epilogue: partials copied into the ring
+    __shared__ __align__(8) uint64_t epi_exit;   // epilogue -> consumers: epilogue done
     __shared__ __align__(8) uint64_t q_full[2];  // fused: epilogue -> consumers, chunk inputs ready
     __shared__ StageMeta meta[Cfg::kStages];
     __shared__ EpiInfo epi;
@@ -664,6 +705,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     __shared__ int s_b0;
     __shared__ long long s_pref_b0;
     __shared__ int s_abort;
+    __shared__ int s_last;  // final chunk: this CTA arrived last on its segment
+    // A non-final split chunk whose segment the epilogue warp found this CTA
+    // last to finish: merged by the consumer threads after their final chunk.
+    __shared__ struct { int valid, b, nh, head0, nch; long long slot0; } s_pend;
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x;
@@ -773,7 +818,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         mbar_init(&fin_bar, kConsumerWarps * 32);
         mbar_init(&epi_full, 2);
         mbar_init(&epi_empty, 1);
-        mbar_init(&merge_bar, 1);
+        mbar_init(&epi_exit, 1);
+        s_pend.valid = 0;
         mbar_init(&q_full[0], 1);
         mbar_init(&q_full[1], 1);
         s_abort = 0;
@@ -889,17 +935,13 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
 
     if (warp == kEpilogueWarp) {
         // ------------------------------------------------------ epilogue --
-        // Combines the two half-CTA states of a finished chunk, then writes the
-        // bf16 output (whole segment) or a partial plus, for the last chunk of a
-        // split segment to arrive, the log-sum-exp merge of all its partials.
+        // Takes every chunk but the CTA's final one off the consumers' path:
+        // combines the two half-CTA states, then writes the bf16 output (whole
+        // segment) or, for a split segment (only the CTA's first chunk can be
+        // one here), leaves its partial and counts it; if it came last, the
+        // merge is left to the consumer threads (s_pend). The final chunk is
+        // finished by the consumer threads themselves.
         constexpr int KD = HD / 32;  // head dims per lane
-        uint32_t merge_phase = 0;
-        // Segments this CTA merges (it was the last to finish them): at most
-        // its first and its final chunk, merged once the consumers are done.
-        struct PendingMerge {
-            int b, head0, nh, seg, c_first, nch;
-        } pend[2];
-        int npend = 0;
         // Fused: chunk j's inputs go to buffer j & 1. Before waiting for chunk k
         // to finish, chunks up to k + 1 are prepared; buffer (k + 1) & 1 was
         // last read by chunk k - 1, which has finished. The dependency wait
@@ -970,60 +1012,36 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                         put_out<PEER>(p, orow + h * HD + kk * 32 + lane,
                                       __float2bfloat16(O[h][kk] * il));
                 }
-                if (e.final) break;  // the consumers' end-of-range message is not needed
                 continue;
             }
-            // Partial of a split segment: slot = segment + this CTA.
+            // Partial of a split segment in slot segment + this CTA, then its
+            // arrival; the last piece to arrive merges.
             const long long slot = (long long)e.seg + cta;
-            float *wo = p.ws_o + slot * kHeadsPerCta * HD;
+            uint64_t *wo = p.ws_o + slot * kHeadsPerCta * HD;
 #pragma unroll
             for (int h = 0; h < kHeadsPerCta; ++h) {
                 const float il = 1.f / Lh[h];
 #pragma unroll
-                for (int kk = 0; kk < KD; ++kk) wo[h * HD + kk * 32 + lane] = O[h][kk] * il;
-                if (lane == h) p.ws_lse[slot * kHeadsPerCta + h] = Mh[h] + __log2f(Lh[h]);
+                for (int kk = 0; kk < KD; ++kk) st_part(wo + h * HD + kk * 32 + lane, part_word(O[h][kk] * il));
+                if (lane == h) st_part(p.ws_lse + slot * kHeadsPerCta + h, part_word(Mh[h] + __log2f(Lh[h])));
             }
-            // Publish the partial, then count it; the last CTA to arrive merges.
-            // Release pattern: every lane's stores, an acq_rel fence, the warp
-            // sync, then lane 0's atomic, an acquire for the merge (the one
-            // thread that issues its copies).
-            fence_acq_rel_gpu();
-            __syncwarp();
             const int c_first = owner_cta(e.seg_start, T, C);
             const int nch = owner_cta(e.seg_start + e.pages_b - 1, T, C) - c_first + 1;
             int last = 0;
-            if (lane == 0) last = atom_add_acquire_gpu(p.ws_cnt + e.seg, 1) == nch - 1;
-            if (!__shfl_sync(0xffffffffu, last, 0)) {
-                if (e.final) break;
-                continue;
+            if (lane == 0) last = atomicAdd(p.ws_cnt + e.seg, 1) == nch - 1;
+            if (__shfl_sync(0xffffffffu, last, 0) && lane == 0) {
+                p.ws_cnt[e.seg] = 0;  // ready for the next call
+                s_pend.b = e.b;
+                s_pend.nh = e.nh;
+                s_pend.head0 = e.head0;
+                s_pend.nch = nch;
+                s_pend.slot0 = (long long)e.seg + c_first;
+                s_pend.valid = 1;
             }
-            // This CTA merges the segment, after its final chunk: then the stage
-            // ring is idle and takes all the partials in one round of bulk
-            // copies. Split chunks are a CTA's first and final ones only.
-            const PendingMerge pm = {e.b, e.head0, e.nh, e.seg, c_first, nch};
-            if (npend == 0) pend[0] = pm;
-            else pend[1] = pm;
-            ++npend;
-            if (e.final) break;
         }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            if (i >= npend || s_abort) break;
-            const PendingMerge &m = pend[i];
-            const bool ok = merge_from_ring<HD, PEER>(
-                p, p.out + (int64_t)m.b * p.out_stride + (int64_t)m.head0 * HD, m.nh, p.ws_o,
-                p.ws_lse,
-                (long long)m.seg + m.c_first, m.nch, smem_gen, &merge_bar, merge_phase, &s_abort,
-                p.status, lane);
-            merge_phase += (m.nch + kMergeRingSlots<HD>() - 1) / kMergeRingSlots<HD>();
-            if (!ok) break;
-            if (lane == 0) p.ws_cnt[m.seg] = 0;  // ready for the next call
-        }
-        if constexpr (PEER) {
-            fence_acq_rel_sys();
-            __syncwarp();
-            if (lane == 0) peer_arrive(p);
-        }
+        if constexpr (PEER) fence_acq_rel_sys();  // this warp's output stores
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&epi_exit);
         return;
     }
 
@@ -1043,7 +1061,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         const int s = it % Cfg::kStages;
         if (!mbar_wait_bounded(&full_bar[s], (it / Cfg::kStages) & 1, &s_abort, p.status)) break;
         const StageMeta m = meta[s];
-        if (m.flags & kDone) {
+        if (m.flags & kDone) {  // not reached: the final chunk ends the loop
             if (warp < 2) {  // tell the epilogue warp to finish
                 if (chunk_idx > 0)
                     mbar_wait_bounded(&epi_empty, (chunk_idx - 1) & 1, &s_abort, p.status);
@@ -1155,7 +1173,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
             st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, off);
             st.l1 += __shfl_xor_sync(0xffffffffu, st.l1, off);
         }
-        // Halve the 4 warp states into the 2 shared slots, hand them over.
+        // Halve the 4 warp states into the 2 shared slots. Every chunk but the
+        // CTA's final one is then handed to the epilogue warp; for the final
+        // one the epilogue is only told to finish.
+        const bool final_chunk = (m.flags & kFinal) != 0;
         if (chunk_idx > 0) mbar_wait_bounded(&epi_empty, (chunk_idx - 1) & 1, &s_abort, p.status);
         if (warp >= 2) state_store<HD>(red + (warp - 2) * kRedFloats, st, lane);
         consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
@@ -1170,22 +1191,95 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                 epi.head0 = kvh * p.group + hsub * kHeadsPerCta;
                 epi.pages_b = m.pages_b;
                 epi.whole = m.chunk_p0 == 0 && m.take == m.pages_b;
-                epi.done = 0;
+                epi.done = final_chunk;
                 epi.seg_start = m.seg_start;
-                epi.final = (m.flags & kFinal) != 0;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&epi_full);
         }
         ++chunk_idx;
         st.reset();
+        if (!final_chunk) continue;
+
+        // ------------------------------------- the final chunk, 128 threads --
+        // Thread ct owns head ct >> 4, dims (ct & 15) * HD/16 .. + HD/16 of the
+        // CTA's state for this chunk: whole segment -> output; split segment ->
+        // partial + arrival, and the merge if this CTA came last.
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);  // both slots stored
+        constexpr int ND = ShareMap<HD>::ND;
+        const ShareMap<HD> sm(warp * 32 + lane);
+        const float *r0 = red, *r1 = red + kRedFloats;
+        const float m0 = r0[kHeadsPerCta * HD + sm.h], m1 = r1[kHeadsPerCta * HD + sm.h];
+        const float l0 = r0[kHeadsPerCta * HD + kHeadsPerCta + sm.h];
+        const float l1 = r1[kHeadsPerCta * HD + kHeadsPerCta + sm.h];
+        const float M = fmaxf(m0, m1);
+        const float u = M == -INFINITY ? 0.f : M;
+        const float e0 = fast_exp2(m0 - u), e1 = fast_exp2(m1 - u);
+        const float Ls = l0 * e0 + l1 * e1;
+        const float il = 1.f / Ls;
+        float o[ND];
+#pragma unroll
+        for (int i = 0; i < ND; i += 4) {
+            const float4 a = *reinterpret_cast<const float4 *>(r0 + sm.h * HD + sm.d0 + i);
+            const float4 b = *reinterpret_cast<const float4 *>(r1 + sm.h * HD + sm.d0 + i);
+            o[i] = (a.x * e0 + b.x * e1) * il;
+            o[i + 1] = (a.y * e0 + b.y * e1) * il;
+            o[i + 2] = (a.z * e0 + b.z * e1) * il;
+            o[i + 3] = (a.w * e0 + b.w * e1) * il;
+        }
+        bf16 *orow = sm.h < nh ? p.out + (int64_t)m.b * p.out_stride +
+                                     (int64_t)(kvh * p.group + hsub * kHeadsPerCta) * HD
+                               : nullptr;
+        if (m.chunk_p0 == 0 && m.take == m.pages_b) {
+            if (orow) put_out_vec<ND, PEER>(p, orow + sm.h * HD + sm.d0, o);
+            break;
+        }
+        const int seg = m.b * G + m.g;
+        const long long slot = (long long)seg + cta;
+        const float lse = M + __log2f(Ls);
+        {
+            uint64_t *wo = p.ws_o + (slot * kHeadsPerCta + sm.h) * HD + sm.d0;
+#pragma unroll
+            for (int i = 0; i < ND; i += 2) st_part2(wo + i, part_word(o[i]), part_word(o[i + 1]));
+            if (sm.d0 == 0) st_part(p.ws_lse + slot * kHeadsPerCta + sm.h, part_word(lse));
+        }
+        const int c_first = owner_cta(m.seg_start, T, C);
+        const int nch = owner_cta(m.seg_start + m.pages_b - 1, T, C) - c_first + 1;
+        if (warp == 0 && lane == 0) s_last = atomicAdd(p.ws_cnt + seg, 1) == nch - 1;
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        if (s_last && !s_abort) {
+            if (warp == 0 && lane == 0) p.ws_cnt[seg] = 0;  // ready for the next call
+            merge_split_segment<HD, PEER>(p, (long long)seg + c_first, nch, cta - c_first, o, lse,
+                                          sm.h, sm.d0, orow, &s_abort);
+        }
+        break;
+    }
+
+    // ---------------------------------------------------------------- exit --
+    // A segment the epilogue warp found this CTA last to finish (its first
+    // chunk) is merged here, once the epilogue is done.
+    mbar_wait_bounded(&epi_exit, 0, &s_abort, p.status);
+    if (s_pend.valid && !s_abort) {
+        const ShareMap<HD> sm(warp * 32 + lane);
+        float none[HD / 16] = {};
+        bf16 *orow = sm.h < s_pend.nh
+                         ? p.out + (int64_t)s_pend.b * p.out_stride + (int64_t)s_pend.head0 * HD
+                         : nullptr;
+        merge_split_segment<HD, PEER>(p, s_pend.slot0, s_pend.nch, -1, none, 0.f, sm.h, sm.d0,
+                                      orow, &s_abort);
+    }
+    if constexpr (PEER) {
+        fence_acq_rel_sys();  // this thread's output stores, then one arrival per CTA
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        if (warp == 0 && lane == 0) peer_arrive(p);
     }
 }
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// Workspace layout: counters [batch*segments] int32 | lse [slots][8] f32 |
-// o [slots][8][hd] f32, with slots = persistent CTAs + batch*segments.
+// Workspace layout: counters [batch*segments] int32 | lse [slots][8] and
+// o [slots][8][hd] as tagged 64-bit words (value, tag), with slots = persistent
+// CTAs + batch*segments (slot of a piece = its segment + its CTA).
 struct WsLayout {
     size_t cnt_bytes, lse_bytes, o_bytes;
     size_t total() const { return cnt_bytes + lse_bytes + o_bytes; }
@@ -1196,8 +1290,8 @@ WsLayout ws_layout(int batch, int segments_per_seq, int hd, int max_ctas) {
     const size_t slots = segs + (size_t)max_ctas;
     WsLayout l;
     l.cnt_bytes = align256(segs * 4);
-    l.lse_bytes = align256(slots * kHeadsPerCta * 4);
-    l.o_bytes = slots * kHeadsPerCta * hd * 4;
+    l.lse_bytes = align256(slots * kHeadsPerCta * 8);
+    l.o_bytes = slots * kHeadsPerCta * hd * 8;
     return l;
 }
 
@@ -1356,9 +1450,10 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     prm.scale_log2 = sm_scale * 1.4426950408889634f;
     uint8_t *ws = (uint8_t *)workspace;
     prm.ws_cnt = (int *)ws;
-    prm.ws_lse = (float *)(ws + wl.cnt_bytes);
-    prm.ws_o = (float *)(ws + wl.cnt_bytes + wl.lse_bytes);
+    prm.ws_lse = (uint64_t *)(ws + wl.cnt_bytes);
+    prm.ws_o = (uint64_t *)(ws + wl.cnt_bytes + wl.lse_bytes);
     prm.status = dev_status;
+    prm.out_vec = aligned16(out) && out_stride % 8 == 0;
     cudaStream_t s = as_stream(stream);
     return head_dim == 64 ? launch_decode<64>(prm, grid, k_pool, v_pool, s)
                           : launch_decode<128>(prm, grid, k_pool, v_pool, s);
@@ -1496,9 +1591,10 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
     prm.scale_log2 = sm_scale * 1.4426950408889634f;
     uint8_t *ws = (uint8_t *)workspace;
     prm.ws_cnt = (int *)ws;
-    prm.ws_lse = (float *)(ws + wl.cnt_bytes);
-    prm.ws_o = (float *)(ws + wl.cnt_bytes + wl.lse_bytes);
+    prm.ws_lse = (uint64_t *)(ws + wl.cnt_bytes);
+    prm.ws_o = (uint64_t *)(ws + wl.cnt_bytes + wl.lse_bytes);
     prm.status = dev_status;
+    prm.out_vec = aligned16(out) && out_stride % 8 == 0;
     prm.qkv = (const bf16 *)qkv;
     prm.q_bias = (const bf16 *)q_bias;
     prm.k_bias = (const bf16 *)k_bias;
@@ -1585,9 +1681,10 @@ extern "C" int lc_flash_decoding(void *output, const void *q, const void *k_pool
 // Host code cannot use the array's name as a device address (it names a host
 // shadow); the first call on each device resolves the real address with
 // cudaGetSymbolAddress while that device is current and caches it. Calls share
-// the array and it keeps the last call's contents: each call clears the
-// arrival counters it needs, and calls that overlap on the same GPU (issued on
-// two streams, say) race on it. Each device has its own copy of the array.
+// the array and it keeps the last call's contents: each call clears the part
+// it uses (arrival counters and tagged partials) before its launch, and calls
+// that overlap on the same GPU (issued on two streams, say) race on it. Each
+// device has its own copy of the array.
 static __device__ __align__(256) unsigned char
     lc_static_decode_scratch[LC_PAGED_DECODE_STATIC_SCRATCH_BYTES];
 
@@ -1702,8 +1799,11 @@ extern "C" int lc_paged_decode_static(void *out, int64_t out_stride, const void 
     if (wl.total() > (size_t)LC_PAGED_DECODE_STATIC_SCRATCH_BYTES)
         return LC_ERR_WORKSPACE_TOO_SMALL;  // batch too large for the fixed scratch
     cudaStream_t s = as_stream(stream);
-    // The arrival counters must start at zero; the partials need no clearing.
-    if (cudaMemsetAsync(setup->scratch, 0, wl.cnt_bytes, s) != cudaSuccess) {
+    // The arrival counters and the tags of the partial words must start at
+    // zero. A call that completes leaves them so; one that gave up (timeout)
+    // may not, and this entry has no re-initialisation call, so each call
+    // clears the part of the scratch it uses.
+    if (cudaMemsetAsync(setup->scratch, 0, wl.total(), s) != cudaSuccess) {
         cudaGetLastError();
         return LC_ERR_CUDA;
     }
@@ -1737,9 +1837,10 @@ extern "C" int lc_paged_decode_static(void *out, int64_t out_stride, const void 
     prm.scale_log2 = sm_scale * 1.4426950408889634f;
     uint8_t *ws = (uint8_t *)setup->scratch;
     prm.ws_cnt = (int *)ws;
-    prm.ws_lse = (float *)(ws + wl.cnt_bytes);
-    prm.ws_o = (float *)(ws + wl.cnt_bytes + wl.lse_bytes);
+    prm.ws_lse = (uint64_t *)(ws + wl.cnt_bytes);
+    prm.ws_o = (uint64_t *)(ws + wl.cnt_bytes + wl.lse_bytes);
     prm.status = dev_status;
+    prm.out_vec = aligned16(out) && out_stride % 8 == 0;
     return head_dim == 64 ? launch_decode_static<64>(prm, grid, k_pool, v_pool, s)
                           : launch_decode_static<128>(prm, grid, k_pool, v_pool, s);
 }

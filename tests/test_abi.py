@@ -203,11 +203,12 @@ def test_peer_exchange_rejects_bad_arguments():
 
 
 def test_workspace_sizes():
-    # host-only sizing assumes a 148-SM B200: 3 CTAs/SM at hd 64, 2 at hd 128
+    # host-only sizing assumes a 148-SM B200: 3 CTAs/SM at hd 64, 2 at hd 128;
+    # int32 counters, then tagged 64-bit partial words (log2-sum-exp, outputs)
     segs = 64 * 2                      # batch x (kv heads x 8-head slices)
     slots = segs + 148 * 3
-    want = ((segs * 4 + 255) // 256 * 256 + (slots * 8 * 4 + 255) // 256 * 256
-            + slots * 8 * 64 * 4)
+    want = ((segs * 4 + 255) // 256 * 256 + (slots * 8 * 8 + 255) // 256 * 256
+            + slots * 8 * 64 * 8)
     assert L.paged_decode_workspace_size(64, 14, 2, 64) == want
     assert L.paged_decode_workspace_size(1, 64, 4, 128) > 0   # group 16: two slices per kv head
     assert L.paged_decode_workspace_size(4, 14, 3, 64) == 0   # invalid shape

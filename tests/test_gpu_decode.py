@@ -106,6 +106,20 @@ def test_decode_strided_q_and_out_rows():
     assert not wide[:, hq * hd:].any()
 
 
+def test_decode_out_rows_without_16_byte_alignment():
+    """out rows 2 bytes past a 16-byte boundary with an odd stride: the
+    kernels fall back to element stores there."""
+    hq, hkv, hd = 14, 2, 64
+    case = make_case(6, hq, hkv, hd, [1, 40, 700, 1500, 3000, 17], seed=31)
+    d = dev_case(case)
+    wide = torch.zeros(case.batch, hq * hd + 3, dtype=torch.bfloat16, device="cuda")
+    out = wide[:, 1:1 + hq * hd]
+    _, st = gpu_decode(case, d=d, out=out)
+    assert st == 0
+    assert max_err(from_device(out.contiguous()), oracle_decode(case)) <= ATTN_ATOL
+    assert not wide[:, 0].any() and not wide[:, 1 + hq * hd:].any()
+
+
 def test_decode_positions_mode_and_workspace_reuse():
     """len_offset=1 (positions, like the reference's pos_ptr) and two calls in a
     row on one workspace give the same result (arrival counters reset)."""
@@ -117,7 +131,8 @@ def test_decode_positions_mode_and_workspace_reuse():
     b, _ = gpu_decode(case, d=d, partition_tokens=64, len_offset=1, ws=ws)
     assert np.array_equal(a, from_device(b))
     assert max_err(a, oracle_decode(case)) <= ATTN_ATOL
-    assert not ws[:6 * 2 * 4].any()  # arrival counters (batch x kv heads) back at zero
+    # arrival counters and every tagged partial word back at zero
+    assert not ws.any()
 
 
 def test_decode_empty_context_gives_zeros():
