@@ -103,7 +103,7 @@ struct DecodeParams {
     // epilogue warp reads the first chunk's position, rope rows and biases
     // before it and only the qkv rows after.
     int pdl_mode;
-    // out and out_stride allow 16-byte row pieces (else element stores).
+    // out and out_stride keep bf16 pairs 4-byte aligned (else element stores).
     int out_vec;
     uint64_t *ws_o;    // [slots][8][HD] tagged words (split-segment partials)
     uint64_t *ws_lse;  // [slots][8] tagged words
@@ -444,11 +444,12 @@ __device__ __forceinline__ void bulk_load(void *smem_dst, const void *src, uint3
 
 // Barrier of the 128 consumer threads built on an mbarrier, so that a warp
 // that gave up on a wait cannot leave the others blocked for good.
-__device__ __forceinline__ void consumer_sync(uint64_t *bar, uint32_t &phase,
+__device__ __forceinline__ bool consumer_sync(uint64_t *bar, uint32_t &phase,
                                               volatile int *abort_flag, int *status) {
     mbar_arrive(bar);
-    mbar_wait_bounded(bar, phase & 1, abort_flag, status);
+    const bool ok = mbar_wait_bounded(bar, phase & 1, abort_flag, status);
     ++phase;
+    return ok;
 }
 
 // Per-warp running softmax state of one chunk: heads 2c, 2c+1 of this lane.
@@ -519,12 +520,14 @@ __device__ __forceinline__ uint64_t part_word(float v) { return kPartTag | __flo
 __device__ __forceinline__ bool part_ok(uint64_t w) { return (w >> 32) == 1u; }
 __device__ __forceinline__ float part_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
 
+// Plain stores: an aligned 8-byte store is written whole; strong (relaxed.gpu)
+// stores cost several times more issue time here for no gain, as the reader
+// re-checks every word's tag.
 __device__ __forceinline__ void st_part(uint64_t *a, uint64_t x) {
-    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(a), "l"(x) : "memory");
+    asm volatile("st.global.b64 [%0], %1;" ::"l"(a), "l"(x) : "memory");
 }
 __device__ __forceinline__ void st_part2(uint64_t *a, uint64_t x, uint64_t y) {
-    asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(a), "l"(x), "l"(y)
-                 : "memory");
+    asm volatile("st.global.v2.b64 [%0], {%1, %2};" ::"l"(a), "l"(x), "l"(y) : "memory");
 }
 __device__ __forceinline__ uint64_t ld_part(const uint64_t *a) {
     uint64_t x;
@@ -558,129 +561,151 @@ struct LseAcc {
     }
 };
 
-// ND output elements of one head as bf16 (8 or 16 bytes); PEER kernels store
-// them into every peer's buffer as well.
-template <int ND, bool PEER>
-__device__ __forceinline__ void put_out_vec(const DecodeParams &p, bf16 *a, const float (&v)[ND]) {
-    static_assert(ND == 4 || ND == 8, "4 or 8 elements");
-    uint32_t w[ND / 2];
+// bf16 pairs of one head's output: pair k at dims 32k + 2t, 32k + 2t + 1
+// (NP = HD / 32 pairs); PEER kernels store them into every peer's buffer too.
+template <int NP, bool PEER>
+__device__ __forceinline__ void put_out_pairs(const DecodeParams &p, bf16 *head_row, int t,
+                                              const float (&v)[2 * NP]) {
 #pragma unroll
-    for (int i = 0; i < ND / 2; ++i) w[i] = pack_bf16(v[2 * i], v[2 * i + 1]);
-    auto st = [&](char *dst) {
-        if constexpr (ND == 4)
-            *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
-        else
-            *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-    };
-    if (!p.out_vec) {  // rows not 16-byte aligned: element stores
+    for (int k = 0; k < NP; ++k) {
+        bf16 *a = head_row + 32 * k + 2 * t;
+        if (!p.out_vec) {  // rows not 4-byte aligned: element stores
+            put_out<PEER>(p, a, __float2bfloat16(v[2 * k]));
+            put_out<PEER>(p, a + 1, __float2bfloat16(v[2 * k + 1]));
+            continue;
+        }
+        const uint32_t w = pack_bf16(v[2 * k], v[2 * k + 1]);
+        *reinterpret_cast<uint32_t *>(a) = w;
+        if constexpr (PEER) {
 #pragma unroll
-        for (int i = 0; i < ND; ++i) put_out<PEER>(p, a + i, __float2bfloat16(v[i]));
-        return;
-    }
-    st(reinterpret_cast<char *>(a));
-    if constexpr (PEER) {
-#pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r)
-            if (r < p.n_peer) st(reinterpret_cast<char *>(a) + p.peer_delta[r]);
+            for (int r = 0; r < kMaxPeers; ++r)
+                if (r < p.n_peer)
+                    *reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(a) + p.peer_delta[r]) = w;
+        }
     }
 }
 
 // Consumer-thread share of a segment's [8][HD] result in the final-chunk path:
-// thread ct (0..127) owns head ct >> 4, dims (ct & 15) * ND .. + ND.
+// thread ct (0..127) owns head h = ct >> 4 and, with t = ct & 15, the dim
+// pairs 32k + 2t (+1), k < HD / 32. Sixteen threads of a head thus read and
+// write 16 consecutive pairs at a time (no shared-memory bank conflicts).
 template <int HD>
 struct ShareMap {
-    static constexpr int ND = HD / 16;
-    int h, d0;
-    __device__ __forceinline__ explicit ShareMap(int ct) : h(ct >> 4), d0((ct & 15) * ND) {}
+    static constexpr int NP = HD / 32;  // pairs per thread
+    static constexpr int ND = 2 * NP;   // values per thread
+    int h, t;
+    __device__ __forceinline__ explicit ShareMap(int ct) : h(ct >> 4), t(ct & 15) {}
+    __device__ __forceinline__ int dim(int k) const { return 32 * k + 2 * t; }
 };
 
 // Merge of split segment `seg` by its last piece, run by the 128 consumer
-// threads: pieces j = 0..nch-1 sit in slots slot0 + j; piece `own` (or none,
-// -1) is this CTA's, whose normalised result and log2-sum-exp the caller holds
-// (`own_o`, `own_lse`) and whose words it wrote too. Combines the pieces in
-// slot order (the same order whichever piece merges, so the result does not
-// depend on arrival order), writes the head's ND outputs to `orow` (null: the
-// head is past the group), and clears every consumed word. Returns false when
-// a word stayed untagged past the wait limit (abort flag and status set).
+// threads once the stage ring is idle: pieces j = 0..nch-1 sit in slots
+// slot0 + j; piece `own` (or none, -1) is this CTA's, whose normalised result
+// and log2-sum-exp the caller holds (`own_o`, `own_lse`; its words are in its
+// slot too). The slots' words come into the ring with one bulk copy per batch
+// (all of the segment's pieces in one round trip when they fit); a thread that
+// finds one of its words still untagged (the piece's stores are on their way)
+// reads those words again from global memory until they are (bounded). Pieces
+// are combined in slot order, the same whichever piece merges, so the result
+// does not depend on arrival order. Writes the head's outputs to `orow` (null:
+// the head is past the group) and clears every consumed word. Returns false
+// when a wait gave up (abort flag and status set).
 template <int HD, bool PEER>
-__device__ __forceinline__ bool merge_split_segment(const DecodeParams &p, long long slot0, int nch,
-                                                    int own, const float (&own_o)[HD / 16],
-                                                    float own_lse, int h, int d0, bf16 *orow,
-                                                    volatile int *abort_flag) {
-    constexpr int ND = HD / 16;
-    constexpr int kB = 16 / ND;  // pieces loaded per round: 4 at hd 64, 2 at hd 128
+__device__ __forceinline__ bool merge_split_segment(
+    const DecodeParams &p, long long slot0, int nch, int own, const float (&own_o)[HD / 16],
+    float own_lse, const ShareMap<HD> &sm, bf16 *orow, uint8_t *ring, uint64_t *bar,
+    uint32_t &bar_phase, uint64_t *sync_bar, uint32_t &sync_phase, volatile int *abort_flag,
+    bool leader) {
+    constexpr int NP = ShareMap<HD>::NP, ND = ShareMap<HD>::ND;
+    constexpr int kPartWords = kHeadsPerCta * HD;
+    constexpr int kRingBytes = DecodeCfg<HD>::kStages * DecodeCfg<HD>::kStageBytes;
+    constexpr int kMax = kRingBytes / ((kPartWords + kHeadsPerCta) * 8);
+    static_assert(kMax >= 8, "the ring holds at least 8 pieces");
+    const int h = sm.h;
+    const uint64_t *ro = reinterpret_cast<const uint64_t *>(ring);
+    const uint64_t *rl = ro + kMax * kPartWords;
     LseAcc<ND> acc;
     acc.reset();
-    bool ok = true;
-    for (int j0 = 0; j0 < nch && ok; j0 += kB) {
-        uint64_t lw[kB], ow[kB][ND];
-#pragma unroll
-        for (int jj = 0; jj < kB; ++jj) {
-            const int j = j0 + jj;
-            if (j >= nch || j == own) continue;
-            const long long slot = slot0 + j;
-            lw[jj] = ld_part(p.ws_lse + slot * kHeadsPerCta + h);
-            const uint64_t *src = p.ws_o + (slot * kHeadsPerCta + h) * HD + d0;
-#pragma unroll
-            for (int i = 0; i < ND; i += 2) ld_part2(src + i, ow[jj][i], ow[jj][i + 1]);
+    for (int j0 = 0; j0 < nch; j0 += kMax) {
+        const int cnt = min(kMax, nch - j0);
+        if (j0 > 0 && !consumer_sync(sync_bar, sync_phase, abort_flag, p.status))
+            return false;  // every thread is done with the previous batch
+        if (leader) {
+            // Words written by other CTAs (generic proxy) and the ring's last
+            // generic reads, before the bulk copy (async proxy).
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const uint32_t ob = (uint32_t)(cnt * kPartWords * 8), lb = (uint32_t)(cnt * kHeadsPerCta * 8);
+            mbar_arrive_expect_tx(bar, ob + lb);
+            bulk_load(ring, p.ws_o + (slot0 + j0) * kPartWords, ob, bar);
+            bulk_load(const_cast<uint64_t *>(rl), p.ws_lse + (slot0 + j0) * kHeadsPerCta, lb, bar);
         }
-#pragma unroll
-        for (int jj = 0; jj < kB; ++jj) {
+        if (!mbar_wait_bounded(bar, bar_phase & 1, abort_flag, p.status)) {
+            if (leader) mbar_wait_drain(bar, bar_phase & 1);
+            return false;
+        }
+        ++bar_phase;
+        for (int jj = 0; jj < cnt; ++jj) {
             const int j = j0 + jj;
-            if (j >= nch) break;
             if (j == own) {
                 acc.add(own_o, own_lse);
                 continue;
             }
-            const long long slot = slot0 + j;
-            const uint64_t *src = p.ws_o + (slot * kHeadsPerCta + h) * HD + d0;
-            auto ready = [&]() {
-                bool r = part_ok(lw[jj]);
+            // Value bits low, tag high: x/z values, y/w tags of the two words.
+            uint2 lw = *reinterpret_cast<const uint2 *>(rl + jj * kHeadsPerCta + h);
+            uint4 q[NP];
 #pragma unroll
-                for (int i = 0; i < ND; ++i) r = r && part_ok(ow[jj][i]);
-                return r;
+            for (int k = 0; k < NP; ++k)
+                q[k] = *reinterpret_cast<const uint4 *>(ro + jj * kPartWords + h * HD + sm.dim(k));
+            auto all_tagged = [&]() {
+                uint32_t ok = lw.y == 1u;
+#pragma unroll
+                for (int k = 0; k < NP; ++k) ok &= (q[k].y == 1u) & (q[k].w == 1u);
+                return ok != 0;
             };
-            if (!ready()) {  // the piece's stores are still on their way
+            if (!all_tagged()) {  // a store of that piece had not landed when copied
+                const long long slot = slot0 + j;
+                const uint64_t *src = p.ws_o + (slot * kHeadsPerCta + h) * HD;
                 const uint64_t t0 = global_timer_ns();
-                for (uint32_t it = 1; !ready(); ++it) {
+                for (uint32_t it = 1; !all_tagged(); ++it) {
                     if ((it & 63u) == 0 && (*abort_flag || global_timer_ns() - t0 > kWaitLimitNs)) {
                         *abort_flag = 1;
                         set_status(p.status, LC_DEV_TIMEOUT);
-                        ok = false;
-                        break;
+                        return false;
                     }
-                    lw[jj] = ld_part(p.ws_lse + slot * kHeadsPerCta + h);
+                    const uint64_t l64 = ld_part(p.ws_lse + slot * kHeadsPerCta + h);
+                    lw = make_uint2((uint32_t)l64, (uint32_t)(l64 >> 32));
 #pragma unroll
-                    for (int i = 0; i < ND; i += 2) ld_part2(src + i, ow[jj][i], ow[jj][i + 1]);
+                    for (int k = 0; k < NP; ++k) {
+                        uint64_t a, b;
+                        ld_part2(src + sm.dim(k), a, b);
+                        q[k] = make_uint4((uint32_t)a, (uint32_t)(a >> 32), (uint32_t)b, (uint32_t)(b >> 32));
+                    }
                 }
-                if (!ok) break;
             }
             float v[ND];
 #pragma unroll
-            for (int i = 0; i < ND; ++i) v[i] = part_val(ow[jj][i]);
-            acc.add(v, part_val(lw[jj]));
-        }
-        // Clear what this round consumed (own words included). The 16 threads
-        // of a head read its log2-sum-exp word; they are one half-warp.
-        __syncwarp();
-#pragma unroll
-        for (int jj = 0; jj < kB; ++jj) {
-            const int j = j0 + jj;
-            if (j >= nch || !ok) break;
-            const long long slot = slot0 + j;
-            uint64_t *dst = p.ws_o + (slot * kHeadsPerCta + h) * HD + d0;
-#pragma unroll
-            for (int i = 0; i < ND; i += 2) st_part2(dst + i, 0ull, 0ull);
-            if (d0 == 0) st_part(p.ws_lse + slot * kHeadsPerCta + h, 0ull);
+            for (int k = 0; k < NP; ++k) {
+                v[2 * k] = __uint_as_float(q[k].x);
+                v[2 * k + 1] = __uint_as_float(q[k].z);
+            }
+            acc.add(v, __uint_as_float(lw.x));
         }
     }
-    if (!ok) return false;
+    // Clear the consumed words (own included) for the next call.
+    for (int j = 0; j < nch; ++j) {
+        const long long slot = slot0 + j;
+        uint64_t *dst = p.ws_o + (slot * kHeadsPerCta + h) * HD;
+#pragma unroll
+        for (int k = 0; k < NP; ++k) st_part2(dst + sm.dim(k), 0ull, 0ull);
+        if (sm.t == 0) st_part(p.ws_lse + slot * kHeadsPerCta + h, 0ull);
+    }
     if (orow) {
         const float inv = 1.f / acc.s;
         float v[ND];
 #pragma unroll
         for (int i = 0; i < ND; ++i) v[i] = acc.acc[i] * inv;
-        put_out_vec<ND, PEER>(p, orow + h * HD + d0, v);
+        put_out_pairs<NP, PEER>(p, orow + h * HD, sm.t, v);
     }
     return true;
 }
@@ -698,6 +723,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     __shared__ __align__(8) uint64_t epi_full;   // consumers -> epilogue: slots hold a chunk
     __shared__ __align__(8) uint64_t epi_empty;  // epilogue -> consumers: slots free again
     __shared__ __align__(8) uint64_t epi_exit;   // epilogue -> consumers: epilogue done
+    __shared__ __align__(8) uint64_t merge_bar;  // consumers: partials copied into the ring
     __shared__ __align__(8) uint64_t q_full[2];  // fused: epilogue -> consumers, chunk inputs ready
     __shared__ StageMeta meta[Cfg::kStages];
     __shared__ EpiInfo epi;
@@ -819,6 +845,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         mbar_init(&epi_full, 2);
         mbar_init(&epi_empty, 1);
         mbar_init(&epi_exit, 1);
+        mbar_init(&merge_bar, 1);
         s_pend.valid = 0;
         mbar_init(&q_full[0], 1);
         mbar_init(&q_full[1], 1);
@@ -1052,7 +1079,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     const int v_row = (mi >> 1) * 8 + r8, v_chunk = mi & 1;  // PV A operand (V^T tile)
     if (p.pdl_mode == 2) griddep_wait();
     uint32_t qf[KSTEPS][2];
-    uint32_t fin_phase = 0;
+    uint32_t fin_phase = 0, merge_phase = 0;
     int chunk_idx = 0;  // chunks handed to the epilogue so far
     int nk_it = -1, nk_warp = -1;  // fused: stage and warp of the new token's page
     WarpState<HD> st;
@@ -1202,11 +1229,11 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         if (!final_chunk) continue;
 
         // ------------------------------------- the final chunk, 128 threads --
-        // Thread ct owns head ct >> 4, dims (ct & 15) * HD/16 .. + HD/16 of the
+        // Thread ct owns head ct >> 4 and dim pairs 32k + 2 (ct & 15) of the
         // CTA's state for this chunk: whole segment -> output; split segment ->
         // partial + arrival, and the merge if this CTA came last.
         consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);  // both slots stored
-        constexpr int ND = ShareMap<HD>::ND;
+        constexpr int NP = ShareMap<HD>::NP, ND = ShareMap<HD>::ND;
         const ShareMap<HD> sm(warp * 32 + lane);
         const float *r0 = red, *r1 = red + kRedFloats;
         const float m0 = r0[kHeadsPerCta * HD + sm.h], m1 = r1[kHeadsPerCta * HD + sm.h];
@@ -1219,29 +1246,28 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         const float il = 1.f / Ls;
         float o[ND];
 #pragma unroll
-        for (int i = 0; i < ND; i += 4) {
-            const float4 a = *reinterpret_cast<const float4 *>(r0 + sm.h * HD + sm.d0 + i);
-            const float4 b = *reinterpret_cast<const float4 *>(r1 + sm.h * HD + sm.d0 + i);
-            o[i] = (a.x * e0 + b.x * e1) * il;
-            o[i + 1] = (a.y * e0 + b.y * e1) * il;
-            o[i + 2] = (a.z * e0 + b.z * e1) * il;
-            o[i + 3] = (a.w * e0 + b.w * e1) * il;
+        for (int k = 0; k < NP; ++k) {
+            const float2 a = *reinterpret_cast<const float2 *>(r0 + sm.h * HD + sm.dim(k));
+            const float2 b = *reinterpret_cast<const float2 *>(r1 + sm.h * HD + sm.dim(k));
+            o[2 * k] = (a.x * e0 + b.x * e1) * il;
+            o[2 * k + 1] = (a.y * e0 + b.y * e1) * il;
         }
         bf16 *orow = sm.h < nh ? p.out + (int64_t)m.b * p.out_stride +
                                      (int64_t)(kvh * p.group + hsub * kHeadsPerCta) * HD
                                : nullptr;
         if (m.chunk_p0 == 0 && m.take == m.pages_b) {
-            if (orow) put_out_vec<ND, PEER>(p, orow + sm.h * HD + sm.d0, o);
+            if (orow) put_out_pairs<NP, PEER>(p, orow + sm.h * HD, sm.t, o);
             break;
         }
         const int seg = m.b * G + m.g;
         const long long slot = (long long)seg + cta;
         const float lse = M + __log2f(Ls);
         {
-            uint64_t *wo = p.ws_o + (slot * kHeadsPerCta + sm.h) * HD + sm.d0;
+            uint64_t *wo = p.ws_o + (slot * kHeadsPerCta + sm.h) * HD;
 #pragma unroll
-            for (int i = 0; i < ND; i += 2) st_part2(wo + i, part_word(o[i]), part_word(o[i + 1]));
-            if (sm.d0 == 0) st_part(p.ws_lse + slot * kHeadsPerCta + sm.h, part_word(lse));
+            for (int k = 0; k < NP; ++k)
+                st_part2(wo + sm.dim(k), part_word(o[2 * k]), part_word(o[2 * k + 1]));
+            if (sm.t == 0) st_part(p.ws_lse + slot * kHeadsPerCta + sm.h, part_word(lse));
         }
         const int c_first = owner_cta(m.seg_start, T, C);
         const int nch = owner_cta(m.seg_start + m.pages_b - 1, T, C) - c_first + 1;
@@ -1250,7 +1276,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         if (s_last && !s_abort) {
             if (warp == 0 && lane == 0) p.ws_cnt[seg] = 0;  // ready for the next call
             merge_split_segment<HD, PEER>(p, (long long)seg + c_first, nch, cta - c_first, o, lse,
-                                          sm.h, sm.d0, orow, &s_abort);
+                                          sm, orow, smem_gen, &merge_bar, merge_phase,
+                                          &fin_bar, fin_phase, &s_abort, warp == 0 && lane == 0);
         }
         break;
     }
@@ -1259,14 +1286,16 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     // A segment the epilogue warp found this CTA last to finish (its first
     // chunk) is merged here, once the epilogue is done.
     mbar_wait_bounded(&epi_exit, 0, &s_abort, p.status);
-    if (s_pend.valid && !s_abort) {
+    if (s_pend.valid && !s_abort &&
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status)) {  // the ring is free again
         const ShareMap<HD> sm(warp * 32 + lane);
         float none[HD / 16] = {};
         bf16 *orow = sm.h < s_pend.nh
                          ? p.out + (int64_t)s_pend.b * p.out_stride + (int64_t)s_pend.head0 * HD
                          : nullptr;
-        merge_split_segment<HD, PEER>(p, s_pend.slot0, s_pend.nch, -1, none, 0.f, sm.h, sm.d0,
-                                      orow, &s_abort);
+        merge_split_segment<HD, PEER>(p, s_pend.slot0, s_pend.nch, -1, none, 0.f, sm, orow,
+                                      smem_gen, &merge_bar, merge_phase, &fin_bar,
+                                      fin_phase, &s_abort, warp == 0 && lane == 0);
     }
     if constexpr (PEER) {
         fence_acq_rel_sys();  // this thread's output stores, then one arrival per CTA
@@ -1453,7 +1482,7 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     prm.ws_lse = (uint64_t *)(ws + wl.cnt_bytes);
     prm.ws_o = (uint64_t *)(ws + wl.cnt_bytes + wl.lse_bytes);
     prm.status = dev_status;
-    prm.out_vec = aligned16(out) && out_stride % 8 == 0;
+    prm.out_vec = ((uintptr_t)out & 3) == 0 && out_stride % 2 == 0;
     cudaStream_t s = as_stream(stream);
     return head_dim == 64 ? launch_decode<64>(prm, grid, k_pool, v_pool, s)
                           : launch_decode<128>(prm, grid, k_pool, v_pool, s);
@@ -1594,7 +1623,7 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
     prm.ws_lse = (uint64_t *)(ws + wl.cnt_bytes);
     prm.ws_o = (uint64_t *)(ws + wl.cnt_bytes + wl.lse_bytes);
     prm.status = dev_status;
-    prm.out_vec = aligned16(out) && out_stride % 8 == 0;
+    prm.out_vec = ((uintptr_t)out & 3) == 0 && out_stride % 2 == 0;
     prm.qkv = (const bf16 *)qkv;
     prm.q_bias = (const bf16 *)q_bias;
     prm.k_bias = (const bf16 *)k_bias;
@@ -1840,7 +1869,7 @@ extern "C" int lc_paged_decode_static(void *out, int64_t out_stride, const void 
     prm.ws_lse = (uint64_t *)(ws + wl.cnt_bytes);
     prm.ws_o = (uint64_t *)(ws + wl.cnt_bytes + wl.lse_bytes);
     prm.status = dev_status;
-    prm.out_vec = aligned16(out) && out_stride % 8 == 0;
+    prm.out_vec = ((uintptr_t)out & 3) == 0 && out_stride % 2 == 0;
     return head_dim == 64 ? launch_decode_static<64>(prm, grid, k_pool, v_pool, s)
                           : launch_decode_static<128>(prm, grid, k_pool, v_pool, s);
 }
