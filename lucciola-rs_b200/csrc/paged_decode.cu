@@ -760,9 +760,16 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     const int per = (p.batch + kThreads - 1) / kThreads;
     const int bs = min(p.batch, tid * per), be = min(p.batch, bs + per);
     long long mine = 0;
-    for (int b = bs; b < be; ++b) mine += (seq_tokens(p, b, false) + kBlockSize - 1) / kBlockSize;
+    // Do all sequences hold the same (non-zero) number of pages as sequence 0?
+    const int pages0 = (seq_tokens(p, 0, false) + kBlockSize - 1) / kBlockSize;
+    bool same = pages0 > 0;
+    for (int b = bs; b < be; ++b) {
+        const int pb = (seq_tokens(p, b, false) + kBlockSize - 1) / kBlockSize;
+        mine += pb;
+        same = same && pb == pages0;
+    }
     s_part[tid] = mine;
-    __syncthreads();
+    const bool uniform = __syncthreads_and(same) != 0;
     if (warp == 0) {  // exclusive scan of the kThreads partial sums
         constexpr int kPer = kThreads / 32;
         long long v[kPer], run = 0;
@@ -807,6 +814,16 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                                    : (T + kMinPagesPerCta - 1) / kMinPagesPerCta;
         if (want < C) C = (int)(want < 1 ? 1 : want);
         if (T < C) C = (int)T;
+        // Segments of equal length and several CTAs per segment (a short,
+        // uniform batch such as one sequence): a multiple of the segment count
+        // puts every range inside one segment, so that no CTA holds pieces of
+        // two split segments (two merges in a row), at the cost of at most an
+        // eighth of the CTAs.
+        const long long S = uniform ? T / pages0 : 0;  // uniform: pages0 > 0
+        if (uniform && p.partition_tokens == 0 && C >= 2 * S) {
+            const long long Cs = S * (C / S);
+            if ((C - Cs) * 8 <= C) C = (int)Cs;
+        }
     }
     const int cta = blockIdx.x;
     const long long start = (long long)cta * T / C;
