@@ -6,7 +6,8 @@ pools the same appended rows.
 On one GPU two ranks are emulated by one process (lc_peer_group_local over two
 regions of this device): each launch's signal is complete before the wait
 that reads it is queued, so nothing waits on a kernel running beside it. With
-two GPUs two processes exchange IPC handles and run the real NVLink path.
+N >= 2 GPUs, N processes (one per GPU) exchange IPC handles and run the real
+NVLink path; 2, 4 and 8 ranks are covered where that many GPUs are present.
 """
 import ctypes as C
 import os
@@ -22,7 +23,7 @@ pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
 
-HQ, HKV, HD = 16, 4, 128
+HQ, HKV, HD = 32, 8, 128  # 8 kv heads: 1, 2, 4 or 8 per rank
 CTX = np.array([0, 15, 300, 2000, 4095, 17, 1023], np.int32)
 
 
@@ -213,7 +214,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _two_gpu_worker(rank, port, q):
+def _gpu_worker(rank, world, port, q):
     import sys
     from pathlib import Path
     root = Path(__file__).resolve().parents[1]
@@ -225,12 +226,11 @@ def _two_gpu_worker(rank, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    dist.init_process_group("gloo", rank=rank, world_size=2,
+    dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
     ok, msg = False, ""
     try:
         import lucciola as L
-        world = 2
         case, rope, shards = _inputs(world)
         ref_rank, peer_rank = _Rank(case, rope, shards[rank]), _Rank(case, rope, shards[rank])
         region = L.PeerRegion(_region_bytes(2))
@@ -275,18 +275,21 @@ def _two_gpu_worker(rank, port, q):
     q.put((rank, ok, msg))
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="needs two GPUs")
-def test_peer_decode_two_processes_over_nvlink():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_decode_processes_over_nvlink(world):
+    """One process per GPU: every rank's region ends up with all ranks' rows,
+    bit for bit, over four layers in a row."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_two_gpu_worker, args=(r, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_gpu_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=240)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    results = sorted(q.get() for _ in range(2))
+    results = sorted(q.get() for _ in range(world))
     assert all(ok for _, ok, _ in results), results
