@@ -1,7 +1,7 @@
 """Benchmark of the paged decode-attention path on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c1|c3|c4|c4p|c5|s2] [--driver]
+                    [--config c2|c1|c3|c4|c4p|c5|s2|c2d|c3d] [--driver]
 
 Default workload: BASELINE config 2 (Qwen2.5-0.5B shape batched ragged decode:
 64 sequences per GPU, 14 q heads / 2 KV heads, head_dim 64, context lengths
@@ -993,6 +993,135 @@ def run_head_sharded(args, rank, world, local):
         dist.destroy_process_group()
 
 
+# ------------------------------------------- decode-step projections (c2d/c3d) --
+
+DECODE_PROJ = {
+    "c2d": ("qwen2.5-0.5b decode-step projections at batch 64 (BASELINE config 2 shape): QKV "
+            "with bias + RoPE + paged append fused, then o_proj with the residual", 64, 14, 2, 64,
+            896),
+    "c3d": ("qwen2.5-7b decode-step projections at batch 32 (BASELINE config 3 shape): QKV with "
+            "bias + RoPE + paged append fused, then o_proj with the residual", 32, 28, 4, 128,
+            3584),
+}
+
+
+def run_decode_proj_bench(args, rank, world, local):
+    """One decode step's projections per layer at M = batch token rows (the
+    weight-streaming kernel of proj_decode.cu): lc_qkv_proj_rope_append (the
+    new token of every sequence: bias, RoPE, paged append) then lc_proj_gemm
+    for o_proj with the residual in place. Weight sets rotate over enough
+    layers to exceed L2 twice over. The bound is reading the weights: the
+    metric is weight bytes per second. Beside it, the reference's sequence:
+    cublasGemmEx (torch.matmul, bf16 in, fp32 compute) then lc_rope_append, and
+    torch.matmul plus the residual add for o_proj."""
+    import lucciola as L
+    label, B, hq, hkv, hd, hidden = DECODE_PROJ[args.config]
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(919)
+    N, K, No = (hq + 2 * hkv) * hd, hidden, hidden
+    wbytes = (N * K + No * hq * hd) * 2  # per layer
+    layers = max(4, -(-2 * 126 * 2 ** 20 // wbytes))
+    wq = [(torch.randn(N, K, generator=gen, device=device) * K ** -0.5).to(torch.bfloat16)
+          for _ in range(layers)]
+    wo = [(torch.randn(No, hq * hd, generator=gen, device=device) * (hq * hd) ** -0.5)
+          .to(torch.bfloat16) for _ in range(layers)]
+    x = torch.randn(B, K, generator=gen, device=device).to(torch.bfloat16)
+    attn = torch.randn(B, hq * hd, generator=gen, device=device).to(torch.bfloat16)
+    hidden_st = torch.randn(B, No, generator=gen, device=device).to(torch.bfloat16)
+    qkv = torch.empty(B, N, dtype=torch.bfloat16, device=device)
+    rng = np.random.default_rng(5)
+    ctx = rng.integers(256, 4096, B).astype(np.int32)
+    pages = (ctx + 1 + 15) // 16
+    nb = int(pages.sum()) + 1
+    perm = rng.permutation(nb).astype(np.int32)
+    tables_np = np.full((B, int(pages.max())), -1, np.int32)
+    off = 0
+    for b, n in enumerate(pages):
+        tables_np[b, :n] = perm[off:off + n]
+        off += n
+    tables = torch.from_numpy(tables_np).to(device)
+    positions = torch.from_numpy(ctx).to(device)
+    k_pool = torch.zeros((nb, 1, hkv, 16, hd), dtype=torch.bfloat16, device=device)
+    v_pool = torch.zeros_like(k_pool)
+    bias = (torch.randn(N, generator=gen, device=device) * 0.01).to(torch.bfloat16)
+    qb, kb, vb = (bias[:hq * hd].contiguous(), bias[hq * hd:(hq + hkv) * hd].contiguous(),
+                  bias[(hq + hkv) * hd:].contiguous())
+    cos, sin = (torch.from_numpy(t).to(device) for t in L.rope_table_host(4096 + 16, hd, 1e6))
+
+    def ours(l):
+        L.qkv_proj_rope_append(qkv, x, wq[l], positions, qb, kb, vb, cos, sin, k_pool, v_pool, nb,
+                               1, 0, hq, hkv, hd, tables, tokens_per_seq=1)
+        L.proj_gemm(hidden_st, attn, wo[l], residual=hidden_st)
+
+    def library(l):
+        torch.matmul(x, wq[l].t(), out=qkv)
+        L.rope_append(qkv, positions, qb, kb, vb, cos, sin, k_pool, v_pool, nb, 1, 0, hq, hkv, hd,
+                      tables)
+        hidden_st.add_(torch.matmul(attn, wo[l].t()))
+
+    if args.mode == "kernel":
+        for i in range(args.warmup + args.steps):
+            ours(i % layers)
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": "kernel", "config": args.config,
+                          "launches": 2 * (args.warmup + args.steps)}))
+        return
+
+    def timed(fn, steps):
+        for i in range(max(args.warmup, 3) * layers):
+            fn(i % layers)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps * layers):
+            fn(i % layers)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (steps * layers)
+
+    sampler = ClockSampler(local)
+    t_end = time.perf_counter() + 1.0
+    while time.perf_counter() < t_end:
+        for l in range(layers):
+            ours(l)
+    torch.cuda.synchronize()
+    ms = timed(ours, args.steps)
+    ms_lib = timed(library, args.steps)
+    clocks = sampler.stop()
+    # the two launches separately (CUDA events around each, back to back)
+    qkv_only = timed(lambda l: L.qkv_proj_rope_append(qkv, x, wq[l], positions, qb, kb, vb, cos,
+                                                      sin, k_pool, v_pool, nb, 1, 0, hq, hkv, hd,
+                                                      tables, tokens_per_seq=1), args.steps)
+    peak, peak_kind = measured_peak()
+    value = wbytes / (ms * 1e-3) / 1e9
+    q_bytes = N * K * 2
+    q_gbs = q_bytes / (qkv_only * 1e-3) / 1e9
+    print(json.dumps({
+        "metric": "decode-step projection weight GB/s (QKV fused with bias + RoPE + append, "
+                  "o_proj with residual)",
+        "value": round(value, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded bf16 x ~N(0,1), w ~N(0,1/hidden))",
+        "config": {"workload": label, "batch": B, "qkv_n": N, "hidden": K,
+                   "layers_rotated": layers,
+                   "l2": "no flush: %d distinct weight sets, %.0f MB > 2 x 126 MB L2" %
+                         (layers, layers * wbytes / 1e6)},
+        "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(value / peak, 4), "peak_kind": f"{peak_kind} (burst copy)",
+                     "qkv_launch_ms": round(qkv_only, 5), "qkv_achieved": round(q_gbs, 1),
+                     "qkv_frac": round(q_gbs / peak, 4)},
+        "library_path": {"ms_per_layer": round(ms_lib, 5),
+                         "how": "torch.matmul (cublasGemmEx) + lc_rope_append; torch.matmul + "
+                                "residual add for o_proj"},
+        "speedup_vs_library": round(ms_lib / ms, 3),
+        "gpu_launches": 2 * args.steps * layers,
+        "clocks": clocks,
+    }), flush=True)
+
+
 # ------------------------------------------------------------ prefill (c4) --
 
 PREFILL = {"c4": ("qwen2.5-1.5b causal prefill into the paged cache (BASELINE config 4)",
@@ -1282,7 +1411,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(PREFILL) + sorted(HEAD_SHARDED) +
-                    sorted(PROJ) + sorted(SAMPLING),
+                    sorted(PROJ) + sorted(SAMPLING) + sorted(DECODE_PROJ),
                     default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mode", choices=["bench", "kernel"], default="bench",
@@ -1323,6 +1452,15 @@ def main():
     if args.config in SAMPLING:
         if rank == 0:
             run_sampling_bench(args, rank, world, local)
+        return 0
+    if args.config in DECODE_PROJ:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm is run on "
+                              "the decode headline (config 2); its projections are cuBLAS, timed "
+                              "beside ours in this config's library_path"}))
+            return 0
+        if rank == 0:
+            run_decode_proj_bench(args, rank, world, local)
         return 0
     if args.config in PROJ:
         if args.impl == "reference":

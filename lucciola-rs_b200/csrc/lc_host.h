@@ -46,6 +46,35 @@ int sm_count();
 // Process-wide programmatic-dependent-launch mode (lc_set_dependent_launch).
 int dependent_launch_mode();
 
+// The decode-step projection (proj_decode.cu): out[M][N] = x[M][K] . w[N][K]^T
+// for M <= kDecodeProjMaxRows token rows, with epilogue `epi` (0 plain,
+// 1 residual, 2 QKV with bias + RoPE + paged append: the fields after
+// res_stride then apply). Shapes and pointers are checked by the caller.
+constexpr int kDecodeProjMaxRows = 128;
+struct DecodeProjArgs {
+    int epi, M, N, K;
+    void *out;
+    int64_t out_stride;
+    const void *x;
+    int64_t x_stride;
+    const void *w;
+    int64_t w_stride;
+    const void *residual;
+    int64_t res_stride;
+    int tokens_per_seq;
+    const int *positions;
+    const void *q_bias, *k_bias, *v_bias;
+    const float *cos_t, *sin_t;
+    int rope_rows;
+    void *k_pool, *v_pool;
+    int64_t num_blocks;
+    int num_layers, layer, num_q_heads, num_kv_heads, head_dim;
+    const int *tables;
+    int table_stride;
+    int *status;
+};
+int decode_proj_launch(const DecodeProjArgs &a, cudaStream_t stream);
+
 }  // namespace lc
 
 // Peer exchange group (lc_peer_group_*): the ranks' exchange regions as this

@@ -1,0 +1,477 @@
+// proj_decode.cu - the projections either side of attention for a decode
+// step: out[M][N] = x[M][K] . w[N][K]^T with M <= 128 token rows (one row per
+// sequence of the batch), as Qwen2Model::matmul_bf16 computes them per token
+// (src/models.rs:252-292: cublasGemmEx, CUBLAS_COMPUTE_32F, bf16 C; qkv_proj at
+// :470-483, o_proj with beta 1 at :553-566). At this size the GEMM is bound by
+// reading the weights once (x is a few hundred KiB and stays in L2), so the
+// kernel is laid out to stream w over as many SMs as possible:
+//
+//  * The MMA's M dimension is the weights: a tile is 128 weight rows (output
+//    columns); the token rows are the MMA's N (padded to a multiple of 16).
+//    tcgen05.mma M128 x N(tokens) x K16, bf16 in, fp32 accumulate in TMEM.
+//  * A cluster of `split` CTAs (a power of two up to 8) shares one tile, CTA r
+//    taking the r-th slice of K: nt tiles x split CTAs cover the SMs.
+//  * Warp 0 streams the CTA's K slice with TMA (w box {64 x 128}, x box
+//    {64 x Mt}, 128-byte swizzle) into a 6-stage ring; the weight loads of the
+//    first stages are issued before the programmatic-dependency wait, the
+//    token rows (written by the preceding kernel) after it. Warp 1 issues the
+//    MMAs. Warps 2-5 move the CTA's partial tile from TMEM into its shared
+//    memory (the idle ring).
+//  * Cluster reduction over distributed shared memory: CTA r owns 64/split of
+//    the tile's 64 row pairs (row pair = dims d and d + head_dim/2 of a head,
+//    the pair RoPE rotates together) and sums them over the cluster's partials
+//    in rank order (the same order whatever the timing), then runs the
+//    epilogue on them.
+//
+// Epilogues (the arithmetic of proj_gemm.cu, element by element):
+//   plain     out = bf16(acc)
+//   residual  out = bf16(acc + residual)        (residual may be out itself)
+//   qkv rope  the QKV projection followed by what lc_rope_append does to its
+//             rows: rounded to bf16, bias added, q and k rotated and stored
+//             back, k appended rotated and v + bias appended to the pools.
+//
+// Every mbarrier wait is bounded (LC_DEV_TIMEOUT); every thread reaches both
+// cluster barriers on every path, so a CTA that gave up still releases the
+// others.
+#include <climits>
+
+#include "lc_common.cuh"
+#include "lc_host.h"
+#include "lc_tcgen05.cuh"
+#include "rope_math.cuh"
+
+namespace lc {
+namespace {
+
+constexpr int kPRows = 128;   // weight rows per tile (the MMA's M)
+constexpr int kPK = 64;       // K per stage: one 128-byte swizzle row
+constexpr int kPStages = 6;
+constexpr int kPThreads = 192;  // TMA warp, MMA warp, four epilogue warps
+constexpr int kPPairs = kPRows / 2;
+constexpr int kPMaxTokens = 128;
+constexpr uint32_t kPWTile = kPRows * kPK * 2;         // 16 KiB
+constexpr uint32_t kPXTileMax = kPMaxTokens * kPK * 2;  // 16 KiB
+constexpr uint32_t kPStageBytes = kPWTile + kPXTileMax;
+constexpr int kPSmem = kPStages * kPStageBytes + 1024;  // + 1024-byte alignment slack
+constexpr int kPMaxSplit = 8;
+constexpr uint32_t kPTmemCols = 128;
+
+enum DecEpilogue { kDecPlain = 0, kDecResidual = 1, kDecQkv = 2 };
+
+struct DecProjParams {
+    int M, N, K;
+    int Mt;       // token rows padded to a multiple of 16 (the MMA's N)
+    int split;    // CTAs per cluster (K slices)
+    int kblocks;  // K / 64, rounded up
+    int pdl_mode;
+    bf16 *out;
+    int64_t out_stride;
+    const bf16 *residual;
+    int64_t res_stride;
+    // qkv rope: token rows (row / tokens_per_seq = sequence), columns
+    // [q heads | k heads | v heads] of head_dim each.
+    int tokens_per_seq;
+    const int *positions;
+    const bf16 *q_bias, *k_bias, *v_bias;
+    const float *cos_t, *sin_t;
+    int rope_rows;
+    bf16 *k_pool, *v_pool;
+    int64_t num_blocks;
+    int num_layers, layer, num_q_heads, num_kv_heads, head_dim;
+    const int *tables;
+    int table_stride;
+    int *status;
+};
+
+// Staged partial tile: [128 weight rows][Mt + 4] fp32 (the padding spreads the
+// rows over the shared-memory banks).
+__device__ __forceinline__ int stage_pitch(int Mt) { return Mt + 4; }
+
+// Rows of pair p of a 128-row tile whose heads are HD wide: dims i and
+// i + HD/2 of head p / (HD/2), i = p % (HD/2).
+template <int HD>
+__device__ __forceinline__ void pair_rows(int p, int &ra, int &rb) {
+    constexpr int kHalf = HD / 2;
+    const int head = p / kHalf, i = p - head * kHalf;
+    ra = head * HD + i;
+    rb = ra + kHalf;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// bf16(acc) back as a float: the value the reference's qkv buffer holds.
+__device__ __forceinline__ float round_bf16_dec(float x) {
+    return __bfloat162float(__float2bfloat16(x));
+}
+
+// Pool offset of (position, kv head 0) for token row `row`, or -1 when it must
+// not be appended (status bits set), as rope_append.cu does.
+__device__ __forceinline__ int64_t dec_pool_base(const DecProjParams &p, int row, int pos) {
+    const int b = row / p.tokens_per_seq;
+    const int logical = pos / kBlockSize;
+    if (logical >= p.table_stride) {
+        set_status(p.status, LC_DEV_BAD_POS);
+        return -1;
+    }
+    const int phys = p.tables[(int64_t)b * p.table_stride + logical];
+    if (phys < 0 || phys >= p.num_blocks) {
+        set_status(p.status, LC_DEV_BAD_BLOCK);
+        return -1;
+    }
+    return page_row(phys, p.layer, 0, p.num_layers, p.num_kv_heads) * p.head_dim +
+           (int64_t)(pos % kBlockSize) * p.head_dim;
+}
+
+// Plain / residual epilogue of one output element (token row m, column col).
+template <int EPI>
+__device__ __forceinline__ void dec_store_plain(const DecProjParams &p, int m, int col, float acc) {
+    if (col >= p.N) return;
+    float f = acc;
+    if constexpr (EPI == kDecResidual)
+        f = __fadd_rn(acc, __bfloat162float(p.residual[(int64_t)m * p.res_stride + col]));
+    p.out[(int64_t)m * p.out_stride + col] = __float2bfloat16(f);
+}
+
+// QKV epilogue of one row pair (token row m, columns col and col + HD/2 of
+// one head): what epilogue_qkv in proj_gemm.cu does per element, i.e.
+// rope_append_vec_kernel's arithmetic on the bf16-rounded projection. The row
+// keeps the projection where rope_append leaves it (v, a negative position, a
+// position past the RoPE table).
+template <int HD>
+__device__ __forceinline__ void dec_store_qkv(const DecProjParams &p, int m, int col, float acc_a,
+                                              float acc_b) {
+    constexpr int kHalf = HD / 2;
+    if (col >= p.N) return;
+    const int hq = p.num_q_heads, hkv = p.num_kv_heads;
+    const int g = col / HD, d = col - g * HD;  // head over [q | k | v], dim < HD/2
+    const int kind = g < hq ? 0 : (g < hq + hkv ? 1 : 2);
+    const int pos = p.positions[m];
+    if (pos < 0 || pos >= p.rope_rows) set_status(p.status, LC_DEV_BAD_POS);
+    const bool rope_ok = pos >= 0 && pos < p.rope_rows;
+    float x1 = round_bf16_dec(acc_a), x2 = round_bf16_dec(acc_b);
+    const int64_t base = pos >= 0 && kind != 0 ? dec_pool_base(p, m, pos) : -1;
+    if (pos >= 0 && kind != 2 && rope_ok) {
+        const int hh = kind == 0 ? g : g - hq;
+        const bf16 *bias = (kind == 0 ? p.q_bias : p.k_bias) + hh * HD;
+        const float c = p.cos_t[(int64_t)pos * kHalf + d], s = p.sin_t[(int64_t)pos * kHalf + d];
+        const float v1 = __fadd_rn(x1, __bfloat162float(bias[d]));
+        const float v2 = __fadd_rn(x2, __bfloat162float(bias[d + kHalf]));
+        x1 = rot_sub(v1, c, v2, s);
+        x2 = rot_add(v1, s, v2, c);
+    }
+    bf16 *orow = p.out + (int64_t)m * p.out_stride;
+    orow[col] = __float2bfloat16(x1);
+    orow[col + kHalf] = __float2bfloat16(x2);
+    if (pos >= 0 && base >= 0) {
+        const int64_t stride_blk = (int64_t)kBlockSize * HD;
+        if (kind == 1 && rope_ok) {  // past the RoPE table k is not appended, v still is
+            bf16 *dst = p.k_pool + base + (g - hq) * stride_blk;
+            dst[d] = __float2bfloat16(x1);
+            dst[d + kHalf] = __float2bfloat16(x2);
+        } else if (kind == 2) {
+            const int vh = g - hq - hkv;
+            const bf16 *vb = p.v_bias + vh * HD;
+            bf16 *dst = p.v_pool + base + vh * stride_blk;
+            dst[d] = __float2bfloat16(__fadd_rn(x1, __bfloat162float(vb[d])));
+            dst[d + kHalf] = __float2bfloat16(__fadd_rn(x2, __bfloat162float(vb[d + kHalf])));
+        }
+    }
+}
+
+template <int EPI, int HD>
+__global__ void __launch_bounds__(kPThreads, 1)
+    proj_decode_kernel(const __grid_constant__ CUtensorMap tm_w,
+                       const __grid_constant__ CUtensorMap tm_x, const DecProjParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *gen = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t full[kPStages];
+    __shared__ __align__(8) uint64_t empty[kPStages];
+    __shared__ __align__(8) uint64_t acc_full;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ int s_abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rank = (int)cluster_ctarank();
+    const int tile = (int)blockIdx.x / p.split;
+    const int kb0 = rank * p.kblocks / p.split, kb1 = (rank + 1) * p.kblocks / p.split;
+    const int nkb = kb1 - kb0;
+    const uint32_t xbytes = (uint32_t)p.Mt * kPK * 2;
+    const uint32_t idesc = idesc_bf16_f32(kPRows, p.Mt, 0);
+
+    griddep_launch_dependents();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&acc_full, 1);
+        s_abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(&tmem_base_sh, kPTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_sh;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA --
+        if (lane == 0) {
+            prefetch_tensormap(&tm_w);
+            prefetch_tensormap(&tm_x);
+            // The first stages' weights depend on no earlier kernel: they stream
+            // while the preceding grid drains; the token rows come after it.
+            const int pre = min(nkb, kPStages);
+            for (int i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&full[i], kPWTile + xbytes);
+                tma_load_2d(gen + i * kPStageBytes, &tm_w, (kb0 + i) * kPK, tile * kPRows, &full[i]);
+            }
+            if (p.pdl_mode) griddep_wait();
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d(gen + i * kPStageBytes + kPWTile, &tm_x, (kb0 + i) * kPK, 0, &full[i]);
+            int it = pre;
+            bool ok = true;
+            for (; it < nkb; ++it) {
+                const int s = it % kPStages;
+                if (!mbar_wait_bounded(&empty[s], ((it / kPStages) - 1) & 1, &s_abort, p.status)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *st = gen + s * kPStageBytes;
+                mbar_arrive_expect_tx(&full[s], kPWTile + xbytes);
+                tma_load_2d(st, &tm_w, (kb0 + it) * kPK, tile * kPRows, &full[s]);
+                tma_load_2d(st + kPWTile, &tm_x, (kb0 + it) * kPK, 0, &full[s]);
+            }
+            if (!ok) {  // let the copies in flight land before the CTA moves on
+                for (int k = it - kPStages; k < it; ++k)
+                    if (k >= 0) mbar_wait_drain(&full[k % kPStages], (k / kPStages) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA --
+        if (lane == 0) {
+            bool ok = true;
+            for (int it = 0; it < nkb; ++it) {
+                const int s = it % kPStages;
+                if (!mbar_wait_bounded(&full[s], (it / kPStages) & 1, &s_abort, p.status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(gen + s * kPStageBytes), b = a + kPWTile;
+#pragma unroll
+                for (int kk = 0; kk < kPK / 16; ++kk)
+                    umma_bf16(tmem, sw128_desc(a + kk * 32, 16, 1024),
+                              sw128_desc(b + kk * 32, 16, 1024), idesc,
+                              (it > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&empty[s]);  // the stage is free once these MMAs are done
+            }
+            if (ok && nkb > 0) umma_commit(&acc_full);
+        }
+    } else {
+        // ------------------------------- partial tile: TMEM -> shared memory --
+        // The ring is idle once the accumulator is complete (every stage's
+        // MMAs have read it); it holds the staged tile [128][Mt + 4] fp32.
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        float *stg = reinterpret_cast<float *>(gen);
+        const int pitch = stage_pitch(p.Mt);
+        bool have = nkb > 0 && mbar_wait_bounded(&acc_full, 0, &s_abort, p.status);
+        have = __all_sync(0xffffffffu, have);
+        tc_fence_after();
+        for (int c0 = 0; c0 < p.Mt; c0 += 32) {
+            uint32_t r[32];
+            if (have) {
+                tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, r);
+                tmem_wait_ld_regs(r);
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (c0 + i < p.Mt) stg[row * pitch + c0 + i] = have ? __uint_as_float(r[i]) : 0.f;
+        }
+    }
+    // Every CTA's staged tile is complete and visible to the cluster.
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();
+
+    if (warp >= 2 && !s_abort) {
+        // ------------------------- reduction over the cluster + epilogue --
+        if (p.pdl_mode) griddep_wait();  // outputs / pools after the preceding kernel
+        const int et = threadIdx.x - 64;
+        const int npr = kPPairs / p.split;  // row pairs this CTA finishes
+        const int pr0 = rank * npr;
+        const int pitch = stage_pitch(p.Mt);
+        const uint32_t stg = smem_u32(gen);
+        uint32_t peer[kPMaxSplit];
+#pragma unroll
+        for (int r = 0; r < kPMaxSplit; ++r) peer[r] = r < p.split ? mapa_shared(stg, r) : 0u;
+        const int items = p.M * npr;
+        for (int item = et; item < items; item += 128) {
+            const int m = item / npr, pl = item - m * npr;  // neighbouring threads: neighbouring pairs
+            int ra, rb;
+            pair_rows<EPI == kDecQkv ? HD : 128>(pr0 + pl, ra, rb);
+            float va[kPMaxSplit], vb[kPMaxSplit];
+#pragma unroll
+            for (int r = 0; r < kPMaxSplit; ++r) {
+                if (r < p.split) {
+                    va[r] = ld_dsmem_f32(peer[r] + (uint32_t)(ra * pitch + m) * 4u);
+                    vb[r] = ld_dsmem_f32(peer[r] + (uint32_t)(rb * pitch + m) * 4u);
+                }
+            }
+            float a = 0.f, b = 0.f;  // rank order: the same sum whatever the timing
+#pragma unroll
+            for (int r = 0; r < kPMaxSplit; ++r) {
+                if (r < p.split) {
+                    a += va[r];
+                    b += vb[r];
+                }
+            }
+            const int col = tile * kPRows + ra, colb = tile * kPRows + rb;
+            if constexpr (EPI == kDecQkv) {
+                dec_store_qkv<HD>(p, m, col, a, b);
+            } else {
+                dec_store_plain<EPI>(p, m, col, a);
+                dec_store_plain<EPI>(p, m, colb, b);
+            }
+        }
+    }
+    // No CTA leaves while another may still read its staged tile.
+    __syncwarp();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kPTmemCols);
+    }
+}
+
+// Clusters of `split` CTAs (one CTA per SM: the ring takes most of shared
+// memory) that the device runs at once, per split; cached per device.
+template <int EPI, int HD>
+int max_clusters(int split) {
+    static int cached[64][4] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 0;
+    }
+    const int idx = split == 1 ? 0 : split == 2 ? 1 : split == 4 ? 2 : 3;
+    if (!cached[dev][idx]) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(split);
+        cfg.blockDim = dim3(kPThreads);
+        cfg.dynamicSmemBytes = kPSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = split;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, proj_decode_kernel<EPI, HD>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        cached[dev][idx] = n > 0 ? n : -1;
+    }
+    return cached[dev][idx] > 0 ? cached[dev][idx] : 0;
+}
+
+template <int EPI, int HD>
+int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const void *w,
+                       int64_t w_stride, cudaStream_t stream) {
+    auto kern = proj_decode_kernel<EPI, HD>;
+    int rc = ensure_smem_attr((const void *)kern, kPSmem);
+    if (rc) return rc;
+    const int n_tiles = (prm.N + kPRows - 1) / kPRows;
+    // The widest K split (a power of two, at most 8 and at most the number of
+    // 64-wide K blocks) whose clusters all fit on the device at once.
+    int split = 1;
+    for (int s = kPMaxSplit; s > 1; s >>= 1) {
+        if (s > prm.kblocks) continue;
+        const int fit = max_clusters<EPI, HD>(s);
+        if (fit >= n_tiles) {
+            split = s;
+            break;
+        }
+    }
+    prm.split = split;
+    CUtensorMap tw, tx;
+    rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kPK, kPRows, &tw);
+    if (rc) return rc;
+    rc = tensor_map_2d_sw128(x, prm.K, prm.M, x_stride * 2, kPK, prm.Mt, &tx);
+    if (rc) return rc;
+    const int mode = dependent_launch_mode();
+    prm.pdl_mode = mode;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_tiles * split);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = kPSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = split;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = mode > 0 ? 2 : 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tw, tx, prm) != cudaSuccess) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    return LC_OK;
+}
+
+}  // namespace
+
+int decode_proj_launch(const DecodeProjArgs &a, cudaStream_t stream) {
+    if (a.M <= 0 || a.M > kDecodeProjMaxRows || a.K <= 0 || a.N <= 0) return LC_ERR_INVALID_ARGUMENT;
+    DecProjParams p{};
+    p.M = a.M;
+    p.N = a.N;
+    p.K = a.K;
+    p.Mt = (a.M + 15) & ~15;
+    p.kblocks = (a.K + kPK - 1) / kPK;
+    p.out = (bf16 *)a.out;
+    p.out_stride = a.out_stride;
+    p.residual = (const bf16 *)a.residual;
+    p.res_stride = a.res_stride;
+    p.tokens_per_seq = a.tokens_per_seq;
+    p.positions = a.positions;
+    p.q_bias = (const bf16 *)a.q_bias;
+    p.k_bias = (const bf16 *)a.k_bias;
+    p.v_bias = (const bf16 *)a.v_bias;
+    p.cos_t = a.cos_t;
+    p.sin_t = a.sin_t;
+    p.rope_rows = a.rope_rows;
+    p.k_pool = (bf16 *)a.k_pool;
+    p.v_pool = (bf16 *)a.v_pool;
+    p.num_blocks = a.num_blocks;
+    p.num_layers = a.num_layers;
+    p.layer = a.layer;
+    p.num_q_heads = a.num_q_heads;
+    p.num_kv_heads = a.num_kv_heads;
+    p.head_dim = a.head_dim;
+    p.tables = a.tables;
+    p.table_stride = a.table_stride;
+    p.status = a.status;
+    if (a.epi == kDecQkv)
+        return a.head_dim == 64
+                   ? launch_decode_proj<kDecQkv, 64>(p, a.x, a.x_stride, a.w, a.w_stride, stream)
+                   : launch_decode_proj<kDecQkv, 128>(p, a.x, a.x_stride, a.w, a.w_stride, stream);
+    if (a.epi == kDecResidual)
+        return launch_decode_proj<kDecResidual, 128>(p, a.x, a.x_stride, a.w, a.w_stride, stream);
+    return launch_decode_proj<kDecPlain, 128>(p, a.x, a.x_stride, a.w, a.w_stride, stream);
+}
+
+}  // namespace lc

@@ -12,16 +12,18 @@
 //             rotated and v + bias appended to the paged pools. The result is
 //             bit-identical to lc_proj_gemm then lc_rope_append.
 //
-// Design: a persistent grid of one CTA per SM walks 128 x 256 output tiles
-// (the 256 columns of a tile hold whole heads: head_dim 64 or 128). Warp 0
-// issues TMA loads of 64-wide K blocks (x tile {64 x 128}, w tile {64 x 256},
-// 128-byte swizzle) into a 4-stage ring; warp 1 issues tcgen05.mma
-// (M 128, N 256, K 16, bf16 in, fp32 accumulate) into one of two 256-column
-// TMEM accumulators; warps 2-9 (one output row per thread of a TMEM lane
-// quadrant) drain the other accumulator through the epilogue while the next
-// tile accumulates (two warps per quadrant, each taking every other 32-column
-// chunk or head, so that one warp's loads overlap the other's arithmetic).
-// Every wait is bounded; a timeout sets LC_DEV_TIMEOUT.
+// Design (M > 128 token rows, a prompt): a persistent grid of CTA pairs walks
+// 256 x 256 output tiles (the 256 columns of a tile hold whole heads:
+// head_dim 64 or 128); see the CTA-pair section below. A decode step's
+// M <= 128 rows go to the weight-streaming kernel of proj_decode.cu. In the
+// pair kernel warp 0 issues TMA loads of 64-wide K blocks (128-byte swizzle)
+// into the stage ring; warp 1 issues tcgen05.mma (bf16 in, fp32 accumulate)
+// into one of two 256-column TMEM accumulators; warps 2-9 (one output row per
+// thread of a TMEM lane quadrant) drain the other accumulator through the
+// epilogue while the next tile accumulates (two warps per quadrant, each
+// taking every other 32-column chunk or head, so that one warp's loads
+// overlap the other's arithmetic). Every wait is bounded; a timeout sets
+// LC_DEV_TIMEOUT.
 #include <climits>
 
 #include "lc_common.cuh"
@@ -118,23 +120,9 @@ __device__ __forceinline__ int64_t pool_base(const GemmParams &p, int row, int p
            (int64_t)(pos % kBlockSize) * p.head_dim;
 }
 
-// Output of the epilogue warps. Direct: each thread stores its row's 32
-// values (the 1-SM kernel). Staged (CTA pairs): the warp's 32 rows x 32
-// columns go to shared memory (64-byte rows, 64-byte swizzle as the output
+// Output of the epilogue warps: the warp's 32 rows x 32 columns go to shared memory (64-byte rows, 64-byte swizzle as the output
 // tensor map has it) and lane 0 writes them with one TMA store per box; two
 // buffers of two boxes per warp, so a step's stores overlap the next step.
-struct OutDirect {
-    bf16 *out;
-    int64_t stride;
-    __device__ __forceinline__ void begin() {}
-    __device__ __forceinline__ void put(int row, bool live, int col, int box, const float (&f)[32]) {
-        (void)box;
-        if (live) store32(out + (int64_t)row * stride + col, f);
-    }
-    __device__ __forceinline__ void issue(int, int, int, int, bool) {}
-    __device__ __forceinline__ void drain() {}
-};
-
 struct OutStaged {
     uint8_t *base;  // this warp's 8 KiB, 2 KiB aligned
     const CUtensorMap *map;
@@ -349,141 +337,6 @@ __device__ __forceinline__ void epilogue_qkv(const GemmParams &p, uint32_t tacc,
     }
 }
 
-template <int EPI, int HD>
-__global__ void __launch_bounds__(kThreadsG, 1)
-    proj_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
-                     const __grid_constant__ CUtensorMap tm_b, const GemmParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *gen = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t full[kStagesG];
-    __shared__ __align__(8) uint64_t empty[kStagesG];
-    __shared__ __align__(8) uint64_t acc_full[2];
-    __shared__ __align__(8) uint64_t acc_empty[2];
-    __shared__ uint32_t tmem_base_sh;
-    __shared__ int s_abort;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStagesG; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 32 * kEpiWarps);
-        }
-        s_abort = 0;
-        fence_barrier_init();
-    }
-    if (warp == 1) {
-        tmem_alloc(&tmem_base_sh, kTmemColsG);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = tmem_base_sh;
-    const int tiles = p.m_tiles * p.n_tiles;
-    const int kblocks = (p.K + kBK - 1) / kBK;
-
-    if (warp == 0) {
-        // ---------------------------------------------------------------- TMA --
-        if (lane == 0) {
-            prefetch_tensormap(&tm_a);
-            prefetch_tensormap(&tm_b);
-            int it = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
-                    const int s = it % kStagesG;
-                    if (it >= kStagesG &&
-                        !mbar_wait_bounded(&empty[s], ((it / kStagesG) - 1) & 1, &s_abort, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *st = gen + s * kStageBytesG;
-                    mbar_arrive_expect_tx(&full[s], kStageBytesG);
-                    tma_load_2d(st, &tm_a, kb * kBK, mt * kBM, &full[s]);
-                    tma_load_2d(st + kATile, &tm_b, kb * kBK, nt * kBN, &full[s]);
-                }
-            }
-            if (!ok) {
-                // let the copies in flight land before the CTA exits
-                for (int k = it - kStagesG; k < it; ++k)
-                    if (k >= 0) mbar_wait_drain(&full[k % kStagesG], (k / kStagesG) & 1);
-            }
-        }
-    } else if (warp == 1) {
-        // ---------------------------------------------------------------- MMA --
-        if (lane == 0) {
-            int it = 0, tl = 0;
-            bool ok = true;
-            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++tl) {
-                const int buf = tl & 1;
-                if (tl >= 2 &&
-                    !mbar_wait_bounded(&acc_empty[buf], ((tl >> 1) - 1) & 1, &s_abort, p.status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem + buf * kBN;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
-                    const int s = it % kStagesG;
-                    if (!mbar_wait_bounded(&full[s], (it / kStagesG) & 1, &s_abort, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a = smem_u32(gen + s * kStageBytesG), b = a + kATile;
-#pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk)
-                        umma_bf16(d, sw128_desc(a + kk * 32, 16, 1024),
-                                  sw128_desc(b + kk * 32, 16, 1024), kIdescG,
-                                  (kb > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(&empty[s]);  // the stage is free once these MMAs are done
-                }
-                if (ok) umma_commit(&acc_full[buf]);
-            }
-        }
-    } else {
-        // ----------------------------------------------------------- epilogue --
-        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
-        const int half = (warp - 2) >> 2;
-        const int r = quad * 32 + lane;
-        int tl = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tl) {
-            const int buf = tl & 1;
-            const int mt = tile / p.n_tiles, nt = tile - mt * p.n_tiles;
-            const int row = mt * kBM + r, col0 = nt * kBN;
-            const uint32_t tacc = tmem + ((uint32_t)(quad * 32) << 16) + buf * kBN;
-            OutDirect o{p.out, p.out_stride};
-            const int y = mt * kBM + quad * 32;
-            if constexpr (EPI == kQkvRope) {
-                QkvRow<HD> w;
-                w.load(p, row, col0, half);  // overlaps the tile's MMAs
-                if (!mbar_wait_bounded(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status)) break;
-                tc_fence_after();
-                epilogue_qkv<HD>(p, tacc, row, y, col0, half, w, o);
-            } else {
-                if (!mbar_wait_bounded(&acc_full[buf], (tl >> 1) & 1, &s_abort, p.status)) break;
-                tc_fence_after();
-                epilogue_rows<EPI>(p, tacc, row, y, col0, half, o);
-            }
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem, kTmemColsG);
-    }
-}
-
-
 // ------------------------------------------------------------ CTA pairs --
 // The same GEMM over 256 x 256 tiles shared by a cluster of two CTAs
 // (tcgen05.mma.cta_group::2): CTA r loads rows [128 r, 128 r + 128) of the
@@ -642,22 +495,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsG, 1)
     }
 }
 
-template <int EPI, int HD>
-int launch_gemm(const GemmParams &prm, const void *x, int64_t x_stride, const void *w,
-                int64_t w_stride, cudaStream_t stream) {
-    CUtensorMap ma, mb;
-    int rc = tensor_map_2d_sw128(x, prm.K, prm.M, x_stride * 2, kBK, kBM, &ma);
-    if (rc) return rc;
-    rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kBK, kBN, &mb);
-    if (rc) return rc;
-    rc = ensure_smem_attr((const void *)proj_gemm_kernel<EPI, HD>, kSmemG);
-    if (rc) return rc;
-    const int tiles = prm.m_tiles * prm.n_tiles;
-    const int grid = tiles < sm_count() ? tiles : sm_count();
-    proj_gemm_kernel<EPI, HD><<<grid, kThreadsG, kSmemG, stream>>>(ma, mb, prm);
-    return launch_status();
-}
-
 // Clusters of two that fit on the current device at once (cached per device).
 template <int EPI, int HD>
 int pair_slots() {
@@ -704,11 +541,45 @@ int launch_gemm2(GemmParams prm, const void *x, int64_t x_stride, const void *w,
     return launch_status();
 }
 
+// M <= 128 token rows (a decode step): the weight-streaming kernel of
+// proj_decode.cu; more rows: 256 x 256 tiles on CTA pairs.
 template <int EPI, int HD>
 int launch_any(const GemmParams &prm, const void *x, int64_t x_stride, const void *w,
                int64_t w_stride, cudaStream_t stream) {
-    return prm.M > kBM ? launch_gemm2<EPI, HD>(prm, x, x_stride, w, w_stride, stream)
-                       : launch_gemm<EPI, HD>(prm, x, x_stride, w, w_stride, stream);
+    if (prm.M > kDecodeProjMaxRows) return launch_gemm2<EPI, HD>(prm, x, x_stride, w, w_stride, stream);
+    DecodeProjArgs a{};
+    a.epi = EPI;  // kPlain / kResidual / kQkvRope: the decode kernel's numbering
+    a.M = prm.M;
+    a.N = prm.N;
+    a.K = prm.K;
+    a.out = prm.out;
+    a.out_stride = prm.out_stride;
+    a.x = x;
+    a.x_stride = x_stride;
+    a.w = w;
+    a.w_stride = w_stride;
+    a.residual = prm.residual;
+    a.res_stride = prm.res_stride;
+    a.tokens_per_seq = prm.tokens_per_seq;
+    a.positions = prm.positions;
+    a.q_bias = prm.q_bias;
+    a.k_bias = prm.k_bias;
+    a.v_bias = prm.v_bias;
+    a.cos_t = prm.cos_t;
+    a.sin_t = prm.sin_t;
+    a.rope_rows = prm.rope_rows;
+    a.k_pool = prm.k_pool;
+    a.v_pool = prm.v_pool;
+    a.num_blocks = prm.num_blocks;
+    a.num_layers = prm.num_layers;
+    a.layer = prm.layer;
+    a.num_q_heads = prm.num_q_heads;
+    a.num_kv_heads = prm.num_kv_heads;
+    a.head_dim = prm.head_dim;
+    a.tables = prm.tables;
+    a.table_stride = prm.table_stride;
+    a.status = prm.status;
+    return decode_proj_launch(a, stream);
 }
 
 int check_gemm_shape(const void *out, int64_t out_stride, const void *x, int64_t x_stride,

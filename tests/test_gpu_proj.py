@@ -36,6 +36,14 @@ def _check_gemm(out, ref, K):
     (1, 896, 896),       # a single row (decode shape of o_proj)
     (517, 2048, 1536),   # Qwen2.5-1.5B qkv_proj, ragged M
     (70, 96, 200),       # N and K tails (partial tile, K not a multiple of 64)
+    # decode steps (M = batch <= 128: the weight-streaming kernel, K split
+    # over a cluster): Qwen2.5-0.5B at batch 64, Qwen2.5-7B at batch 32
+    (64, 1152, 896),     # 0.5B qkv_proj
+    (64, 896, 896),      # 0.5B o_proj
+    (32, 4608, 3584),    # 7B qkv_proj
+    (32, 3584, 3584),    # 7B o_proj
+    (128, 2048, 1536),   # 1.5B qkv_proj, the largest decode batch
+    (17, 4608, 3584),    # a batch that is not a multiple of 16
 ])
 def test_proj_gemm_matches_float64(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
@@ -47,10 +55,10 @@ def test_proj_gemm_matches_float64(M, N, K):
     _check_gemm(out, _gemm_ref(x, w), K)
 
 
-def test_proj_gemm_residual_in_place():
+@pytest.mark.parametrize("M,N,K", [(200, 896, 896), (64, 896, 896), (32, 3584, 3584)])
+def test_proj_gemm_residual_in_place(M, N, K):
     """o_proj with beta 1: hidden = bf16(attn . w_o^T + hidden), in place."""
-    M, N, K = 200, 896, 896
-    g = torch.Generator(device="cuda").manual_seed(3)
+    g = torch.Generator(device="cuda").manual_seed(3 + M)
     x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
     w = (torch.randn(N, K, generator=g, device="cuda") * K ** -0.5).to(torch.bfloat16)
     hidden = torch.randn(M, N, generator=g, device="cuda").to(torch.bfloat16)
@@ -108,6 +116,10 @@ def _qkv_case(hq, hkv, hd, hidden, T, start, seed, bad_block=False, past_rope=Fa
     (28, 4, 128, 3584, 70, [100, 0, 5], {}),                   # Qwen2.5-7B
     (14, 2, 64, 896, 40, [0, 0], {"bad_block": True}),         # a table entry outside the pool
     (14, 2, 64, 896, 20, [0], {"past_rope": True}),            # a position past the RoPE table
+    # decode steps: one new token per sequence (the weight-streaming kernel)
+    (14, 2, 64, 896, 1, list(range(7, 4000, 63))[:64], {}),    # 0.5B, batch 64
+    (28, 4, 128, 3584, 1, list(range(11, 4000, 125))[:32], {}),  # 7B, batch 32
+    (12, 2, 128, 1536, 1, list(range(0, 3900, 31))[:125], {}),  # 1.5B, batch 125
 ])
 def test_qkv_proj_rope_append_equals_gemm_then_rope_append(hq, hkv, hd, hidden, T, start, flags):
     case, x, w, bias, rope, pos, tables = _qkv_case(hq, hkv, hd, hidden, T, start,
