@@ -385,6 +385,17 @@ int max_clusters(int split) {
     return cached[dev][idx] > 0 ? cached[dev][idx] : 0;
 }
 
+// The widest K split (a power of two, at most 8 and at most the number of
+// 64-wide K blocks) whose clusters all fit on the device at once.
+template <int EPI, int HD>
+int choose_split(int n_tiles, int kblocks) {
+    for (int s = kPMaxSplit; s > 1; s >>= 1) {
+        if (s > kblocks) continue;
+        if (max_clusters<EPI, HD>(s) >= n_tiles) return s;
+    }
+    return 1;
+}
+
 template <int EPI, int HD>
 int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const void *w,
                        int64_t w_stride, cudaStream_t stream) {
@@ -392,17 +403,7 @@ int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const
     int rc = ensure_smem_attr((const void *)kern, kPSmem);
     if (rc) return rc;
     const int n_tiles = (prm.N + kPRows - 1) / kPRows;
-    // The widest K split (a power of two, at most 8 and at most the number of
-    // 64-wide K blocks) whose clusters all fit on the device at once.
-    int split = 1;
-    for (int s = kPMaxSplit; s > 1; s >>= 1) {
-        if (s > prm.kblocks) continue;
-        const int fit = max_clusters<EPI, HD>(s);
-        if (fit >= n_tiles) {
-            split = s;
-            break;
-        }
-    }
+    const int split = choose_split<EPI, HD>(n_tiles, prm.kblocks);
     prm.split = split;
     CUtensorMap tw, tx;
     rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kPK, kPRows, &tw);
@@ -475,3 +476,16 @@ int decode_proj_launch(const DecodeProjArgs &a, cudaStream_t stream) {
 }
 
 }  // namespace lc
+
+using namespace lc;
+
+extern "C" int lc_proj_decode_plan(int N, int K, int *split, int *ctas, int *clusters_that_fit) {
+    if (N <= 0 || K <= 0 || !split || !ctas) return LC_ERR_INVALID_ARGUMENT;
+    int rc = ensure_smem_attr((const void *)proj_decode_kernel<kDecPlain, 128>, kPSmem);
+    if (rc) return rc;
+    const int n_tiles = (N + kPRows - 1) / kPRows;
+    *split = choose_split<kDecPlain, 128>(n_tiles, (K + kPK - 1) / kPK);
+    *ctas = n_tiles * *split;
+    if (clusters_that_fit) *clusters_that_fit = max_clusters<kDecPlain, 128>(*split);
+    return LC_OK;
+}

@@ -52,6 +52,7 @@ SIGNATURES = {
     "lc_paged_decode_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                       _i32, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32,
                                       _vp, _vp]),
+    "lc_proj_decode_plan": (_i32, [_i32, _i32, _pi32, _pi32, _pi32]),
     "lc_paged_prefill": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                 _i32, _vp, _i32, _vp, _i32, _i32, _i32, _f32, _vp, _vp]),
     "lc_gather_kv": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp,
@@ -550,6 +551,14 @@ class BlockAlloc:
             self.close()
         except Exception:
             pass
+
+
+def proj_decode_plan(n, k):
+    """(split, ctas, clusters_that_fit) of the decode-step projection kernel."""
+    a, b, c = C.c_int(), C.c_int(), C.c_int()
+    check(lib.lc_proj_decode_plan(n, k, C.byref(a), C.byref(b), C.byref(c)),
+          "lc_proj_decode_plan")
+    return a.value, b.value, c.value
 
 
 def proj_gemm(out, x, w, residual=None, stream=None):
