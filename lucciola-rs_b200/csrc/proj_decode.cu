@@ -12,7 +12,8 @@
 //  * A cluster of `split` CTAs (a power of two up to 8) shares one tile, CTA r
 //    taking the r-th slice of K: nt tiles x split CTAs cover the SMs.
 //  * Warp 0 streams the CTA's K slice with TMA (w box {64 x 128}, x box
-//    {64 x Mt}, 128-byte swizzle) into a 6-stage ring; the weight loads of the
+//    {64 x Mt}, 128-byte swizzle) into a 96 KiB ring (3-6 stages, two CTAs
+//    per SM); the weight loads of the
 //    first stages are issued before the programmatic-dependency wait, the
 //    token rows (written by the preceding kernel) after it. Warp 1 issues the
 //    MMAs. Warps 2-5 move the CTA's partial tile from TMEM into its shared
@@ -45,14 +46,12 @@ namespace {
 
 constexpr int kPRows = 128;   // weight rows per tile (the MMA's M)
 constexpr int kPK = 64;       // K per stage: one 128-byte swizzle row
-constexpr int kPStages = 6;
+constexpr int kPMaxStages = 6;
+constexpr uint32_t kPRingBytes = 96 * 1024;  // two CTAs per SM
 constexpr int kPThreads = 192;  // TMA warp, MMA warp, four epilogue warps
 constexpr int kPPairs = kPRows / 2;
-constexpr int kPMaxTokens = 128;
 constexpr uint32_t kPWTile = kPRows * kPK * 2;         // 16 KiB
-constexpr uint32_t kPXTileMax = kPMaxTokens * kPK * 2;  // 16 KiB
-constexpr uint32_t kPStageBytes = kPWTile + kPXTileMax;
-constexpr int kPSmem = kPStages * kPStageBytes + 1024;  // + 1024-byte alignment slack
+constexpr int kPSmem = kPRingBytes + 1024;  // + 1024-byte alignment slack
 constexpr int kPMaxSplit = 8;
 constexpr uint32_t kPTmemCols = 128;
 
@@ -62,6 +61,8 @@ struct DecProjParams {
     int M, N, K;
     int Mt;       // token rows padded to a multiple of 16 (the MMA's N)
     int split;    // CTAs per cluster (K slices)
+    int stages;   // ring stages of (w tile + x tile) that fit kPRingBytes
+    uint32_t stage_bytes;
     int kblocks;  // K / 64, rounded up
     int pdl_mode;
     bf16 *out;
@@ -183,14 +184,14 @@ __device__ __forceinline__ void dec_store_qkv(const DecProjParams &p, int m, int
 }
 
 template <int EPI, int HD>
-__global__ void __launch_bounds__(kPThreads, 1)
+__global__ void __launch_bounds__(kPThreads, 2)
     proj_decode_kernel(const __grid_constant__ CUtensorMap tm_w,
                        const __grid_constant__ CUtensorMap tm_x, const DecProjParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *gen = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t full[kPStages];
-    __shared__ __align__(8) uint64_t empty[kPStages];
+    __shared__ __align__(8) uint64_t full[kPMaxStages];
+    __shared__ __align__(8) uint64_t empty[kPMaxStages];
     __shared__ __align__(8) uint64_t acc_full;
     __shared__ uint32_t tmem_base_sh;
     __shared__ int s_abort;
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
     griddep_launch_dependents();
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kPStages; ++s) {
+        for (int s = 0; s < p.stages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -228,30 +229,30 @@ __global__ void __launch_bounds__(kPThreads, 1)
             prefetch_tensormap(&tm_x);
             // The first stages' weights depend on no earlier kernel: they stream
             // while the preceding grid drains; the token rows come after it.
-            const int pre = min(nkb, kPStages);
+            const int pre = min(nkb, p.stages);
             for (int i = 0; i < pre; ++i) {
                 mbar_arrive_expect_tx(&full[i], kPWTile + xbytes);
-                tma_load_2d(gen + i * kPStageBytes, &tm_w, (kb0 + i) * kPK, tile * kPRows, &full[i]);
+                tma_load_2d(gen + i * p.stage_bytes, &tm_w, (kb0 + i) * kPK, tile * kPRows, &full[i]);
             }
             if (p.pdl_mode) griddep_wait();
             for (int i = 0; i < pre; ++i)
-                tma_load_2d(gen + i * kPStageBytes + kPWTile, &tm_x, (kb0 + i) * kPK, 0, &full[i]);
+                tma_load_2d(gen + i * p.stage_bytes + kPWTile, &tm_x, (kb0 + i) * kPK, 0, &full[i]);
             int it = pre;
             bool ok = true;
             for (; it < nkb; ++it) {
-                const int s = it % kPStages;
-                if (!mbar_wait_bounded(&empty[s], ((it / kPStages) - 1) & 1, &s_abort, p.status)) {
+                const int s = it % p.stages;
+                if (!mbar_wait_bounded(&empty[s], ((it / p.stages) - 1) & 1, &s_abort, p.status)) {
                     ok = false;
                     break;
                 }
-                uint8_t *st = gen + s * kPStageBytes;
+                uint8_t *st = gen + s * p.stage_bytes;
                 mbar_arrive_expect_tx(&full[s], kPWTile + xbytes);
                 tma_load_2d(st, &tm_w, (kb0 + it) * kPK, tile * kPRows, &full[s]);
                 tma_load_2d(st + kPWTile, &tm_x, (kb0 + it) * kPK, 0, &full[s]);
             }
             if (!ok) {  // let the copies in flight land before the CTA moves on
-                for (int k = it - kPStages; k < it; ++k)
-                    if (k >= 0) mbar_wait_drain(&full[k % kPStages], (k / kPStages) & 1);
+                for (int k = it - p.stages; k < it; ++k)
+                    if (k >= 0) mbar_wait_drain(&full[k % p.stages], (k / p.stages) & 1);
             }
         }
     } else if (warp == 1) {
@@ -259,13 +260,13 @@ __global__ void __launch_bounds__(kPThreads, 1)
         if (lane == 0) {
             bool ok = true;
             for (int it = 0; it < nkb; ++it) {
-                const int s = it % kPStages;
-                if (!mbar_wait_bounded(&full[s], (it / kPStages) & 1, &s_abort, p.status)) {
+                const int s = it % p.stages;
+                if (!mbar_wait_bounded(&full[s], (it / p.stages) & 1, &s_abort, p.status)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a = smem_u32(gen + s * kPStageBytes), b = a + kPWTile;
+                const uint32_t a = smem_u32(gen + s * p.stage_bytes), b = a + kPWTile;
 #pragma unroll
                 for (int kk = 0; kk < kPK / 16; ++kk)
                     umma_bf16(tmem, sw128_desc(a + kk * 32, 16, 1024),
@@ -405,6 +406,9 @@ int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const
     const int n_tiles = (prm.N + kPRows - 1) / kPRows;
     const int split = choose_split<EPI, HD>(n_tiles, prm.kblocks);
     prm.split = split;
+    prm.stage_bytes = kPWTile + (uint32_t)prm.Mt * kPK * 2;  // multiple of 1 KiB
+    prm.stages = (int)(kPRingBytes / prm.stage_bytes);
+    if (prm.stages > kPMaxStages) prm.stages = kPMaxStages;
     CUtensorMap tw, tx;
     rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kPK, kPRows, &tw);
     if (rc) return rc;
