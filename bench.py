@@ -1107,9 +1107,9 @@ def run_decode_proj_bench(args, rank, world, local):
         "data": "synthetic (seeded bf16 x ~N(0,1), w ~N(0,1/hidden))",
         "config": {"workload": label, "batch": B, "qkv_n": N, "hidden": K,
                    "layers_rotated": layers,
-                   "plan_qkv": dict(zip(("split", "ctas", "clusters_that_fit"),
+                   "plan_qkv": dict(zip(("split", "ctas", "clusters_that_fit", "ctas_per_sm"),
                                         L.proj_decode_plan(N, K))),
-                   "plan_o": dict(zip(("split", "ctas", "clusters_that_fit"),
+                   "plan_o": dict(zip(("split", "ctas", "clusters_that_fit", "ctas_per_sm"),
                                       L.proj_decode_plan(No, hq * hd))),
                    "l2": "no flush: %d distinct weight sets, %.0f MB > 2 x 126 MB L2" %
                          (layers, layers * wbytes / 1e6)},

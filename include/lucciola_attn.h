@@ -257,10 +257,12 @@ int lc_paged_decode_static(void *out, int64_t out_stride, const void *q,
 /* How lc_proj_gemm / lc_qkv_proj_rope_append run a decode step (M <= 128 token
  * rows: one per sequence) on the current device: the weights are split into
  * ceil(N / 128)-row tiles, each tile's K over a cluster of `split` CTAs;
- * `ctas` is the grid and `clusters_that_fit` (optional) how many clusters of
- * that size the device runs at once. No counterpart in the reference, which
- * calls cublasGemmEx (src/models.rs:252-292). */
-int lc_proj_decode_plan(int N, int K, int *split, int *ctas, int *clusters_that_fit);
+ * `ctas` is the grid, and (optional) `clusters_that_fit` how many clusters of
+ * that size the device runs at once and `ctas_per_sm` how many of the
+ * kernel's CTAs share an SM. No counterpart in the reference, which calls
+ * cublasGemmEx (src/models.rs:252-292). */
+int lc_proj_decode_plan(int N, int K, int *split, int *ctas, int *clusters_that_fit,
+                        int *ctas_per_sm);
 
 /* Causal prefill over the paged pool (tcgen05 tensor-core path). Query token i
  * of sequence b sits at position start_pos[b] + i and attends to cache tokens

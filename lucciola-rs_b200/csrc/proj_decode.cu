@@ -355,6 +355,41 @@ __global__ void __launch_bounds__(kPThreads, 2)
 
 // Clusters of `split` CTAs (one CTA per SM: the ring takes most of shared
 // memory) that the device runs at once, per split; cached per device.
+// Shared-memory size and carveout of the kernel (once per instance and device:
+// the carveout lets two CTAs of 97 KiB share an SM).
+template <int EPI, int HD>
+int prepare_kernel() {
+    static bool done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    int rc = ensure_smem_attr((const void *)proj_decode_kernel<EPI, HD>, kPSmem);
+    if (rc) return rc;
+    if (!done[dev]) {
+        if (cudaFuncSetAttribute(proj_decode_kernel<EPI, HD>,
+                                 cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
+            cudaGetLastError();
+            return LC_ERR_CUDA;
+        }
+        done[dev] = true;
+    }
+    return LC_OK;
+}
+
+template <int EPI, int HD>
+int ctas_per_sm() {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, proj_decode_kernel<EPI, HD>, kPThreads,
+                                                      kPSmem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
 template <int EPI, int HD>
 int max_clusters(int split) {
     static int cached[64][4] = {};
@@ -401,7 +436,7 @@ template <int EPI, int HD>
 int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const void *w,
                        int64_t w_stride, cudaStream_t stream) {
     auto kern = proj_decode_kernel<EPI, HD>;
-    int rc = ensure_smem_attr((const void *)kern, kPSmem);
+    int rc = prepare_kernel<EPI, HD>();
     if (rc) return rc;
     const int n_tiles = (prm.N + kPRows - 1) / kPRows;
     const int split = choose_split<EPI, HD>(n_tiles, prm.kblocks);
@@ -483,10 +518,12 @@ int decode_proj_launch(const DecodeProjArgs &a, cudaStream_t stream) {
 
 using namespace lc;
 
-extern "C" int lc_proj_decode_plan(int N, int K, int *split, int *ctas, int *clusters_that_fit) {
+extern "C" int lc_proj_decode_plan(int N, int K, int *split, int *ctas, int *clusters_that_fit,
+                                   int *ctas_per_sm_out) {
     if (N <= 0 || K <= 0 || !split || !ctas) return LC_ERR_INVALID_ARGUMENT;
-    int rc = ensure_smem_attr((const void *)proj_decode_kernel<kDecPlain, 128>, kPSmem);
+    int rc = prepare_kernel<kDecPlain, 128>();
     if (rc) return rc;
+    if (ctas_per_sm_out) *ctas_per_sm_out = ctas_per_sm<kDecPlain, 128>();
     const int n_tiles = (N + kPRows - 1) / kPRows;
     *split = choose_split<kDecPlain, 128>(n_tiles, (K + kPK - 1) / kPK);
     *ctas = n_tiles * *split;

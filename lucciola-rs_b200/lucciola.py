@@ -52,7 +52,7 @@ SIGNATURES = {
     "lc_paged_decode_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                       _i32, _i32, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _f32,
                                       _vp, _vp]),
-    "lc_proj_decode_plan": (_i32, [_i32, _i32, _pi32, _pi32, _pi32]),
+    "lc_proj_decode_plan": (_i32, [_i32, _i32, _pi32, _pi32, _pi32, _pi32]),
     "lc_paged_prefill": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _i64, _i32, _i32, _i32, _i32,
                                 _i32, _vp, _i32, _vp, _i32, _i32, _i32, _f32, _vp, _vp]),
     "lc_gather_kv": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp,
@@ -554,11 +554,12 @@ class BlockAlloc:
 
 
 def proj_decode_plan(n, k):
-    """(split, ctas, clusters_that_fit) of the decode-step projection kernel."""
-    a, b, c = C.c_int(), C.c_int(), C.c_int()
-    check(lib.lc_proj_decode_plan(n, k, C.byref(a), C.byref(b), C.byref(c)),
+    """(split, ctas, clusters_that_fit, ctas_per_sm) of the decode-step
+    projection kernel."""
+    a, b, c, d = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+    check(lib.lc_proj_decode_plan(n, k, C.byref(a), C.byref(b), C.byref(c), C.byref(d)),
           "lc_proj_decode_plan")
-    return a.value, b.value, c.value
+    return a.value, b.value, c.value, d.value
 
 
 def proj_gemm(out, x, w, residual=None, stream=None):
