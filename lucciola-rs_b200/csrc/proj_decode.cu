@@ -6,23 +6,26 @@
 // reading the weights once (x is a few hundred KiB and stays in L2), so the
 // kernel is laid out to stream w over as many SMs as possible:
 //
-//  * The MMA's M dimension is the weights: a tile is 128 weight rows (output
-//    columns); the token rows are the MMA's N (padded to a multiple of 16).
-//    tcgen05.mma M128 x N(tokens) x K16, bf16 in, fp32 accumulate in TMEM.
+//  * The MMA's M dimension is the weights: a tile is 64 weight rows (output
+//    columns) in two boxes of 32, the first holding dims d and the second
+//    dims d + head_dim/2 of the same head at head_dim 128 (the pairs RoPE
+//    rotates together; at head_dim 64 a tile is one head); the token rows are
+//    the MMA's N (padded to a multiple of 16). tcgen05.mma M64 x N(tokens) x
+//    K16, bf16 in, fp32 accumulate in TMEM, where weight row m of the tile
+//    sits in lane (m % 16) + 32 (m / 16).
 //  * A cluster of `split` CTAs (a power of two up to 8) shares one tile, CTA r
-//    taking the r-th slice of K: nt tiles x split CTAs cover the SMs.
-//  * Warp 0 streams the CTA's K slice with TMA (w box {64 x 128}, x box
-//    {64 x Mt}, 128-byte swizzle) into a 96 KiB ring (3-6 stages, two CTAs
-//    per SM); the weight loads of the
+//    taking the r-th slice of K: tiles x split CTAs cover the SMs (one CTA per
+//    SM; the split is the widest whose clusters all fit at once).
+//  * Warp 0 streams the CTA's K slice with TMA (w boxes {64 x 32}, x box
+//    {64 x Mt}, 128-byte swizzle) into a 192 KiB ring; the weight loads of the
 //    first stages are issued before the programmatic-dependency wait, the
 //    token rows (written by the preceding kernel) after it. Warp 1 issues the
 //    MMAs. Warps 2-5 move the CTA's partial tile from TMEM into its shared
 //    memory (the idle ring).
-//  * Cluster reduction over distributed shared memory: CTA r owns 64/split of
-//    the tile's 64 row pairs (row pair = dims d and d + head_dim/2 of a head,
-//    the pair RoPE rotates together) and sums them over the cluster's partials
-//    in rank order (the same order whatever the timing), then runs the
-//    epilogue on them.
+//  * Cluster reduction over distributed shared memory: CTA r owns 32/split of
+//    the tile's 32 row pairs and sums them over the cluster's partials in rank
+//    order (the same order whatever the timing), then runs the epilogue on
+//    them.
 //
 // Epilogues (the arithmetic of proj_gemm.cu, element by element):
 //   plain     out = bf16(acc)
@@ -44,13 +47,14 @@
 namespace lc {
 namespace {
 
-constexpr int kPRows = 128;   // weight rows per tile (the MMA's M)
+constexpr int kPRows = 64;    // weight rows per tile (the MMA's M)
 constexpr int kPK = 64;       // K per stage: one 128-byte swizzle row
-constexpr int kPMaxStages = 6;
-constexpr uint32_t kPRingBytes = 96 * 1024;  // two CTAs per SM
+constexpr int kPMaxStages = 16;
+constexpr uint32_t kPRingBytes = 192 * 1024;
 constexpr int kPThreads = 192;  // TMA warp, MMA warp, four epilogue warps
 constexpr int kPPairs = kPRows / 2;
-constexpr uint32_t kPWTile = kPRows * kPK * 2;         // 16 KiB
+constexpr uint32_t kPWTile = kPRows * kPK * 2;         // 8 KiB: two boxes of 32 rows
+constexpr uint32_t kPWBox = 32 * kPK * 2;
 constexpr int kPSmem = kPRingBytes + 1024;  // + 1024-byte alignment slack
 constexpr int kPMaxSplit = 8;
 constexpr uint32_t kPTmemCols = 128;
@@ -84,18 +88,23 @@ struct DecProjParams {
     int *status;
 };
 
-// Staged partial tile: [128 weight rows][Mt + 4] fp32 (the padding spreads the
+// Staged partial tile: [64 weight rows][Mt + 4] fp32 (the padding spreads the
 // rows over the shared-memory banks).
-__device__ __forceinline__ int stage_pitch(int Mt) { return Mt + 4; }
+__host__ __device__ __forceinline__ int stage_pitch(int Mt) { return Mt + 4; }
 
-// Rows of pair p of a 128-row tile whose heads are HD wide: dims i and
-// i + HD/2 of head p / (HD/2), i = p % (HD/2).
-template <int HD>
-__device__ __forceinline__ void pair_rows(int p, int &ra, int &rb) {
-    constexpr int kHalf = HD / 2;
-    const int head = p / kHalf, i = p - head * kHalf;
-    ra = head * HD + i;
-    rb = ra + kHalf;
+// First weight rows of the two 32-row boxes of tile t. With heads of 128 dims
+// (QKV) box 1 holds the partners (dim + 64) of box 0's dims; otherwise the
+// boxes are the tile's 64 consecutive rows (at head_dim 64 exactly one head:
+// dim d in box 0, its partner d + 32 in box 1). Tile-local row pair p (< 32)
+// is rows (r0 + p, r1 + p).
+__host__ __device__ __forceinline__ void tile_rows(int t, bool heads128, int &r0, int &r1) {
+    if (heads128) {
+        r0 = (t >> 1) * 128 + (t & 1) * 32;
+        r1 = r0 + 64;
+    } else {
+        r0 = t * 64;
+        r1 = r0 + 32;
+    }
 }
 
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
@@ -184,7 +193,7 @@ __device__ __forceinline__ void dec_store_qkv(const DecProjParams &p, int m, int
 }
 
 template <int EPI, int HD>
-__global__ void __launch_bounds__(kPThreads, 2)
+__global__ void __launch_bounds__(kPThreads, 1)
     proj_decode_kernel(const __grid_constant__ CUtensorMap tm_w,
                        const __grid_constant__ CUtensorMap tm_x, const DecProjParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -198,6 +207,8 @@ __global__ void __launch_bounds__(kPThreads, 2)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rank = (int)cluster_ctarank();
     const int tile = (int)blockIdx.x / p.split;
+    int wr0, wr1;
+    tile_rows(tile, EPI == kDecQkv && HD == 128, wr0, wr1);
     const int kb0 = rank * p.kblocks / p.split, kb1 = (rank + 1) * p.kblocks / p.split;
     const int nkb = kb1 - kb0;
     const uint32_t xbytes = (uint32_t)p.Mt * kPK * 2;
@@ -232,7 +243,8 @@ __global__ void __launch_bounds__(kPThreads, 2)
             const int pre = min(nkb, p.stages);
             for (int i = 0; i < pre; ++i) {
                 mbar_arrive_expect_tx(&full[i], kPWTile + xbytes);
-                tma_load_2d(gen + i * p.stage_bytes, &tm_w, (kb0 + i) * kPK, tile * kPRows, &full[i]);
+                tma_load_2d(gen + i * p.stage_bytes, &tm_w, (kb0 + i) * kPK, wr0, &full[i]);
+                tma_load_2d(gen + i * p.stage_bytes + kPWBox, &tm_w, (kb0 + i) * kPK, wr1, &full[i]);
             }
             if (p.pdl_mode) griddep_wait();
             for (int i = 0; i < pre; ++i)
@@ -247,7 +259,8 @@ __global__ void __launch_bounds__(kPThreads, 2)
                 }
                 uint8_t *st = gen + s * p.stage_bytes;
                 mbar_arrive_expect_tx(&full[s], kPWTile + xbytes);
-                tma_load_2d(st, &tm_w, (kb0 + it) * kPK, tile * kPRows, &full[s]);
+                tma_load_2d(st, &tm_w, (kb0 + it) * kPK, wr0, &full[s]);
+                tma_load_2d(st + kPWBox, &tm_w, (kb0 + it) * kPK, wr1, &full[s]);
                 tma_load_2d(st + kPWTile, &tm_x, (kb0 + it) * kPK, 0, &full[s]);
             }
             if (!ok) {  // let the copies in flight land before the CTA moves on
@@ -279,9 +292,11 @@ __global__ void __launch_bounds__(kPThreads, 2)
     } else {
         // ------------------------------- partial tile: TMEM -> shared memory --
         // The ring is idle once the accumulator is complete (every stage's
-        // MMAs have read it); it holds the staged tile [128][Mt + 4] fp32.
+        // MMAs have read it); it holds the staged tile [64][Mt + 4] fp32.
+        // An M64 accumulator fills lanes 0-15 of each 32-lane quadrant: lane i
+        // of quadrant q holds the tile's weight row 16 q + i.
         const int quad = warp & 3;
-        const int row = quad * 32 + lane;
+        const int row = quad * 16 + lane;
         float *stg = reinterpret_cast<float *>(gen);
         const int pitch = stage_pitch(p.Mt);
         bool have = nkb > 0 && mbar_wait_bounded(&acc_full, 0, &s_abort, p.status);
@@ -293,9 +308,11 @@ __global__ void __launch_bounds__(kPThreads, 2)
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, r);
                 tmem_wait_ld_regs(r);
             }
+            if (lane < 16) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (c0 + i < p.Mt) stg[row * pitch + c0 + i] = have ? __uint_as_float(r[i]) : 0.f;
+                for (int i = 0; i < 32; ++i)
+                    if (c0 + i < p.Mt) stg[row * pitch + c0 + i] = have ? __uint_as_float(r[i]) : 0.f;
+            }
         }
     }
     // Every CTA's staged tile is complete and visible to the cluster.
@@ -317,8 +334,7 @@ __global__ void __launch_bounds__(kPThreads, 2)
         const int items = p.M * npr;
         for (int item = et; item < items; item += 128) {
             const int m = item / npr, pl = item - m * npr;  // neighbouring threads: neighbouring pairs
-            int ra, rb;
-            pair_rows<EPI == kDecQkv ? HD : 128>(pr0 + pl, ra, rb);
+            const int ra = pr0 + pl, rb = ra + 32;  // tile-local rows of the pair
             float va[kPMaxSplit], vb[kPMaxSplit];
 #pragma unroll
             for (int r = 0; r < kPMaxSplit; ++r) {
@@ -335,7 +351,7 @@ __global__ void __launch_bounds__(kPThreads, 2)
                     b += vb[r];
                 }
             }
-            const int col = tile * kPRows + ra, colb = tile * kPRows + rb;
+            const int col = wr0 + ra, colb = wr1 + ra;  // colb = col + head_dim/2 (QKV)
             if constexpr (EPI == kDecQkv) {
                 dec_store_qkv<HD>(p, m, col, a, b);
             } else {
@@ -355,8 +371,7 @@ __global__ void __launch_bounds__(kPThreads, 2)
 
 // Clusters of `split` CTAs (one CTA per SM: the ring takes most of shared
 // memory) that the device runs at once, per split; cached per device.
-// Shared-memory size and carveout of the kernel (once per instance and device:
-// the carveout lets two CTAs of 97 KiB share an SM).
+// Shared-memory size and carveout of the kernel (once per instance and device).
 template <int EPI, int HD>
 int prepare_kernel() {
     static bool done[64] = {};
@@ -445,7 +460,7 @@ int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const
     prm.stages = (int)(kPRingBytes / prm.stage_bytes);
     if (prm.stages > kPMaxStages) prm.stages = kPMaxStages;
     CUtensorMap tw, tx;
-    rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kPK, kPRows, &tw);
+    rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kPK, 32, &tw);
     if (rc) return rc;
     rc = tensor_map_2d_sw128(x, prm.K, prm.M, x_stride * 2, kPK, prm.Mt, &tx);
     if (rc) return rc;
