@@ -16,12 +16,16 @@
 //  * A cluster of `split` CTAs (a power of two up to 8) shares one tile, CTA r
 //    taking the r-th slice of K: tiles x split CTAs cover the SMs (one CTA per
 //    SM; the split is the widest whose clusters all fit at once).
-//  * Warp 0 streams the CTA's K slice with TMA (w boxes {64 x 32}, x box
-//    {64 x Mt}, 128-byte swizzle) into a 192 KiB ring; the weight loads of the
-//    first stages are issued before the programmatic-dependency wait, the
+//  * Warps 2-5 stream the CTA's K slice into a 192 KiB ring with cp.async,
+//    four K blocks per ring slot, so that one warp instruction fetches 512
+//    contiguous bytes of one weight row (TMA boxes of 32 rows x 128 bytes from
+//    rows 7 KiB apart ran at ~27 GB/s per SM: the copy engine handled them one
+//    128-byte row at a time, arrivals 0.45 us apart per stage); the copies
+//    land in the 128-byte-swizzled layout the MMA reads. The weight loads of
+//    the first slots are issued before the programmatic-dependency wait, the
 //    token rows (written by the preceding kernel) after it. Warp 1 issues the
-//    MMAs. Warps 2-5 move the CTA's partial tile from TMEM into its shared
-//    memory (the idle ring).
+//    MMAs. Then warps 2-5 move the CTA's partial tile from TMEM into its
+//    shared memory (the idle ring).
 //  * Cluster reduction over distributed shared memory: CTA r owns 32/split of
 //    the tile's 32 row pairs and sums them over the cluster's partials in rank
 //    order (the same order whatever the timing), then runs the epilogue on
@@ -54,7 +58,7 @@ constexpr uint32_t kPRingBytes = 192 * 1024;
 constexpr int kPThreads = 192;  // TMA warp, MMA warp, four epilogue warps
 constexpr int kPPairs = kPRows / 2;
 constexpr uint32_t kPWTile = kPRows * kPK * 2;         // 8 KiB: two boxes of 32 rows
-constexpr uint32_t kPWBox = 32 * kPK * 2;
+constexpr int kPGroupKB = 4;  // K blocks per ring slot: 512 contiguous bytes of a row
 constexpr int kPSmem = kPRingBytes + 1024;  // + 1024-byte alignment slack
 constexpr int kPMaxSplit = 8;
 constexpr uint32_t kPTmemCols = 128;
@@ -63,10 +67,12 @@ enum DecEpilogue { kDecPlain = 0, kDecResidual = 1, kDecQkv = 2 };
 
 struct DecProjParams {
     int M, N, K;
+    const bf16 *w, *x;
+    int64_t w_stride, x_stride;
     int Mt;       // token rows padded to a multiple of 16 (the MMA's N)
     int split;    // CTAs per cluster (K slices)
-    int stages;   // ring stages of (w tile + x tile) that fit kPRingBytes
-    uint32_t stage_bytes;
+    int stages;   // ring slots: groups of kPGroupKB (w tile + x tile) stages
+    uint32_t stage_bytes;  // one K block: w tile (8 KiB) + x tile
     int kblocks;  // K / 64, rounded up
     int pdl_mode;
     bf16 *out;
@@ -105,6 +111,22 @@ __host__ __device__ __forceinline__ void tile_rows(int t, bool heads128, int &r0
         r0 = t * 64;
         r1 = r0 + 32;
     }
+}
+
+// 16-byte asynchronous copy global -> shared (zero fill when !valid).
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)),
+                 "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+// The mbarrier counts this thread's arrival once all its earlier cp.async copies
+// have landed (no separate arrive).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
@@ -194,8 +216,7 @@ __device__ __forceinline__ void dec_store_qkv(const DecProjParams &p, int m, int
 
 template <int EPI, int HD>
 __global__ void __launch_bounds__(kPThreads, 1)
-    proj_decode_kernel(const __grid_constant__ CUtensorMap tm_w,
-                       const __grid_constant__ CUtensorMap tm_x, const DecProjParams p) {
+    proj_decode_kernel(const DecProjParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *gen = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -211,13 +232,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
     tile_rows(tile, EPI == kDecQkv && HD == 128, wr0, wr1);
     const int kb0 = rank * p.kblocks / p.split, kb1 = (rank + 1) * p.kblocks / p.split;
     const int nkb = kb1 - kb0;
-    const uint32_t xbytes = (uint32_t)p.Mt * kPK * 2;
+    const int ngroups = (nkb + kPGroupKB - 1) / kPGroupKB;
+    const uint32_t group_bytes = kPGroupKB * p.stage_bytes;
     const uint32_t idesc = idesc_bf16_f32(kPRows, p.Mt, 0);
 
     griddep_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], 128);  // the four loading warps' cp.async arrivals
             mbar_init(&empty[s], 1);
         }
         mbar_init(&acc_full, 1);
@@ -233,63 +255,82 @@ __global__ void __launch_bounds__(kPThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
 
-    if (warp == 0) {
-        // ---------------------------------------------------------------- TMA --
-        if (lane == 0) {
-            prefetch_tensormap(&tm_w);
-            prefetch_tensormap(&tm_x);
-            // The first stages' weights depend on no earlier kernel: they stream
-            // while the preceding grid drains; the token rows come after it.
-            const int pre = min(nkb, p.stages);
-            for (int i = 0; i < pre; ++i) {
-                mbar_arrive_expect_tx(&full[i], kPWTile + xbytes);
-                tma_load_2d(gen + i * p.stage_bytes, &tm_w, (kb0 + i) * kPK, wr0, &full[i]);
-                tma_load_2d(gen + i * p.stage_bytes + kPWBox, &tm_w, (kb0 + i) * kPK, wr1, &full[i]);
-            }
-            if (p.pdl_mode) griddep_wait();
-            for (int i = 0; i < pre; ++i)
-                tma_load_2d(gen + i * p.stage_bytes + kPWTile, &tm_x, (kb0 + i) * kPK, 0, &full[i]);
-            int it = pre;
-            bool ok = true;
-            for (; it < nkb; ++it) {
-                const int s = it % p.stages;
-                if (!mbar_wait_bounded(&empty[s], ((it / p.stages) - 1) & 1, &s_abort, p.status)) {
-                    ok = false;
-                    break;
-                }
-                uint8_t *st = gen + s * p.stage_bytes;
-                mbar_arrive_expect_tx(&full[s], kPWTile + xbytes);
-                tma_load_2d(st, &tm_w, (kb0 + it) * kPK, wr0, &full[s]);
-                tma_load_2d(st + kPWBox, &tm_w, (kb0 + it) * kPK, wr1, &full[s]);
-                tma_load_2d(st + kPWTile, &tm_x, (kb0 + it) * kPK, 0, &full[s]);
-            }
-            if (!ok) {  // let the copies in flight land before the CTA moves on
-                for (int k = it - p.stages; k < it; ++k)
-                    if (k >= 0) mbar_wait_drain(&full[k % p.stages], (k / p.stages) & 1);
-            }
-        }
-    } else if (warp == 1) {
+    if (warp == 1) {
         // ---------------------------------------------------------------- MMA --
         if (lane == 0) {
             bool ok = true;
-            for (int it = 0; it < nkb; ++it) {
-                const int s = it % p.stages;
-                if (!mbar_wait_bounded(&full[s], (it / p.stages) & 1, &s_abort, p.status)) {
+            for (int gi = 0; gi < ngroups; ++gi) {
+                const int s = gi % p.stages;
+                if (!mbar_wait_bounded(&full[s], (gi / p.stages) & 1, &s_abort, p.status)) {
                     ok = false;
                     break;
                 }
+                // The copies are generic-proxy writes; the MMAs read through the
+                // async proxy.
+                fence_proxy_async_smem();
                 tc_fence_after();
-                const uint32_t a = smem_u32(gen + s * p.stage_bytes), b = a + kPWTile;
+                const int nj = min(kPGroupKB, nkb - gi * kPGroupKB);
+                for (int j = 0; j < nj; ++j) {
+                    const uint32_t a = smem_u32(gen + s * group_bytes + j * p.stage_bytes);
+                    const uint32_t b = a + kPWTile;
 #pragma unroll
-                for (int kk = 0; kk < kPK / 16; ++kk)
-                    umma_bf16(tmem, sw128_desc(a + kk * 32, 16, 1024),
-                              sw128_desc(b + kk * 32, 16, 1024), idesc,
-                              (it > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&empty[s]);  // the stage is free once these MMAs are done
+                    for (int kk = 0; kk < kPK / 16; ++kk)
+                        umma_bf16(tmem, sw128_desc(a + kk * 32, 16, 1024),
+                                  sw128_desc(b + kk * 32, 16, 1024), idesc,
+                                  (gi > 0 || j > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&empty[s]);  // the group's slot is free once these MMAs are done
             }
             if (ok && nkb > 0) umma_commit(&acc_full);
         }
-    } else {
+    } else if (warp >= 2) {
+        // ------------------------------------------------------ loads (cp.async) --
+        // Warps 2-5 copy each group of kPGroupKB K blocks: one warp instruction
+        // moves 512 contiguous bytes of one weight (or token) row, lane l taking
+        // K block l / 8, 16-byte chunk l % 8, into the 128-byte-swizzled tile
+        // the MMA reads (chunk c of row r at r * 128 + ((c ^ (r % 8)) * 16)).
+        // Rows past N or M and K past the end are zero-filled. The first
+        // groups' weights are requested before the programmatic-dependency
+        // wait, the token rows after it.
+        const int pw = warp - 2;
+        const int jl = lane >> 3, cl = lane & 7;
+        auto load_w = [&](int gi) {
+            uint8_t *base = gen + (gi % p.stages) * group_bytes + jl * p.stage_bytes;
+            const int kb = kb0 + gi * kPGroupKB + jl;
+            const bool kok = kb < kb1 && kb * kPK + cl * 8 < p.K;
+            for (int r = pw; r < kPRows; r += 4) {
+                const int grow = r < 32 ? wr0 + r : wr1 + (r - 32);
+                const bool ok = kok && grow < p.N;
+                const bf16 *src = ok ? p.w + (int64_t)grow * p.w_stride + kb * kPK + cl * 8 : p.w;
+                cp_async16(base + r * 128 + ((cl ^ (r & 7)) << 4), src, ok);
+            }
+        };
+        auto load_x = [&](int gi) {
+            uint8_t *base = gen + (gi % p.stages) * group_bytes + jl * p.stage_bytes + kPWTile;
+            const int kb = kb0 + gi * kPGroupKB + jl;
+            const bool kok = kb < kb1 && kb * kPK + cl * 8 < p.K;
+            for (int t = pw; t < p.Mt; t += 4) {
+                const bool ok = kok && t < p.M;
+                const bf16 *src = ok ? p.x + (int64_t)t * p.x_stride + kb * kPK + cl * 8 : p.x;
+                cp_async16(base + t * 128 + ((cl ^ (t & 7)) << 4), src, ok);
+            }
+        };
+        const int pre = min(ngroups, p.stages);
+        for (int gi = 0; gi < pre; ++gi) load_w(gi);
+        if (p.pdl_mode) griddep_wait();
+        for (int gi = 0; gi < pre; ++gi) {
+            load_x(gi);
+            cp_async_arrive_noinc(&full[gi]);  // lands with this thread's copies so far
+        }
+        for (int gi = pre; gi < ngroups; ++gi) {
+            const int s = gi % p.stages;
+            if (!mbar_wait_bounded(&empty[s], ((gi / p.stages) - 1) & 1, &s_abort, p.status)) break;
+            load_w(gi);
+            load_x(gi);
+            cp_async_arrive_noinc(&full[s]);
+        }
+        cp_async_wait_all();  // no copy may land in the ring after this point
+
         // ------------------------------- partial tile: TMEM -> shared memory --
         // The ring is idle once the accumulator is complete (every stage's
         // MMAs have read it); it holds the staged tile [64][Mt + 4] fp32.
@@ -456,14 +497,13 @@ int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const
     const int n_tiles = (prm.N + kPRows - 1) / kPRows;
     const int split = choose_split<EPI, HD>(n_tiles, prm.kblocks);
     prm.split = split;
-    prm.stage_bytes = kPWTile + (uint32_t)prm.Mt * kPK * 2;  // multiple of 1 KiB
-    prm.stages = (int)(kPRingBytes / prm.stage_bytes);
+    prm.stage_bytes = kPWTile + (uint32_t)prm.Mt * kPK * 2;  // multiple of 2 KiB
+    prm.stages = (int)(kPRingBytes / (kPGroupKB * prm.stage_bytes));
     if (prm.stages > kPMaxStages) prm.stages = kPMaxStages;
-    CUtensorMap tw, tx;
-    rc = tensor_map_2d_sw128(w, prm.K, prm.N, w_stride * 2, kPK, 32, &tw);
-    if (rc) return rc;
-    rc = tensor_map_2d_sw128(x, prm.K, prm.M, x_stride * 2, kPK, prm.Mt, &tx);
-    if (rc) return rc;
+    prm.w = (const bf16 *)w;
+    prm.x = (const bf16 *)x;
+    prm.w_stride = w_stride;
+    prm.x_stride = x_stride;
     const int mode = dependent_launch_mode();
     prm.pdl_mode = mode;
     cudaLaunchConfig_t cfg = {};
@@ -480,7 +520,7 @@ int launch_decode_proj(DecProjParams prm, const void *x, int64_t x_stride, const
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = mode > 0 ? 2 : 1;
-    if (cudaLaunchKernelEx(&cfg, kern, tw, tx, prm) != cudaSuccess) {
+    if (cudaLaunchKernelEx(&cfg, kern, prm) != cudaSuccess) {
         cudaGetLastError();
         return LC_ERR_CUDA;
     }
