@@ -1018,6 +1018,8 @@ def run_decode_proj_bench(args, rank, world, local):
     label, B, hq, hkv, hd, hidden = DECODE_PROJ[args.config]
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    # a launch's first weight loads overlap the preceding launch's tail
+    L.set_dependent_launch(args.pdl)
     gen = torch.Generator(device=device)
     gen.manual_seed(919)
     N, K, No = (hq + 2 * hkv) * hd, hidden, hidden
@@ -1106,7 +1108,7 @@ def run_decode_proj_bench(args, rank, world, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded bf16 x ~N(0,1), w ~N(0,1/hidden))",
         "config": {"workload": label, "batch": B, "qkv_n": N, "hidden": K,
-                   "layers_rotated": layers,
+                   "layers_rotated": layers, "programmatic_dependent_launch": args.pdl,
                    "plan_qkv": dict(zip(("split", "ctas", "clusters_that_fit", "ctas_per_sm"),
                                         L.proj_decode_plan(N, K))),
                    "plan_o": dict(zip(("split", "ctas", "clusters_that_fit", "ctas_per_sm"),
