@@ -1072,15 +1072,26 @@ def run_decode_proj_bench(args, rank, world, local):
         return
 
     def timed(fn, steps):
+        # One CUDA graph over all rotated layers, replayed: the launches run
+        # back to back on the device, with no host-side launch cost between
+        # them (the same for both arms).
         for i in range(max(args.warmup, 3) * layers):
             fn(i % layers)
         torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for l in range(layers):
+                fn(l)
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for i in range(steps * layers):
-            fn(i % layers)
+        for _ in range(steps):
+            g.replay()
         e1.record()
         torch.cuda.synchronize()
+        del g
         return e0.elapsed_time(e1) / (steps * layers)
 
     sampler = ClockSampler(local)
@@ -1114,7 +1125,9 @@ def run_decode_proj_bench(args, rank, world, local):
                    "plan_o": dict(zip(("split", "ctas", "clusters_that_fit", "ctas_per_sm"),
                                       L.proj_decode_plan(No, hq * hd))),
                    "l2": "no flush: %d distinct weight sets, %.0f MB > 2 x 126 MB L2" %
-                         (layers, layers * wbytes / 1e6)},
+                         (layers, layers * wbytes / 1e6),
+                   "timing": "both arms: one CUDA graph over the rotated layers, replayed "
+                             "--steps times"},
         "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(value / peak, 4), "peak_kind": f"{peak_kind} (burst copy)",
                      "qkv_launch_ms": round(qkv_only, 5), "qkv_achieved": round(q_gbs, 1),
