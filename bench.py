@@ -1107,6 +1107,7 @@ def run_decode_proj_bench(args, rank, world, local):
     qkv_only = timed(lambda l: L.qkv_proj_rope_append(qkv, x, wq[l], positions, qb, kb, vb, cos,
                                                       sin, k_pool, v_pool, nb, 1, 0, hq, hkv, hd,
                                                       tables, tokens_per_seq=1), args.steps)
+    lib_gemm_only = timed(lambda l: torch.matmul(x, wq[l].t(), out=qkv), args.steps)
     peak, peak_kind = measured_peak()
     value = wbytes / (ms * 1e-3) / 1e9
     q_bytes = N * K * 2
@@ -1133,6 +1134,8 @@ def run_decode_proj_bench(args, rank, world, local):
                      "qkv_launch_ms": round(qkv_only, 5), "qkv_achieved": round(q_gbs, 1),
                      "qkv_frac": round(q_gbs / peak, 4)},
         "library_path": {"ms_per_layer": round(ms_lib, 5),
+                         "qkv_gemm_ms": round(lib_gemm_only, 5),
+                         "qkv_gemm_gbs": round(q_bytes / (lib_gemm_only * 1e-3) / 1e9, 1),
                          "how": "torch.matmul (cublasGemmEx) + lc_rope_append; torch.matmul + "
                                 "residual add for o_proj"},
         "speedup_vs_library": round(ms_lib / ms, 3),

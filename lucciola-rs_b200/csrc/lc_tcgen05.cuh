@@ -161,6 +161,7 @@ __device__ inline void tmem_wait_ld_regs(uint32_t (&r)[32]) {
 }
 __device__ inline void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+
 // ------------------------------------------------------- CTA pairs (2-SM) --
 // A cluster of two CTAs on neighbouring SMs sharing one tcgen05.mma: each CTA
 // holds half of A (M/2 rows) and half of B (N/2 rows) in its shared memory and
@@ -183,6 +184,14 @@ __device__ inline uint32_t mapa_shared(uint32_t local, uint32_t rank) {
 __device__ inline void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                      : "memory");
+}
+// The two halves of cluster_sync, for work in between: every thread of the
+// cluster arrives once, then waits once.
+__device__ inline void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ inline void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ inline void tmem_alloc_2sm(uint32_t *smem_dst, uint32_t ncols) {

@@ -16,7 +16,7 @@
 //  * A cluster of `split` CTAs (a power of two up to 8) shares one tile, CTA r
 //    taking the r-th slice of K: tiles x split CTAs cover the SMs (one CTA per
 //    SM; the split is the widest whose clusters all fit at once).
-//  * Warps 2-5 stream the CTA's K slice into a 192 KiB ring with cp.async,
+//  * Warps 2-9 stream the CTA's K slice into a 192 KiB ring with cp.async,
 //    four K blocks per ring slot, so that one warp instruction fetches 512
 //    contiguous bytes of one weight row (TMA boxes of 32 rows x 128 bytes from
 //    rows 7 KiB apart ran at ~27 GB/s per SM: the copy engine handled them one
@@ -24,7 +24,7 @@
 //    land in the 128-byte-swizzled layout the MMA reads. The weight loads of
 //    the first slots are issued before the programmatic-dependency wait, the
 //    token rows (written by the preceding kernel) after it. Warp 1 issues the
-//    MMAs. Then warps 2-5 move the CTA's partial tile from TMEM into its
+//    MMAs. Then warps 2-9 move the CTA's partial tile from TMEM into its
 //    shared memory (the idle ring).
 //  * Cluster reduction over distributed shared memory: CTA r owns 32/split of
 //    the tile's 32 row pairs and sums them over the cluster's partials in rank
@@ -55,13 +55,19 @@ constexpr int kPRows = 64;    // weight rows per tile (the MMA's M)
 constexpr int kPK = 64;       // K per stage: one 128-byte swizzle row
 constexpr int kPMaxStages = 16;
 constexpr uint32_t kPRingBytes = 192 * 1024;
-constexpr int kPThreads = 192;  // TMA warp, MMA warp, four epilogue warps
+constexpr int kPLoadWarps = 8;  // copy, then stage and finish the tile
+constexpr int kPThreads = 64 + 32 * kPLoadWarps;  // idle warp, MMA warp, loading warps
 constexpr int kPPairs = kPRows / 2;
 constexpr uint32_t kPWTile = kPRows * kPK * 2;         // 8 KiB: two boxes of 32 rows
 constexpr int kPGroupKB = 4;  // K blocks per ring slot: 512 contiguous bytes of a row
 constexpr int kPSmem = kPRingBytes + 1024;  // + 1024-byte alignment slack
 constexpr int kPMaxSplit = 8;
 constexpr uint32_t kPTmemCols = 128;
+// Cluster sums of the items a CTA finishes (<= 128 token rows x 32 row pairs
+// float2 = 32 KiB), in the ring past the staged tile (<= 64 x 132 fp32).
+constexpr uint32_t kPSumsOff = 64 * 1024;
+constexpr int kPBatch = 4;  // items whose partials are loaded together
+static_assert(kPSumsOff + kDecodeProjMaxRows * 32 * 8 <= kPRingBytes, "sums fit the ring");
 
 enum DecEpilogue { kDecPlain = 0, kDecResidual = 1, kDecQkv = 2 };
 
@@ -239,7 +245,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
     griddep_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
-            mbar_init(&full[s], 128);  // the four loading warps' cp.async arrivals
+            mbar_init(&full[s], 32 * kPLoadWarps);  // the loading warps' cp.async arrivals
             mbar_init(&empty[s], 1);
         }
         mbar_init(&acc_full, 1);
@@ -285,49 +291,76 @@ __global__ void __launch_bounds__(kPThreads, 1)
         }
     } else if (warp >= 2) {
         // ------------------------------------------------------ loads (cp.async) --
-        // Warps 2-5 copy each group of kPGroupKB K blocks: one warp instruction
+        // Warps 2-9 copy each group of kPGroupKB K blocks: one warp instruction
         // moves 512 contiguous bytes of one weight (or token) row, lane l taking
         // K block l / 8, 16-byte chunk l % 8, into the 128-byte-swizzled tile
         // the MMA reads (chunk c of row r at r * 128 + ((c ^ (r % 8)) * 16)).
         // Rows past N or M and K past the end are zero-filled. The first
         // groups' weights are requested before the programmatic-dependency
         // wait, the token rows after it.
+        // Each thread's rows, their source rows and swizzled offsets are fixed
+        // for the whole K slice: computed once, so that a group is a run of
+        // independent copies (one loading warp per SM sub-partition cannot
+        // hide a chain of address arithmetic per copy).
         const int pw = warp - 2;
         const int jl = lane >> 3, cl = lane & 7;
-        auto load_w = [&](int gi) {
-            uint8_t *base = gen + (gi % p.stages) * group_bytes + jl * p.stage_bytes;
+        constexpr int kWRows = kPRows / kPLoadWarps;  // weight rows per thread
+        constexpr int kXRows = kDecodeProjMaxRows / kPLoadWarps;
+        const bf16 *wsrc[kWRows];
+        uint32_t wdst[kWRows];
+        bool wok[kWRows];
+#pragma unroll
+        for (int i = 0; i < kWRows; ++i) {
+            const int r = pw + kPLoadWarps * i;
+            const int grow = r < 32 ? wr0 + r : wr1 + (r - 32);
+            wok[i] = grow < p.N;
+            wsrc[i] = p.w + (wok[i] ? (int64_t)grow * p.w_stride + cl * 8 : 0);
+            wdst[i] = (uint32_t)(r * 128 + ((cl ^ (r & 7)) << 4));
+        }
+        const bf16 *xsrc = p.x + (int64_t)pw * p.x_stride + cl * 8;
+        const int64_t xstep = (int64_t)kPLoadWarps * p.x_stride;
+        auto load_w = [&](int slot, int gi) {
+            uint8_t *base = gen + slot * group_bytes + jl * p.stage_bytes;
             const int kb = kb0 + gi * kPGroupKB + jl;
             const bool kok = kb < kb1 && kb * kPK + cl * 8 < p.K;
-            for (int r = pw; r < kPRows; r += 4) {
-                const int grow = r < 32 ? wr0 + r : wr1 + (r - 32);
-                const bool ok = kok && grow < p.N;
-                const bf16 *src = ok ? p.w + (int64_t)grow * p.w_stride + kb * kPK + cl * 8 : p.w;
-                cp_async16(base + r * 128 + ((cl ^ (r & 7)) << 4), src, ok);
-            }
+            const int64_t ko = kok ? (int64_t)kb * kPK : 0;
+#pragma unroll
+            for (int i = 0; i < kWRows; ++i)
+                cp_async16(base + wdst[i], kok && wok[i] ? wsrc[i] + ko : p.w, kok && wok[i]);
         };
-        auto load_x = [&](int gi) {
-            uint8_t *base = gen + (gi % p.stages) * group_bytes + jl * p.stage_bytes + kPWTile;
+        auto load_x = [&](int slot, int gi) {
+            uint8_t *base = gen + slot * group_bytes + jl * p.stage_bytes + kPWTile;
             const int kb = kb0 + gi * kPGroupKB + jl;
             const bool kok = kb < kb1 && kb * kPK + cl * 8 < p.K;
-            for (int t = pw; t < p.Mt; t += 4) {
-                const bool ok = kok && t < p.M;
-                const bf16 *src = ok ? p.x + (int64_t)t * p.x_stride + kb * kPK + cl * 8 : p.x;
-                cp_async16(base + t * 128 + ((cl ^ (t & 7)) << 4), src, ok);
+            const int64_t ko = kok ? (int64_t)kb * kPK : 0;
+#pragma unroll
+            for (int i = 0; i < kXRows; ++i) {
+                const int t = pw + kPLoadWarps * i;
+                if (t < p.Mt) {
+                    const bool ok = kok && t < p.M;
+                    cp_async16(base + t * 128 + ((cl ^ (t & 7)) << 4),
+                               ok ? xsrc + i * xstep + ko : p.x, ok);
+                }
             }
         };
         const int pre = min(ngroups, p.stages);
-        for (int gi = 0; gi < pre; ++gi) load_w(gi);
+        for (int gi = 0; gi < pre; ++gi) load_w(gi, gi);
         if (p.pdl_mode) griddep_wait();
         for (int gi = 0; gi < pre; ++gi) {
-            load_x(gi);
+            load_x(gi, gi);
             cp_async_arrive_noinc(&full[gi]);  // lands with this thread's copies so far
         }
+        int slot = 0;
+        uint32_t wrap_phase = 0;  // parity of the slot's previous use
         for (int gi = pre; gi < ngroups; ++gi) {
-            const int s = gi % p.stages;
-            if (!mbar_wait_bounded(&empty[s], ((gi / p.stages) - 1) & 1, &s_abort, p.status)) break;
-            load_w(gi);
-            load_x(gi);
-            cp_async_arrive_noinc(&full[s]);
+            if (!mbar_wait_bounded(&empty[slot], wrap_phase, &s_abort, p.status)) break;
+            load_w(slot, gi);
+            load_x(slot, gi);
+            cp_async_arrive_noinc(&full[slot]);
+            if (++slot == p.stages) {
+                slot = 0;
+                wrap_phase ^= 1u;
+            }
         }
         cp_async_wait_all();  // no copy may land in the ring after this point
 
@@ -343,7 +376,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
         bool have = nkb > 0 && mbar_wait_bounded(&acc_full, 0, &s_abort, p.status);
         have = __all_sync(0xffffffffu, have);
         tc_fence_after();
-        for (int c0 = 0; c0 < p.Mt; c0 += 32) {
+        // warps 2-5 move columns [0, 32), [64, 96), ...; warps 6-9 the others
+        for (int c0 = 32 * (pw >> 2); c0 < p.Mt; c0 += 64) {
             uint32_t r[32];
             if (have) {
                 tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, r);
@@ -361,49 +395,82 @@ __global__ void __launch_bounds__(kPThreads, 1)
     __syncwarp();
     cluster_sync();
 
-    if (warp >= 2 && !s_abort) {
-        // ------------------------- reduction over the cluster + epilogue --
-        if (p.pdl_mode) griddep_wait();  // outputs / pools after the preceding kernel
-        const int et = threadIdx.x - 64;
-        const int npr = kPPairs / p.split;  // row pairs this CTA finishes
+    // ------------------------------------------- reduction over the cluster --
+    // Each epilogue thread takes a contiguous run of (token row, row pair)
+    // items, all of one token row where the run allows, so that the row's
+    // position and block-table entry are read once. First the sums of all its
+    // items over the cluster's partials (rank order: the same sum whatever the
+    // timing), with every distributed-shared-memory load of a batch in flight
+    // at once, into this CTA's own shared memory past the staged tile; then
+    // the CTA tells the cluster it is done reading, and the epilogue runs
+    // while the slower CTAs finish theirs.
+    const bool run = warp >= 2 && !s_abort;
+    const int npr = kPPairs / p.split;  // row pairs this CTA finishes (a power of two)
+    const int lnpr = 5 - (__ffs(p.split) - 1);
+    const int items = p.M * npr;
+    constexpr int kET = 32 * kPLoadWarps;     // epilogue threads
+    const int ipt = (items + kET - 1) / kET;  // items per epilogue thread
+    const int it0 = (threadIdx.x - 64) * ipt;
+    const int it1 = min(items, it0 + ipt);
+    float2 *sums = reinterpret_cast<float2 *>(gen + kPSumsOff);
+    if (run) {
         const int pr0 = rank * npr;
         const int pitch = stage_pitch(p.Mt);
         const uint32_t stg = smem_u32(gen);
         uint32_t peer[kPMaxSplit];
 #pragma unroll
         for (int r = 0; r < kPMaxSplit; ++r) peer[r] = r < p.split ? mapa_shared(stg, r) : 0u;
-        const int items = p.M * npr;
-        for (int item = et; item < items; item += 128) {
-            const int m = item / npr, pl = item - m * npr;  // neighbouring threads: neighbouring pairs
-            const int ra = pr0 + pl, rb = ra + 32;  // tile-local rows of the pair
-            float va[kPMaxSplit], vb[kPMaxSplit];
+        for (int i0 = it0; i0 < it1; i0 += kPBatch) {
+            float va[kPBatch][kPMaxSplit], vb[kPBatch][kPMaxSplit];
 #pragma unroll
-            for (int r = 0; r < kPMaxSplit; ++r) {
-                if (r < p.split) {
-                    va[r] = ld_dsmem_f32(peer[r] + (uint32_t)(ra * pitch + m) * 4u);
-                    vb[r] = ld_dsmem_f32(peer[r] + (uint32_t)(rb * pitch + m) * 4u);
+            for (int u = 0; u < kPBatch; ++u) {
+                const int item = i0 + u;
+                const int m = item >> lnpr, ra = pr0 + (item & (npr - 1)), rb = ra + 32;
+#pragma unroll
+                for (int r = 0; r < kPMaxSplit; ++r) {
+                    if (item < it1 && r < p.split) {
+                        va[u][r] = ld_dsmem_f32(peer[r] + (uint32_t)(ra * pitch + m) * 4u);
+                        vb[u][r] = ld_dsmem_f32(peer[r] + (uint32_t)(rb * pitch + m) * 4u);
+                    }
                 }
             }
-            float a = 0.f, b = 0.f;  // rank order: the same sum whatever the timing
 #pragma unroll
-            for (int r = 0; r < kPMaxSplit; ++r) {
-                if (r < p.split) {
-                    a += va[r];
-                    b += vb[r];
+            for (int u = 0; u < kPBatch; ++u) {
+                float a = 0.f, b = 0.f;
+#pragma unroll
+                for (int r = 0; r < kPMaxSplit; ++r) {
+                    if (r < p.split) {
+                        a += va[u][r];
+                        b += vb[u][r];
+                    }
                 }
+                if (i0 + u < it1) sums[i0 + u] = make_float2(a, b);
             }
+        }
+    }
+    // This CTA no longer reads the others' staged tiles.
+    __syncwarp();
+    cluster_arrive();
+
+    if (run) {
+        // --------------------------------------------------------- epilogue --
+        if (p.pdl_mode) griddep_wait();  // outputs / pools after the preceding kernel
+        const int pr0 = rank * npr;
+        for (int item = it0; item < it1; ++item) {
+            const int m = item >> lnpr, ra = pr0 + (item & (npr - 1));  // tile-local rows ra, ra + 32
+            const float2 ab = sums[item];
             const int col = wr0 + ra, colb = wr1 + ra;  // colb = col + head_dim/2 (QKV)
             if constexpr (EPI == kDecQkv) {
-                dec_store_qkv<HD>(p, m, col, a, b);
+                dec_store_qkv<HD>(p, m, col, ab.x, ab.y);
             } else {
-                dec_store_plain<EPI>(p, m, col, a);
-                dec_store_plain<EPI>(p, m, colb, b);
+                dec_store_plain<EPI>(p, m, col, ab.x);
+                dec_store_plain<EPI>(p, m, colb, ab.y);
             }
         }
     }
     // No CTA leaves while another may still read its staged tile.
     __syncwarp();
-    cluster_sync();
+    cluster_wait();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kPTmemCols);
