@@ -446,7 +446,10 @@ __device__ __forceinline__ void bulk_load(void *smem_dst, const void *src, uint3
 // that gave up on a wait cannot leave the others blocked for good.
 __device__ __forceinline__ bool consumer_sync(uint64_t *bar, uint32_t &phase,
                                               volatile int *abort_flag, int *status) {
-    mbar_arrive(bar);
+    // One arrival per warp: 128 arrivals on one barrier word queue up behind
+    // each other in the shared-memory unit.
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
     const bool ok = mbar_wait_bounded(bar, phase & 1, abort_flag, status);
     ++phase;
     return ok;
@@ -858,7 +861,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], kConsumerWarps);
         }
-        mbar_init(&fin_bar, kConsumerWarps * 32);
+        mbar_init(&fin_bar, kConsumerWarps);
         mbar_init(&epi_full, 2);
         mbar_init(&epi_empty, 1);
         mbar_init(&epi_exit, 1);

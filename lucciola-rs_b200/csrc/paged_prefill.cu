@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
         }
         for (int t = 0; t < kQT; ++t) {
             mbar_init(&s_full[t], 1);
-            mbar_init(&p_full[t], kBM);
+            mbar_init(&p_full[t], kBM / 32);
             mbar_init(&pv_done[t], 1);
         }
         s_abort = 0;
@@ -429,7 +429,8 @@ __global__ void __launch_bounds__(kThreadsPf, 1)
             tmem_st32(tS + 32, *reinterpret_cast<const uint32_t(*)[32]>(&w[32]));
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&p_full[t]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[t]);  // one arrival per warp
         }
         // ----------------------------------------------------- epilogue --
         if (ok && mbar_wait_bounded(&pv_done[t], (my_nkv - 1) & 1, &s_abort, p.status)) {
