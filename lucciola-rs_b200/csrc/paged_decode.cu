@@ -49,6 +49,9 @@ constexpr int kHeadsPerCta = 8;
 constexpr int kPagesPerStage = kConsumerWarps;  // one page per consumer warp per stage
 constexpr int kMaxPeers = LC_PEER_MAX_RANKS - 1;
 constexpr int kMinPagesPerCta = 8;               // auto split: two stages per CTA at least
+// Single-sequence path: the pages of each segment are split over one thread-
+// block cluster, whose rank 0 gathers the pieces in its shared memory.
+constexpr int kClusterMax = 16;
 
 // kFinal marks the last stage of the CTA's whole range.
 enum : int { kFirst = 1, kLast = 2, kDone = 4, kFinal = 8 };
@@ -77,6 +80,11 @@ struct DecodeCfg {
     static constexpr int kQOffset = kStages * kStageBytes;
     static constexpr int kRedOffset = kQOffset + kStages * kQBytes;
     static constexpr int kSmemBytes = kRedOffset + 2 * kRedFloats * 4 + 1024;  // + alignment
+    // Cluster path: one slot per CTA of the cluster in rank 0, [8][HD] fp32
+    // normalised partial then [8] fp32 log2-sum-exp.
+    static constexpr int kClSlotFloats = kHeadsPerCta * HD + kHeadsPerCta;
+    static constexpr int kClOffset = kRedOffset + 2 * kRedFloats * 4;
+    static constexpr int kSmemClusterBytes = kClOffset + kClusterMax * kClSlotFloats * 4 + 1024;
 };
 
 struct DecodeParams {
@@ -455,6 +463,51 @@ __device__ __forceinline__ bool consumer_sync(uint64_t *bar, uint32_t &phase,
     return ok;
 }
 
+// ------------------------------------------------ thread-block cluster path --
+__device__ __forceinline__ uint32_t cl_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cl_size() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of `local` (a shared::cta address) in CTA `rank`.
+__device__ __forceinline__ uint32_t cl_map(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cl_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+__device__ __forceinline__ void st_cl_f32(uint32_t a, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cl_f32x2(uint32_t a, float x, float y) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(x), "f"(y) : "memory");
+}
+// This thread's (and, through the CTA barrier before it, the CTA's) stores to
+// rank 0, then one arrival on rank 0's gather barrier.
+__device__ __forceinline__ void cl_arrive_rank0(uint64_t *bar) {
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                     cl_map(smem_u32(bar), 0))
+                 : "memory");
+}
+// A CTA with no piece (no pages, or a wait that gave up): an empty slot.
+template <int HD>
+__device__ __forceinline__ void cl_put_empty(uint32_t buf_local, uint64_t *bar) {
+    const uint32_t slot =
+        cl_map(buf_local, 0) + cl_rank() * DecodeCfg<HD>::kClSlotFloats * 4 + kHeadsPerCta * HD * 4;
+#pragma unroll
+    for (int h = 0; h < kHeadsPerCta; ++h) st_cl_f32(slot + h * 4, -INFINITY);
+    cl_arrive_rank0(bar);
+}
+
 // Per-warp running softmax state of one chunk: heads 2c, 2c+1 of this lane.
 template <int HD>
 struct WarpState {
@@ -713,10 +766,11 @@ __device__ __forceinline__ bool merge_split_segment(
     return true;
 }
 
-template <int HD, bool FUSED, bool PEER = false>
+template <int HD, bool FUSED, bool PEER = false, bool CLUSTER = false>
 __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const DecodeParams p) {
+    static_assert(!(CLUSTER && PEER), "the cluster path serves one sequence on one GPU");
     using Cfg = DecodeCfg<HD>;
     constexpr int KSTEPS = HD / 16;
 
@@ -738,6 +792,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     // A non-final split chunk whose segment the epilogue warp found this CTA
     // last to finish: merged by the consumer threads after their final chunk.
     __shared__ struct { int valid, b, nh, head0, nch; long long slot0; } s_pend;
+    // Cluster path: rank 0's gather barrier (one arrival per CTA); whether
+    // this CTA has arrived, and whether rank 0 has seen every arrival.
+    __shared__ __align__(8) uint64_t cl_bar;
+    __shared__ int s_cl_arrived, s_cl_gathered;
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x;
@@ -747,6 +805,16 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     // stream be scheduled as our CTAs retire, and wait for the preceding grid
     // before touching its outputs.
     griddep_launch_dependents();
+    if constexpr (CLUSTER) {
+        // Every CTA's gather barrier exists before any CTA arrives on rank 0's.
+        if (tid == 0) {
+            mbar_init(&cl_bar, cl_size());
+            s_cl_arrived = 0;
+            s_cl_gathered = 0;
+            fence_barrier_init();
+        }
+        cl_sync_all();
+    }
     if (p.pdl_mode == 1) griddep_wait();
     const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     uint8_t *smem_gen = smem_raw + (smem_base - smem_u32(smem_raw));
@@ -829,11 +897,25 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         }
     }
     const int cta = blockIdx.x;
-    const long long start = (long long)cta * T / C;
-    const long long end = (long long)(cta + 1) * T / C;
+    long long start, end;
+    if constexpr (CLUSTER) {
+        // One sequence: cluster c takes segment c, its rank r the r-th share of
+        // the segment's P pages (rank 0 always holds page 0, so P < cluster
+        // size leaves only higher ranks without pages).
+        C = gridDim.x;
+        const long long cs = cl_size(), r = cl_rank(), P = pages0;
+        const long long s0 = (long long)(cta / cs) * P;
+        start = s0 + (P >= cs ? r * P / cs : min(r, P));
+        end = s0 + (P >= cs ? (r + 1) * P / cs : min(r + 1, P));
+    } else {
+        start = (long long)cta * T / C;
+        end = (long long)(cta + 1) * T / C;
+    }
     if (cta >= C || start >= end) {  // no pages: no outputs either
         if constexpr (PEER)
             if (tid == 0) peer_arrive(p);
+        if constexpr (CLUSTER)
+            if (tid == 0) cl_put_empty<HD>(smem_u32(smem_gen + Cfg::kClOffset), &cl_bar);
         return;
     }
     // ---- 2. locate the sequence holding `start` -------------------------------
@@ -1275,6 +1357,52 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         bf16 *orow = sm.h < nh ? p.out + (int64_t)m.b * p.out_stride +
                                      (int64_t)(kvh * p.group + hsub * kHeadsPerCta) * HD
                                : nullptr;
+        if constexpr (CLUSTER) {
+            // The piece goes to slot `rank` of rank 0's gather buffer; rank 0
+            // combines the slots in rank order once every CTA has arrived.
+            const uint32_t buf = smem_u32(smem_gen + Cfg::kClOffset);
+            const uint32_t rank = cl_rank();
+            const uint32_t slot = cl_map(buf, 0) + rank * Cfg::kClSlotFloats * 4;
+#pragma unroll
+            for (int k = 0; k < NP; ++k)
+                st_cl_f32x2(slot + (uint32_t)(sm.h * HD + sm.dim(k)) * 4, o[2 * k], o[2 * k + 1]);
+            if (sm.t == 0) st_cl_f32(slot + (uint32_t)(kHeadsPerCta * HD + sm.h) * 4, M + __log2f(Ls));
+            consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+            if (warp == 0 && lane == 0) {
+                cl_arrive_rank0(&cl_bar);
+                s_cl_arrived = 1;
+            }
+            if (rank == 0) {
+                mbar_wait_drain(&cl_bar, 0);  // bounded by time alone
+                const bool all = mbar_try_wait(&cl_bar, 0);
+                if (warp == 0 && lane == 0) s_cl_gathered = all;
+                if (all && orow) {
+                    const float *bl = reinterpret_cast<const float *>(smem_gen + Cfg::kClOffset);
+                    LseAcc<ND> acc;
+                    acc.reset();
+                    const int cs = (int)cl_size();
+                    for (int j = 0; j < cs; ++j) {
+                        const float *sl = bl + j * Cfg::kClSlotFloats;
+                        const float l = sl[kHeadsPerCta * HD + sm.h];
+                        if (l == -INFINITY) continue;  // a CTA without pages
+                        float v[ND];
+#pragma unroll
+                        for (int k = 0; k < NP; ++k) {
+                            const float2 x = *reinterpret_cast<const float2 *>(sl + sm.h * HD + sm.dim(k));
+                            v[2 * k] = x.x;
+                            v[2 * k + 1] = x.y;
+                        }
+                        acc.add(v, l);
+                    }
+                    const float inv = 1.f / acc.s;
+                    float v[ND];
+#pragma unroll
+                    for (int i = 0; i < ND; ++i) v[i] = acc.acc[i] * inv;
+                    put_out_pairs<NP, PEER>(p, orow + sm.h * HD, sm.t, v);
+                }
+            }
+            break;
+        }
         if (m.chunk_p0 == 0 && m.take == m.pages_b) {
             if (orow) put_out_pairs<NP, PEER>(p, orow + sm.h * HD, sm.t, o);
             break;
@@ -1321,6 +1449,15 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         fence_acq_rel_sys();  // this thread's output stores, then one arrival per CTA
         consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
         if (warp == 0 && lane == 0) peer_arrive(p);
+    }
+    if constexpr (CLUSTER) {
+        // Every CTA arrives on rank 0's barrier exactly once (an empty slot if
+        // its piece was not stored), and rank 0 stays until all have: their
+        // stores land in its shared memory.
+        if (warp == 0 && lane == 0) {
+            if (!s_cl_arrived) cl_put_empty<HD>(smem_u32(smem_gen + Cfg::kClOffset), &cl_bar);
+            if (cl_rank() == 0 && !s_cl_gathered) mbar_wait_drain(&cl_bar, 0);
+        }
     }
 }
 
@@ -1407,6 +1544,62 @@ int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const v
     cfg.numAttrs = mode > 0 ? 1 : 0;
     if (cudaLaunchKernelEx(&cfg, paged_decode_kernel<HD, FUSED, PEER>, mk, mv, prm2) !=
         cudaSuccess) {
+        cudaGetLastError();
+        return LC_ERR_CUDA;
+    }
+    return LC_OK;
+}
+
+// Single-sequence fused decode over clusters of `cs` CTAs, one cluster per
+// segment (grid = segments x cs). Returns LC_ERR_NOT_SUPPORTED, launching
+// nothing, when the device cannot run such clusters.
+template <int HD>
+int launch_decode_cluster(const DecodeParams &prm, int segments, int cs, const void *k_pool,
+                          const void *v_pool, cudaStream_t stream) {
+    auto kern = paged_decode_kernel<HD, true, false, true>;
+    const int smem = DecodeCfg<HD>::kSmemClusterBytes;
+    CUtensorMap mk, mv;
+    int rc = pool_tensor_map(k_pool, prm.pool_rows, HD, &mk);
+    if (rc) return rc;
+    rc = pool_tensor_map(v_pool, prm.pool_rows, HD, &mv);
+    if (rc) return rc;
+    static std::mutex mu;
+    static int fits[64][kClusterMax + 1];  // 0 unknown, 1 yes, -1 no; per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LC_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(segments * cs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (fits[dev][cs] == 0) {
+            int n = 0;
+            cfg.numAttrs = 1;
+            const bool ok =
+                ensure_smem_attr((const void *)kern, smem) == LC_OK &&
+                (cs <= 8 || cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                                                 1) == cudaSuccess) &&
+                cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 1;
+            cudaGetLastError();
+            fits[dev][cs] = ok ? 1 : -1;
+        }
+        if (fits[dev][cs] < 0) return LC_ERR_NOT_SUPPORTED;
+    }
+    const int mode = dependent_launch_mode();
+    DecodeParams prm2 = prm;
+    prm2.pdl_mode = mode;
+    cfg.numAttrs = mode > 0 ? 2 : 1;
+    if (cudaLaunchKernelEx(&cfg, kern, mk, mv, prm2) != cudaSuccess) {
         cudaGetLastError();
         return LC_ERR_CUDA;
     }
@@ -1676,6 +1869,18 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
         }
         return head_dim == 64 ? launch_decode<64, true, true>(prm, grid, k_pool, v_pool, s)
                               : launch_decode<128, true, true>(prm, grid, k_pool, v_pool, s);
+    }
+    // One sequence: each segment's pages over a cluster of up to kClusterMax
+    // CTAs (at least 4 pages each), merged in rank 0's shared memory instead
+    // of through the workspace.
+    if (batch == 1 && partition_tokens == 0 && max_context_len > 0) {
+        const int pages = (max_context_len + kBlockSize - 1) / kBlockSize;
+        const int cs = min(kClusterMax, pages / 4);
+        if (cs >= 2) {
+            const int rc = head_dim == 64 ? launch_decode_cluster<64>(prm, G, cs, k_pool, v_pool, s)
+                                          : launch_decode_cluster<128>(prm, G, cs, k_pool, v_pool, s);
+            if (rc != LC_ERR_NOT_SUPPORTED) return rc;
+        }
     }
     return head_dim == 64 ? launch_decode<64, true>(prm, grid, k_pool, v_pool, s)
                           : launch_decode<128, true>(prm, grid, k_pool, v_pool, s);
