@@ -61,6 +61,31 @@ CONFIGS = {
 
 # ------------------------------------------------------------------ helpers --
 
+def host_link_gbs(device, nbytes=16 << 20, reps=5):
+    """This box's pinned host <-> device copy bandwidth (median of `reps`
+    copies of `nbytes` each way, CUDA events), reported beside `e2e`: the
+    end-to-end number moves with it from box to box."""
+    import torch
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    res = {}
+    for name, fn in (("h2d_gbs", lambda: d.copy_(h, non_blocking=True)),
+                     ("d2h_gbs", lambda: h.copy_(d, non_blocking=True))):
+        fn()
+        torch.cuda.synchronize(device)
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        res[name] = round(nbytes / (sorted(ts)[reps // 2] * 1e-3) / 1e9, 2)
+    res["bytes_per_copy"] = nbytes
+    return res
+
+
 def env_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -498,6 +523,7 @@ def run_ours(args, rank, world, local):
 
     if rank == 0:
         peak, peak_kind = measured_peak()
+        link = host_link_gbs(device)  # after the timed regions
         value = kv_bytes_all / (ms_step * 1e-3) / 1e9
         e2e_value = kv_bytes_all / (e2e_ms_step * 1e-3) / 1e9
         # Dominant kernel's average launch duration over the timed region: the
@@ -545,7 +571,7 @@ def run_ours(args, rank, world, local):
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(w.h2d_bytes), "d2h_bytes_per_step": int(w.d2h_bytes),
                     "ms_per_step": round(e2e_ms_step, 5),
-                    "how": e2e_how},
+                    "how": e2e_how, "host_link": link},
             "gpu_launches": runner.launches_per_step * args.steps,
             "clocks": clocks,
         }

@@ -52,6 +52,10 @@ constexpr int kMinPagesPerCta = 8;               // auto split: two stages per C
 // Single-sequence path: the pages of each segment are split over one thread-
 // block cluster, whose rank 0 gathers the pieces in its shared memory.
 constexpr int kClusterMax = 16;
+#ifndef LC_CL_MIN_PAGES
+#define LC_CL_MIN_PAGES 4
+#endif
+constexpr int kClusterMinPages = LC_CL_MIN_PAGES;  // pages per CTA at least
 
 // kFinal marks the last stage of the CTA's whole range.
 enum : int { kFirst = 1, kLast = 2, kDone = 4, kFinal = 8 };
@@ -150,10 +154,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-}
-
 __device__ __forceinline__ void fence_acq_rel_sys() {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
@@ -189,11 +189,6 @@ __device__ __forceinline__ void peer_arrive(const DecodeParams &p) {
                          : "memory");
 }
 
-__device__ __forceinline__ int atom_add_acquire_gpu(int *addr, int v) {
-    int old;
-    asm volatile("atom.acquire.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
-    return old;
-}
 
 __device__ __forceinline__ int seq_tokens(const DecodeParams &p, int b, bool report) {
     int n = __ldg(p.ctx_lens + b) + p.len_offset;
@@ -573,8 +568,6 @@ __device__ __forceinline__ void state_combine(WarpState<HD> &st, const float *re
 constexpr uint64_t kPartTag = 1ull << 32;
 
 __device__ __forceinline__ uint64_t part_word(float v) { return kPartTag | __float_as_uint(v); }
-__device__ __forceinline__ bool part_ok(uint64_t w) { return (w >> 32) == 1u; }
-__device__ __forceinline__ float part_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
 
 // Plain stores: an aligned 8-byte store is written whole; strong (relaxed.gpu)
 // stores cost several times more issue time here for no gain, as the reader
@@ -1875,7 +1868,7 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
     // of through the workspace.
     if (batch == 1 && partition_tokens == 0 && max_context_len > 0) {
         const int pages = (max_context_len + kBlockSize - 1) / kBlockSize;
-        const int cs = min(kClusterMax, pages / 4);
+        const int cs = min(kClusterMax, pages / kClusterMinPages);
         if (cs >= 2) {
             const int rc = head_dim == 64 ? launch_decode_cluster<64>(prm, G, cs, k_pool, v_pool, s)
                                           : launch_decode_cluster<128>(prm, G, cs, k_pool, v_pool, s);

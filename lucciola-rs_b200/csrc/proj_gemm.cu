@@ -34,15 +34,10 @@
 namespace lc {
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStagesG = 4;
+constexpr int kBM = 128, kBN = 256, kBK = 64;
 constexpr int kEpiWarps = 8;    // two per TMEM lane quadrant
 constexpr int kThreadsG = 64 + 32 * kEpiWarps;  // TMA warp, MMA warp, epilogue warps
-constexpr uint32_t kATile = kBM * kBK * 2;  // 16 KiB
-constexpr uint32_t kBTile = kBN * kBK * 2;  // 32 KiB
-constexpr uint32_t kStageBytesG = kATile + kBTile;
-constexpr int kSmemG = kStagesG * kStageBytesG + 1024;  // + 1024-byte alignment slack
-constexpr uint32_t kTmemColsG = 2 * kBN;                 // two accumulators
-constexpr uint32_t kIdescG = idesc_bf16_f32(kBM, kBN, 0);
+constexpr uint32_t kTmemColsG = 2 * kBN;         // two accumulators
 
 enum Epilogue { kPlain = 0, kResidual = 1, kQkvRope = 2 };
 
