@@ -1478,9 +1478,10 @@ def main():
                          "driver (lc_kv_pool) with positions advancing every step")
     ap.add_argument("--partition", type=int, default=None,
                     help="override the split-K partition size in tokens (0 = auto)")
-    ap.add_argument("--gather", choices=["peer", "nccl"], default="nccl",
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="config 5: assemble all heads by peer stores from the decode "
-                         "(lc_rope_append_decode_peer + lc_peer_wait) or by an NCCL "
+                         "(lc_rope_append_decode_peer + lc_peer_wait; the default: level "
+                         "with the all-gather at 2 GPUs, 2 %% ahead at 4) or by an NCCL "
                          "all-gather after it")
     args = ap.parse_args()
     if args.warmup < 3:
