@@ -892,14 +892,17 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     const int cta = blockIdx.x;
     long long start, end;
     if constexpr (CLUSTER) {
-        // One sequence: cluster c takes segment c, its rank r the r-th share of
-        // the segment's P pages (rank 0 always holds page 0, so P < cluster
-        // size leaves only higher ranks without pages).
+        // One sequence: cluster c takes segment c, its ranks one share each of
+        // the segment's P pages. Rank r takes share (r + cs/2) mod cs, so that
+        // the last share (the new token's page, and the extra page of an
+        // uneven split) is not rank 0's, which also gathers. With P below the
+        // cluster size rank r takes page r (rank 0 always holds one).
         C = gridDim.x;
         const long long cs = cl_size(), r = cl_rank(), P = pages0;
         const long long s0 = (long long)(cta / cs) * P;
-        start = s0 + (P >= cs ? r * P / cs : min(r, P));
-        end = s0 + (P >= cs ? (r + 1) * P / cs : min(r + 1, P));
+        const long long c = P >= cs ? (r + cs / 2) % cs : r;
+        start = s0 + (P >= cs ? c * P / cs : min(c, P));
+        end = s0 + (P >= cs ? (c + 1) * P / cs : min(c + 1, P));
     } else {
         start = (long long)cta * T / C;
         end = (long long)(cta + 1) * T / C;
@@ -1370,28 +1373,38 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                 const bool all = mbar_try_wait(&cl_bar, 0);
                 if (warp == 0 && lane == 0) s_cl_gathered = all;
                 if (all && orow) {
+                    // Two passes over the slots, every load of a pass in flight at
+                    // once: the largest log2-sum-exp, then the weighted sum in rank
+                    // order (slots with -inf, CTAs without pages, weigh nothing).
                     const float *bl = reinterpret_cast<const float *>(smem_gen + Cfg::kClOffset);
-                    LseAcc<ND> acc;
-                    acc.reset();
                     const int cs = (int)cl_size();
-                    for (int j = 0; j < cs; ++j) {
-                        const float *sl = bl + j * Cfg::kClSlotFloats;
-                        const float l = sl[kHeadsPerCta * HD + sm.h];
-                        if (l == -INFINITY) continue;  // a CTA without pages
-                        float v[ND];
+                    float lj[kClusterMax];
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < kClusterMax; ++j) {
+                        lj[j] = j < cs ? bl[j * Cfg::kClSlotFloats + kHeadsPerCta * HD + sm.h] : -INFINITY;
+                        mx = fmaxf(mx, lj[j]);
+                    }
+                    float ssum = 0.f, acc[ND];
+#pragma unroll
+                    for (int i = 0; i < ND; ++i) acc[i] = 0.f;
+#pragma unroll
+                    for (int j = 0; j < kClusterMax; ++j) {
+                        if (lj[j] == -INFINITY) continue;
+                        const float w = fast_exp2(lj[j] - mx);
+                        ssum += w;
+                        const float *sl = bl + j * Cfg::kClSlotFloats + sm.h * HD;
 #pragma unroll
                         for (int k = 0; k < NP; ++k) {
-                            const float2 x = *reinterpret_cast<const float2 *>(sl + sm.h * HD + sm.dim(k));
-                            v[2 * k] = x.x;
-                            v[2 * k + 1] = x.y;
+                            const float2 x = *reinterpret_cast<const float2 *>(sl + sm.dim(k));
+                            acc[2 * k] = fmaf(w, x.x, acc[2 * k]);
+                            acc[2 * k + 1] = fmaf(w, x.y, acc[2 * k + 1]);
                         }
-                        acc.add(v, l);
                     }
-                    const float inv = 1.f / acc.s;
-                    float v[ND];
+                    const float inv = 1.f / ssum;
 #pragma unroll
-                    for (int i = 0; i < ND; ++i) v[i] = acc.acc[i] * inv;
-                    put_out_pairs<NP, PEER>(p, orow + sm.h * HD, sm.t, v);
+                    for (int i = 0; i < ND; ++i) acc[i] *= inv;
+                    put_out_pairs<NP, PEER>(p, orow + sm.h * HD, sm.t, acc);
                 }
             }
             break;
