@@ -479,28 +479,18 @@ __device__ __forceinline__ void cl_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                      : "memory");
 }
-__device__ __forceinline__ void st_cl_f32(uint32_t a, float v) {
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_cl_f32x2(uint32_t a, float x, float y) {
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(x), "f"(y) : "memory");
-}
-// This thread's (and, through the CTA barrier before it, the CTA's) stores to
-// rank 0, then one arrival on rank 0's gather barrier.
-__device__ __forceinline__ void cl_arrive_rank0(uint64_t *bar) {
-    asm volatile("fence.acq_rel.cluster;" ::: "memory");
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-                     cl_map(smem_u32(bar), 0))
+// Stores into another CTA's shared memory that count their bytes, on landing,
+// against that CTA's mbarrier (complete_tx): no fence and no separate arrival.
+__device__ __forceinline__ void st_async_f32(uint32_t a, float v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(a),
+                 "f"(v), "r"(bar)
                  : "memory");
 }
-// A CTA with no piece (no pages, or a wait that gave up): an empty slot.
-template <int HD>
-__device__ __forceinline__ void cl_put_empty(uint32_t buf_local, uint64_t *bar) {
-    const uint32_t slot =
-        cl_map(buf_local, 0) + cl_rank() * DecodeCfg<HD>::kClSlotFloats * 4 + kHeadsPerCta * HD * 4;
-#pragma unroll
-    for (int h = 0; h < kHeadsPerCta; ++h) st_cl_f32(slot + h * 4, -INFINITY);
-    cl_arrive_rank0(bar);
+__device__ __forceinline__ void st_async_f32x2(uint32_t a, float x, float y, uint32_t bar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(a),
+        "f"(x), "f"(y), "r"(bar)
+        : "memory");
 }
 
 // Per-warp running softmax state of one chunk: heads 2c, 2c+1 of this lane.
@@ -647,6 +637,27 @@ struct ShareMap {
     __device__ __forceinline__ int dim(int k) const { return 32 * k + 2 * t; }
 };
 
+// Cluster path: consumer thread ct's share of this CTA's piece (its head's dim
+// pairs, and the log2-sum-exp when t == 0) into slot `rank` of rank 0's gather
+// buffer. Every rank's 128 threads each send their share exactly once, so rank
+// 0's barrier completes when kClSlotFloats * 4 bytes per rank have landed.
+template <int HD>
+__device__ __forceinline__ void cl_send(int ct, const float (&o)[HD / 16], float lse,
+                                        uint32_t buf_local, uint64_t *bar) {
+    const ShareMap<HD> sm(ct);
+    const uint32_t rb = cl_map(smem_u32(bar), 0);
+    const uint32_t slot = cl_map(buf_local, 0) + cl_rank() * DecodeCfg<HD>::kClSlotFloats * 4;
+#pragma unroll
+    for (int k = 0; k < ShareMap<HD>::NP; ++k)
+        st_async_f32x2(slot + (uint32_t)(sm.h * HD + sm.dim(k)) * 4, o[2 * k], o[2 * k + 1], rb);
+    if (sm.t == 0) st_async_f32(slot + (uint32_t)(kHeadsPerCta * HD + sm.h) * 4, lse, rb);
+}
+template <int HD>
+__device__ __forceinline__ void cl_send_empty(int ct, uint32_t buf_local, uint64_t *bar) {
+    const float z[HD / 16] = {};
+    cl_send<HD>(ct, z, -INFINITY, buf_local, bar);
+}
+
 // Merge of split segment `seg` by its last piece, run by the 128 consumer
 // threads once the stage ring is idle: pieces j = 0..nch-1 sit in slots
 // slot0 + j; piece `own` (or none, -1) is this CTA's, whose normalised result
@@ -785,10 +796,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     // A non-final split chunk whose segment the epilogue warp found this CTA
     // last to finish: merged by the consumer threads after their final chunk.
     __shared__ struct { int valid, b, nh, head0, nch; long long slot0; } s_pend;
-    // Cluster path: rank 0's gather barrier (one arrival per CTA); whether
-    // this CTA has arrived, and whether rank 0 has seen every arrival.
+    // Cluster path: rank 0's gather barrier (every rank's slot, in bytes), and
+    // whether rank 0 has seen all of them.
     __shared__ __align__(8) uint64_t cl_bar;
-    __shared__ int s_cl_arrived, s_cl_gathered;
+    __shared__ int s_cl_gathered;
     extern __shared__ uint8_t smem_raw[];
 
     const int tid = threadIdx.x;
@@ -801,8 +812,11 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     if constexpr (CLUSTER) {
         // Every CTA's gather barrier exists before any CTA arrives on rank 0's.
         if (tid == 0) {
-            mbar_init(&cl_bar, cl_size());
-            s_cl_arrived = 0;
+            // Rank 0 expects every rank's slot, in bytes (count 1: its own
+            // arrival, which states them).
+            mbar_init(&cl_bar, 1);
+            if (cl_rank() == 0)
+                mbar_arrive_expect_tx(&cl_bar, cl_size() * (uint32_t)(Cfg::kClSlotFloats * 4));
             s_cl_gathered = 0;
             fence_barrier_init();
         }
@@ -911,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         if constexpr (PEER)
             if (tid == 0) peer_arrive(p);
         if constexpr (CLUSTER)
-            if (tid == 0) cl_put_empty<HD>(smem_u32(smem_gen + Cfg::kClOffset), &cl_bar);
+            if (tid < 128) cl_send_empty<HD>(tid, smem_u32(smem_gen + Cfg::kClOffset), &cl_bar);
         return;
     }
     // ---- 2. locate the sequence holding `start` -------------------------------
@@ -1178,6 +1192,7 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
     if (p.pdl_mode == 2) griddep_wait();
     uint32_t qf[KSTEPS][2];
     uint32_t fin_phase = 0, merge_phase = 0;
+    bool cl_sent = false;  // cluster path: this thread's share is on its way to rank 0
     int chunk_idx = 0;  // chunks handed to the epilogue so far
     int nk_it = -1, nk_warp = -1;  // fused: stage and warp of the new token's page
     WarpState<HD> st;
@@ -1356,18 +1371,10 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         if constexpr (CLUSTER) {
             // The piece goes to slot `rank` of rank 0's gather buffer; rank 0
             // combines the slots in rank order once every CTA has arrived.
-            const uint32_t buf = smem_u32(smem_gen + Cfg::kClOffset);
             const uint32_t rank = cl_rank();
-            const uint32_t slot = cl_map(buf, 0) + rank * Cfg::kClSlotFloats * 4;
-#pragma unroll
-            for (int k = 0; k < NP; ++k)
-                st_cl_f32x2(slot + (uint32_t)(sm.h * HD + sm.dim(k)) * 4, o[2 * k], o[2 * k + 1]);
-            if (sm.t == 0) st_cl_f32(slot + (uint32_t)(kHeadsPerCta * HD + sm.h) * 4, M + __log2f(Ls));
-            consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
-            if (warp == 0 && lane == 0) {
-                cl_arrive_rank0(&cl_bar);
-                s_cl_arrived = 1;
-            }
+            cl_send<HD>(warp * 32 + lane, o, M + __log2f(Ls), smem_u32(smem_gen + Cfg::kClOffset),
+                        &cl_bar);
+            cl_sent = true;
             if (rank == 0) {
                 mbar_wait_drain(&cl_bar, 0);  // bounded by time alone
                 const bool all = mbar_try_wait(&cl_bar, 0);
@@ -1457,13 +1464,11 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         if (warp == 0 && lane == 0) peer_arrive(p);
     }
     if constexpr (CLUSTER) {
-        // Every CTA arrives on rank 0's barrier exactly once (an empty slot if
-        // its piece was not stored), and rank 0 stays until all have: their
-        // stores land in its shared memory.
-        if (warp == 0 && lane == 0) {
-            if (!s_cl_arrived) cl_put_empty<HD>(smem_u32(smem_gen + Cfg::kClOffset), &cl_bar);
-            if (cl_rank() == 0 && !s_cl_gathered) mbar_wait_drain(&cl_bar, 0);
-        }
+        // Every consumer thread sends its share of the slot exactly once (an
+        // empty share if its piece was not sent), and rank 0 stays until all
+        // bytes have landed: they land in its shared memory.
+        if (!cl_sent) cl_send_empty<HD>(warp * 32 + lane, smem_u32(smem_gen + Cfg::kClOffset), &cl_bar);
+        if (warp == 0 && lane == 0 && cl_rank() == 0 && !s_cl_gathered) mbar_wait_drain(&cl_bar, 0);
     }
 }
 
