@@ -88,7 +88,8 @@ struct DecodeCfg {
     // normalised partial then [8] fp32 log2-sum-exp.
     static constexpr int kClSlotFloats = kHeadsPerCta * HD + kHeadsPerCta;
     static constexpr int kClOffset = kRedOffset + 2 * kRedFloats * 4;
-    static constexpr int kSmemClusterBytes = kClOffset + kClusterMax * kClSlotFloats * 4 + 1024;
+    static constexpr int kRed4Offset = kClOffset + kClusterMax * kClSlotFloats * 4;
+    static constexpr int kSmemClusterBytes = kRed4Offset + 2 * kRedFloats * 4 + 1024;
 };
 
 struct DecodeParams {
@@ -1071,6 +1072,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
 
     float *red = reinterpret_cast<float *>(smem_gen + Cfg::kRedOffset);
     constexpr int kRedFloats = Cfg::kRedFloats;
+    // Cluster path: two more warp-state slots past rank 0's gather buffer.
+    float *red4 = reinterpret_cast<float *>(smem_gen + Cfg::kRed4Offset);
 
     if (warp == kEpilogueWarp) {
         // ------------------------------------------------------ epilogue --
@@ -1317,10 +1320,24 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         // CTA's final one is then handed to the epilogue warp; for the final
         // one the epilogue is only told to finish.
         const bool final_chunk = (m.flags & kFinal) != 0;
+        // Cluster path: a CTA holds one chunk, its final one. The four warp
+        // states go to four slots at once (no halving round), and the
+        // epilogue warp is only told to finish.
+        const bool four = CLUSTER && final_chunk;
         if (chunk_idx > 0) mbar_wait_bounded(&epi_empty, (chunk_idx - 1) & 1, &s_abort, p.status);
-        if (warp >= 2) state_store<HD>(red + (warp - 2) * kRedFloats, st, lane);
-        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
-        if (warp < 2) {
+        if (four) {
+            state_store<HD>(warp < 2 ? red + warp * kRedFloats
+                                     : red4 + (warp - 2) * kRedFloats, st, lane);
+            if (warp < 2) {  // epi_full counts warps 0 and 1
+                if (warp == 0 && lane == 0) epi.done = 1;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&epi_full);
+            }
+        } else if (warp >= 2) {
+            state_store<HD>(red + (warp - 2) * kRedFloats, st, lane);
+        }
+        if (!four) consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);
+        if (!four && warp < 2) {
             state_combine<HD>(st, red + warp * kRedFloats, lane);
             __syncwarp();
             state_store<HD>(red + warp * kRedFloats, st, lane);
@@ -1345,25 +1362,45 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
         // Thread ct owns head ct >> 4 and dim pairs 32k + 2 (ct & 15) of the
         // CTA's state for this chunk: whole segment -> output; split segment ->
         // partial + arrival, and the merge if this CTA came last.
-        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);  // both slots stored
+        consumer_sync(&fin_bar, fin_phase, &s_abort, p.status);  // both (four) slots stored
         constexpr int NP = ShareMap<HD>::NP, ND = ShareMap<HD>::ND;
         const ShareMap<HD> sm(warp * 32 + lane);
-        const float *r0 = red, *r1 = red + kRedFloats;
-        const float m0 = r0[kHeadsPerCta * HD + sm.h], m1 = r1[kHeadsPerCta * HD + sm.h];
-        const float l0 = r0[kHeadsPerCta * HD + kHeadsPerCta + sm.h];
-        const float l1 = r1[kHeadsPerCta * HD + kHeadsPerCta + sm.h];
-        const float M = fmaxf(m0, m1);
+        // Slots in order: red[0], red[1] (and red4[0], red4[1] in the cluster path).
+        constexpr int NS = CLUSTER ? 4 : 2;
+        const float *rs[NS];
+        rs[0] = red;
+        rs[1] = red + kRedFloats;
+        if constexpr (CLUSTER) {
+            rs[2] = red4;
+            rs[3] = red4 + kRedFloats;
+        }
+        float mj[NS], ej[NS];
+        float M = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < NS; ++j) {
+            mj[j] = rs[j][kHeadsPerCta * HD + sm.h];
+            M = fmaxf(M, mj[j]);
+        }
         const float u = M == -INFINITY ? 0.f : M;
-        const float e0 = fast_exp2(m0 - u), e1 = fast_exp2(m1 - u);
-        const float Ls = l0 * e0 + l1 * e1;
+        float Ls = 0.f;
+#pragma unroll
+        for (int j = 0; j < NS; ++j) {
+            ej[j] = fast_exp2(mj[j] - u);
+            Ls += rs[j][kHeadsPerCta * HD + kHeadsPerCta + sm.h] * ej[j];
+        }
         const float il = 1.f / Ls;
         float o[ND];
 #pragma unroll
         for (int k = 0; k < NP; ++k) {
-            const float2 a = *reinterpret_cast<const float2 *>(r0 + sm.h * HD + sm.dim(k));
-            const float2 b = *reinterpret_cast<const float2 *>(r1 + sm.h * HD + sm.dim(k));
-            o[2 * k] = (a.x * e0 + b.x * e1) * il;
-            o[2 * k + 1] = (a.y * e0 + b.y * e1) * il;
+            float x = 0.f, y = 0.f;
+#pragma unroll
+            for (int j = 0; j < NS; ++j) {
+                const float2 a = *reinterpret_cast<const float2 *>(rs[j] + sm.h * HD + sm.dim(k));
+                x += a.x * ej[j];
+                y += a.y * ej[j];
+            }
+            o[2 * k] = x * il;
+            o[2 * k + 1] = y * il;
         }
         bf16 *orow = sm.h < nh ? p.out + (int64_t)m.b * p.out_stride +
                                      (int64_t)(kvh * p.group + hsub * kHeadsPerCta) * HD
