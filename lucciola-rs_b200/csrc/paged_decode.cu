@@ -24,9 +24,13 @@
 //    P^T moves from the accumulator layout to the B-operand layout with
 //    movmatrix.trans. Online softmax in base 2.
 //  * A chunk that covers a whole segment writes the bf16 output directly. A
-//    segment split across CTAs writes (O/l, log2-sum-exp) partials; the last
-//    CTA to finish it (arrival counter) merges them with a warp-shuffle
-//    log-sum-exp reduction.
+//    segment split across CTAs writes (O/l, log2-sum-exp) partials as tagged
+//    words; the last CTA to finish it (arrival counter) merges them in slot
+//    order from its stage ring.
+//  * One sequence (the fused entry with batch 1): each segment's pages go to
+//    one thread-block cluster instead, and the pieces are sent into rank 0's
+//    shared memory with st.async, their bytes counted on rank 0's mbarrier;
+//    rank 0 combines them in rank order (no workspace, no counter).
 //
 // Semantics follow attention.cu: out = softmax(q.k * scale) . v over cache
 // tokens 0..n-1, fp32 accumulation, bf16 output. Block-table entries outside
@@ -1407,7 +1411,8 @@ __global__ void __launch_bounds__(kThreads, HD == 64 ? 3 : 2)
                                : nullptr;
         if constexpr (CLUSTER) {
             // The piece goes to slot `rank` of rank 0's gather buffer; rank 0
-            // combines the slots in rank order once every CTA has arrived.
+            // combines the slots in rank order once every rank's bytes have
+            // landed.
             const uint32_t rank = cl_rank();
             cl_send<HD>(warp * 32 + lane, o, M + __log2f(Ls), smem_u32(smem_gen + Cfg::kClOffset),
                         &cl_bar);
