@@ -193,7 +193,13 @@ int lc_paged_decode(void *out, int64_t out_stride, const void *q,
  * back, a side effect nothing after the attention reads (o_proj consumes the
  * attention output, src/models.rs:553-566). Pool writes are bit-identical to
  * lc_rope_append; the output is that of lc_paged_decode. Workspace as for
- * lc_paged_decode (lc_paged_decode_workspace_size). */
+ * lc_paged_decode (lc_paged_decode_workspace_size).
+ * With batch 1, partition_tokens 0 and max_context_len of at least 32 tokens
+ * (one sequence, as Qwen2Model::generate decodes, src/models.rs:230-245),
+ * each kv head's pages are split over one thread-block cluster of up to 16
+ * CTAs whose pieces are combined in shared memory; max_context_len then sizes
+ * the clusters, so it should be the real length or close above it. The
+ * workspace is passed as always and left as found. */
 int lc_rope_append_decode(void *out, int64_t out_stride, const void *qkv,
                           int64_t row_stride, const int *positions,
                           const void *q_bias, const void *k_bias,
