@@ -172,7 +172,9 @@ int lc_paged_decode_workspace_init(void *workspace, size_t workspace_bytes,
  * log-sum-exp reduction. partition_tokens > 0 caps the split at about that
  * many tokens per CTA (0 = fill the GPU). max_context_len is an optional host
  * hint (0 = none) that trims the grid for small batches; lengths are read on
- * the device. */
+ * the device. With batch 1, partition_tokens 0 and a hint of at least 32
+ * tokens the call runs the single-sequence form described at
+ * lc_rope_append_decode (thread-block clusters). */
 int lc_paged_decode(void *out, int64_t out_stride, const void *q,
                     int64_t q_stride, const void *k_pool, const void *v_pool,
                     int64_t num_blocks, int num_layers, int layer,

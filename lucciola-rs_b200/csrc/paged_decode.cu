@@ -1603,13 +1603,13 @@ int launch_decode(const DecodeParams &prm, int grid, const void *k_pool, const v
     return LC_OK;
 }
 
-// Single-sequence fused decode over clusters of `cs` CTAs, one cluster per
-// segment (grid = segments x cs). Returns LC_ERR_NOT_SUPPORTED, launching
-// nothing, when the device cannot run such clusters.
-template <int HD>
+// Single-sequence decode (fused or not) over clusters of `cs` CTAs, one
+// cluster per segment (grid = segments x cs). Returns LC_ERR_NOT_SUPPORTED,
+// launching nothing, when the device cannot run such clusters.
+template <int HD, bool FUSED>
 int launch_decode_cluster(const DecodeParams &prm, int segments, int cs, const void *k_pool,
                           const void *v_pool, cudaStream_t stream) {
-    auto kern = paged_decode_kernel<HD, true, false, true>;
+    auto kern = paged_decode_kernel<HD, FUSED, false, true>;
     const int smem = DecodeCfg<HD>::kSmemClusterBytes;
     CUtensorMap mk, mv;
     int rc = pool_tensor_map(k_pool, prm.pool_rows, HD, &mk);
@@ -1750,6 +1750,19 @@ extern "C" int lc_paged_decode(void *out, int64_t out_stride, const void *q, int
     prm.status = dev_status;
     prm.out_vec = ((uintptr_t)out & 3) == 0 && out_stride % 2 == 0;
     cudaStream_t s = as_stream(stream);
+    // One sequence (lc_flash_decoding, the reference-shaped entry, always):
+    // each segment's pages over one thread-block cluster, as in
+    // lc_rope_append_decode.
+    if (batch == 1 && partition_tokens == 0 && max_context_len > 0) {
+        const int pages = (max_context_len + kBlockSize - 1) / kBlockSize;
+        const int cs = min(kClusterMax, pages / kClusterMinPages);
+        if (cs >= 2) {
+            const int rc = head_dim == 64
+                               ? launch_decode_cluster<64, false>(prm, G, cs, k_pool, v_pool, s)
+                               : launch_decode_cluster<128, false>(prm, G, cs, k_pool, v_pool, s);
+            if (rc != LC_ERR_NOT_SUPPORTED) return rc;
+        }
+    }
     return head_dim == 64 ? launch_decode<64>(prm, grid, k_pool, v_pool, s)
                           : launch_decode<128>(prm, grid, k_pool, v_pool, s);
 }
@@ -1930,8 +1943,9 @@ static int rope_append_decode_impl(void *out, int64_t out_stride, const void *qk
         const int pages = (max_context_len + kBlockSize - 1) / kBlockSize;
         const int cs = min(kClusterMax, pages / kClusterMinPages);
         if (cs >= 2) {
-            const int rc = head_dim == 64 ? launch_decode_cluster<64>(prm, G, cs, k_pool, v_pool, s)
-                                          : launch_decode_cluster<128>(prm, G, cs, k_pool, v_pool, s);
+            const int rc = head_dim == 64
+                               ? launch_decode_cluster<64, true>(prm, G, cs, k_pool, v_pool, s)
+                               : launch_decode_cluster<128, true>(prm, G, cs, k_pool, v_pool, s);
             if (rc != LC_ERR_NOT_SUPPORTED) return rc;
         }
     }

@@ -1,4 +1,4 @@
-"""Single-sequence fused decode (lc_rope_append_decode with batch 1), which
+"""Single-sequence decode (lc_rope_append_decode and lc_paged_decode with batch 1), which
 splits each segment's pages over a thread-block cluster and merges the pieces
 in rank 0's shared memory: pool writes bit-identical to lc_rope_append, the
 qkv rows untouched, outputs against the CPU oracle and against the batched
@@ -77,3 +77,35 @@ def test_single_sequence_cluster_decode(hq, hkv, hd, ctx, hint):
     assert float(np.abs(got - ref).max()) <= ATTN_ATOL
     two = O.bf16_to_f32(from_device(out_a))
     assert float(np.abs(got - two).max()) <= ATTN_ATOL
+
+
+@pytest.mark.parametrize("hq,hkv,hd", [(14, 2, 64), (28, 4, 128), (32, 2, 64)])
+@pytest.mark.parametrize("ctx,hint,len_offset", [(1024, 1024, 0), (1025, 1025, 1), (300, 4096, 0),
+                                                 (9000, 9000, 1)])
+def test_single_sequence_cluster_plain_decode(hq, hkv, hd, ctx, hint, len_offset):
+    """lc_paged_decode with batch 1 (what lc_flash_decoding, the reference-shaped
+    entry, always runs) takes the same cluster path: outputs against the CPU
+    oracle, the same bits on every launch, the workspace left as found."""
+    case = make_case(1, hq, hkv, hd, [ctx], seed=ctx + hd)
+    q, k, v = to_device(case.q), to_device(case.k_pool), to_device(case.v_pool)
+    tables = to_device(case.tables)
+    lens = to_device(np.asarray([ctx - len_offset], np.int32))
+    ws = L.alloc_decode_workspace(1, hq, hkv, hd)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    outs = []
+    for _ in range(3):
+        out = torch.full((1, hq * hd), float("nan"), dtype=torch.bfloat16, device="cuda")
+        L.paged_decode(out, q, k, v, case.num_blocks, case.num_layers, case.layer, hq, hkv, hd,
+                       tables, lens, hint, len_offset=len_offset, workspace=ws, dev_status=st)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert not ws.any()
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16))
+    ref = O.bf16_to_f32(O.paged_decode(case.q, case.k_pool, case.v_pool, case.layer, hq, hkv, hd,
+                                       case.tables, np.asarray([ctx - len_offset], np.int32),
+                                       case.num_layers, len_offset=len_offset, threads=8))
+    got = O.bf16_to_f32(from_device(outs[0]))
+    assert np.isfinite(got).all()
+    assert float(np.abs(got - ref).max()) <= ATTN_ATOL
